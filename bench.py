@@ -1,0 +1,559 @@
+#!/usr/bin/env python
+"""Benchmark of the batched dequant-fused Q4 GEMM (BASELINE metric: "Q4_K GEMM
+tokens/s & HBM GB/s (% of ~8 TB/s) at M=1/8/32, K=N=5120").
+
+Headline workload (N=1): Q4_K, M=32, K=N=5120. A *step* is one pass over R
+distinct weight matrices (R rotating copies, together larger than 2x the L2
+cache, so every GEMM streams its weights from HBM): R GEMM launches on the
+same fp16 activations. ``value`` = tokens/s = M * R * steps / elapsed, i.e.
+M / (average GEMM time) -- the reference's own definition (t/s = B / step
+time, kernels/busfill_v1a.cu:172). Inputs are synthetic (seeded torch RNG, the
+BASELINE config distributions), generated on the device.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl busfill|reference]
+
+N > 1 (launched by torchrun): every weight matrix is split by output columns
+across the ranks (rank r owns rows [r*N/g, (r+1)*N/g)); each GEMM is followed
+by an NCCL all-gather of the [M, N/g] output slices and the re-interleave to
+[M, N] (strong scaling: total work fixed). Timing is the max over ranks.
+
+--impl reference: the CPU dequantize-then-fp32-matmul path (the reference's
+own correctness path, kernels/q4k_batched.py:75,100, restated by the oracle)
+on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["busfill", "reference"], default="busfill")
+    ap.add_argument("--fmt", choices=["q4k", "q4_0"], default="q4k")
+    ap.add_argument("--m", type=int, default=32)
+    ap.add_argument("--n", type=int, default=5120)
+    ap.add_argument("--k", type=int, default=5120)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-extras", action="store_true", help="skip sweep / cuBLAS / e2e / CPU legs")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def alg_bytes(m, n, k):
+    return n * k * 18 // 32 + 2 * m * k + 2 * m * n
+
+
+def profiled_traffic(workload):
+    """dram bytes per launch from a committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", f"{workload}.md")
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip().split()[0])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons with NVML while the timed region runs."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+        0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                bits = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for b, name in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.nv is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread:
+            self._thread.join()
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples),
+                "reasons": sorted(self.reasons - {"gpu_idle"})}
+
+
+# ---------------------------------------------------------------------------
+# synthetic inputs on the device (BASELINE config distributions)
+# ---------------------------------------------------------------------------
+def make_q4k_weights(torch, n, k, gen, dev):
+    s = k // 256
+    blocks = torch.randint(0, 256, (n, s, 144), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, s), device=dev, generator=gen) * 0.009 + 0.001).half()
+    dmin = (torch.rand((n, s), device=dev, generator=gen) * 0.005).half()
+    blocks[:, :, 0:2] = d.view(torch.uint8).view(n, s, 2)
+    blocks[:, :, 2:4] = dmin.view(torch.uint8).view(n, s, 2)
+    return blocks.view(n, s * 144).contiguous()
+
+
+def make_q4_0_weights(torch, n, k, gen, dev):
+    wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=gen)
+    ws = (torch.rand((n, k // 32), device=dev, generator=gen) * 0.019 + 0.001).half()
+    return wq, ws
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_busfill(args):
+    import torch
+    import torch.distributed as dist
+
+    import busfill_b200 as bf
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    bf.load_library()
+    props = torch.cuda.get_device_properties(dev)
+    l2 = getattr(props, "L2_cache_size", 126 * 1024 * 1024) or 126 * 1024 * 1024
+    hbm_peak, tc_peak, peak_src = measured_peaks()
+
+    M, N, K = args.m, args.n, args.k
+    if N % (world * 128) and world > 1:
+        raise SystemExit(f"N={N} must split into multiples of 128 rows over {world} ranks")
+    n_loc = N // world
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + rank)
+    wbytes = n_loc * K * 18 // 32
+    R = max(2, math.ceil(2.2 * l2 / wbytes))
+    if args.fmt == "q4k":
+        base = make_q4k_weights(torch, n_loc, K, gen, dev)
+        weights = [base] + [base.clone() for _ in range(R - 1)]
+    else:
+        wq, ws = make_q4_0_weights(torch, n_loc, K, gen, dev)
+        weights = [(wq, ws)] + [(wq.clone(), ws.clone()) for _ in range(R - 1)]
+    a = torch.randn((M, K), device=dev, generator=gen).half()
+    c_loc = torch.empty((M, n_loc), dtype=torch.float16, device=dev)
+    gathered = torch.empty((world, M, n_loc), dtype=torch.float16, device=dev) if world > 1 else None
+    c_full = torch.empty((M, N), dtype=torch.float16, device=dev) if world > 1 else None
+
+    def gemm(w, stream):
+        if args.fmt == "q4k":
+            bf.gemm_q4k(w, a, out=c_loc, stream=stream)
+        else:
+            bf.gemm_q4_0(w[0], w[1], a, out=c_loc, stream=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered.view(world * M, n_loc), c_loc)
+            c_full.view(M, world, n_loc).copy_(gathered.permute(1, 0, 2))
+
+    def one_step(stream):
+        for w in weights:
+            gemm(w, stream)
+
+    stream = torch.cuda.Stream(device=dev)
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):      # W untimed warm-up steps (also sizes the workspace)
+            one_step(stream)
+    stream.synchronize()
+    if bf.stream_status(stream) != 0:
+        raise SystemExit("device-side error during warm-up")
+
+    def capture(nsteps, fn=one_step):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for _ in range(nsteps):
+                fn(stream)
+        return g
+
+    def time_graph(g, sampler=None):
+        g.replay()                                 # upload / first-replay cost, untimed
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        ctx = sampler if sampler is not None else _Null()
+        with ctx:
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            e1.synchronize()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            dist.barrier()
+        return ms
+
+    steps = args.steps
+    g_main = capture(steps)
+    sampler = ClockSampler(local)
+    ms = time_graph(g_main, sampler)
+    del g_main
+    if bf.stream_status(stream) != 0:
+        raise SystemExit("device-side error in the timed region")
+    launches = steps * R
+    us_per_gemm = ms * 1e3 / launches
+    tok_s = M * launches / (ms / 1e3)
+    b_launch = alg_bytes(M, n_loc, K)
+    achieved = b_launch / (us_per_gemm * 1e-6) / 1e9
+    workload = f"{args.fmt}_gemm_m{M}_k{K}_n{N}"
+    out = {
+        "metric": "Q4_K GEMM tokens/s (M / avg GEMM time) at K=N=5120" if args.fmt == "q4k"
+        else "Q4_0 GEMM tokens/s (M / avg GEMM time)",
+        "value": round(tok_s, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": max(args.warmup, 3),
+        "ms_per_step": round(ms / steps, 6),
+        "us_per_gemm": round(us_per_gemm, 4),
+        "higher_is_better": True,
+        "scaling": "strong" if world > 1 else "weak",
+        "vs_baseline": None,
+        "dtype": "fp16 (fp32 accumulate)",
+        "data": "synthetic (seeded torch RNG, BASELINE config distributions)",
+        "config": {
+            "workload": workload, "format": args.fmt, "M": M, "N": N, "K": K,
+            "parallelism": f"tp{world} (N-split + NCCL all-gather)" if world > 1 else "single GPU",
+            "weight_copies": R, "weight_set_bytes": R * wbytes,
+            "l2": f"inputs larger than L2: {R} rotating weight copies, {R * wbytes / 1e6:.0f} MB > 2x L2 "
+                  f"({l2 / 1e6:.0f} MB)",
+            "timing": "CUDA graph of steps*R back-to-back GEMM launches (PDL on), CUDA events on the "
+                      "launching stream, max over ranks",
+        },
+        "gpu_launches": launches,
+        "roofline": {
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
+            "alg_bytes_per_launch": b_launch, "traffic": profiled_traffic(workload),
+        },
+        "clocks": sampler.summary(),
+    }
+
+    if world == 1 and not args.no_extras:
+        out["isolated_no_pdl"] = isolated_no_pdl(bf, capture, time_graph, min(steps, 50), R, M)
+        out["sweep"] = sweep(torch, bf, dev, l2, hbm_peak, args)
+        out["cublas_fp16"] = cublas_comparator(torch, bf, dev, l2, weights, a, args)
+        out["e2e"] = e2e(torch, bf, dev, weights, a, args, max(10, steps // 10))
+        out["cpu_baseline"] = cpu_baseline(args)
+    elif world > 1:
+        out["e2e"] = None
+
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+class _Null:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *e):
+        return False
+
+
+def isolated_no_pdl(bf, capture, time_graph, steps, R, M):
+    bf.set_pdl(False)
+    try:
+        g = capture(steps)
+        ms = time_graph(g)
+        del g
+    finally:
+        bf.set_pdl(True)
+    us = ms * 1e3 / (steps * R)
+    return {"us_per_gemm": round(us, 4), "tokens_per_s": round(M / (us * 1e-6), 1),
+            "note": "same graph with programmatic dependent launch disabled"}
+
+
+def sweep(torch, bf, dev, l2, hbm_peak, args):
+    rows = []
+    cases = [("q4k", 1, 5120, 5120), ("q4k", 8, 5120, 5120), ("q4k", 32, 5120, 5120), ("q4k", 32, 17408, 5120),
+             ("q4_0", 1, 5120, 5120), ("q4_0", 8, 5120, 5120), ("q4_0", 32, 5120, 5120)]
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 99)
+    for fmt, m, n, k in cases:
+        wbytes = n * k * 18 // 32
+        R = max(2, math.ceil(2.2 * l2 / wbytes))
+        if fmt == "q4k":
+            w0 = make_q4k_weights(torch, n, k, gen, dev)
+            ws = [w0] + [w0.clone() for _ in range(R - 1)]
+        else:
+            q, s = make_q4_0_weights(torch, n, k, gen, dev)
+            ws = [(q, s)] + [(q.clone(), s.clone()) for _ in range(R - 1)]
+        a = torch.randn((m, k), device=dev, generator=gen).half()
+        c = torch.empty((m, n), dtype=torch.float16, device=dev)
+        st = torch.cuda.Stream(device=dev)
+
+        def step():
+            for w in ws:
+                if fmt == "q4k":
+                    bf.gemm_q4k(w, a, out=c, stream=st)
+                else:
+                    bf.gemm_q4_0(w[0], w[1], a, out=c, stream=st)
+
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                step()
+        st.synchronize()
+        nsteps = max(4, min(40, 4000 // R))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(nsteps):
+                step()
+        g.replay()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        assert bf.stream_status(st) == 0
+        us = ms * 1e3 / (nsteps * R)
+        gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
+        rows.append({"format": fmt, "M": m, "N": n, "K": k, "us_per_gemm": round(us, 3),
+                     "tokens_per_s": round(m / (us * 1e-6), 1), "GB_s": round(gbs, 1),
+                     "hbm_frac": round(gbs / hbm_peak, 4)})
+        del g, ws
+        torch.cuda.empty_cache()
+    return rows
+
+
+def cublas_comparator(torch, bf, dev, l2, weights, a, args):
+    """torch.matmul (cuBLAS) on the same weights dequantized to fp16
+    (kernels/q4k_batched.py:111-113, bench/baseline_torch.py:19-25)."""
+    n, k = (weights[0].shape[0] if args.fmt == "q4k" else weights[0][0].shape[0]), args.k
+    if args.fmt == "q4k":
+        w16 = bf.dequant_q4k(weights[0], k)
+    else:
+        w16 = bf.dequant_q4_0(weights[0][0], weights[0][1])
+    R = max(2, math.ceil(2.2 * l2 / (n * k * 2)))
+    ws = [w16] + [w16.clone() for _ in range(R - 1)]
+    st = torch.cuda.Stream(device=dev)
+    c = torch.empty((a.shape[0], n), dtype=torch.float16, device=dev)
+
+    def step():
+        for w in ws:
+            torch.matmul(a, w.t(), out=c)
+
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            step()
+    st.synchronize()
+    nsteps = max(4, min(50, 1000 // R))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for _ in range(nsteps):
+            step()
+    g.replay()
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    g.replay()
+    e1.record(st)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (nsteps * R)
+    del g, ws
+    torch.cuda.empty_cache()
+    m = a.shape[0]
+    return {"us_per_gemm": round(us, 4), "tokens_per_s": round(m / (us * 1e-6), 1),
+            "fp16_weight_bytes": n * k * 2, "copies": R}
+
+
+def e2e(torch, bf, dev, weights, a, args, steps):
+    """The same metric through the public API with HOST buffers: every call
+    copies its activations from pinned host memory, runs the C-ABI GEMM
+    (ctypes, no graph) and reads the output back to pinned host memory."""
+    m, k = a.shape
+    n = weights[0].shape[0] if args.fmt == "q4k" else weights[0][0].shape[0]
+    h_a = torch.empty((m, k), dtype=torch.float16).pin_memory()
+    h_a.copy_(a.cpu())
+    h_c = torch.empty((m, n), dtype=torch.float16).pin_memory()
+    d_a = torch.empty_like(a)
+    d_c = torch.empty((m, n), dtype=torch.float16, device=dev)
+    st = torch.cuda.Stream(device=dev)
+
+    def step():
+        for w in weights:
+            d_a.copy_(h_a, non_blocking=True)
+            if args.fmt == "q4k":
+                bf.gemm_q4k(w, d_a, out=d_c, stream=st)
+            else:
+                bf.gemm_q4_0(w[0], w[1], d_a, out=d_c, stream=st)
+            h_c.copy_(d_c, non_blocking=True)
+
+    with torch.cuda.stream(st):
+        for _ in range(2):
+            step()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            step()
+        e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    assert bf.stream_status(st) == 0
+    calls = steps * len(weights)
+    return {"value": round(m * calls / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": len(weights) * m * k * 2, "d2h_bytes_per_step": len(weights) * m * n * 2,
+            "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps,
+            "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* (C ABI via ctypes) -> pinned host C"}
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (the only places bench.py runs the oracle)
+# ---------------------------------------------------------------------------
+def _cpu_dequant_gemm(orc, fmt, w, a, k, pool, nchunks):
+    import numpy as np
+    import torch
+    n = w.shape[0] if fmt == "q4k" else w[0].shape[0]
+    bounds = [(i * n // nchunks, (i + 1) * n // nchunks) for i in range(nchunks)]
+    t0 = time.perf_counter()
+    if fmt == "q4k":
+        parts = list(pool.map(lambda b: orc.dequant_q4k_f32(w[b[0]:b[1]], k), bounds))
+    else:
+        parts = list(pool.map(lambda b: orc.dequant_q4_0_planes_f32(w[0][b[0]:b[1]], w[1][b[0]:b[1]]), bounds))
+    wf = np.concatenate(parts)
+    t1 = time.perf_counter()
+    c = torch.from_numpy(a).float() @ torch.from_numpy(wf).T          # kernels/q4k_batched.py:100
+    t2 = time.perf_counter()
+    return t1 - t0, t2 - t1, c
+
+
+def cpu_baseline(args, reps=5):
+    from concurrent.futures import ThreadPoolExecutor
+
+    import torch
+
+    from oracle import q4_oracle as orc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    m, n, k = args.m, args.n, args.k
+    w = orc.gen_q4k(n, k, seed=args.seed) if args.fmt == "q4k" else orc.gen_q4_0(n, k, seed=args.seed)
+    a = orc.gen_activations(m, k, seed=args.seed + 1)
+    with ThreadPoolExecutor(cores) as pool:
+        _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
+        ts = [_cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores) for _ in range(reps)]
+    deq = statistics.median(t[0] for t in ts)
+    mm = statistics.median(t[1] for t in ts)
+    return {"value": round(m / (deq + mm), 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{reps} full GEMMs (M={m}, K={k}, N={n}): oracle dequant (numpy, {cores} threads) + "
+                      f"torch fp32 matmul ({cores} threads), median",
+            "dequant_s": round(deq, 4), "matmul_s": round(mm, 4)}
+
+
+def run_reference(args):
+    """The reference's CPU dequantize-then-matmul path, timed on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+
+    import torch
+
+    from oracle import q4_oracle as orc
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    m, n, k = args.m, args.n, args.k
+    rows = max(128, n // 8)            # each step: a bounded row slice of the weight matrix
+    w = orc.gen_q4k(rows, k, seed=args.seed) if args.fmt == "q4k" else orc.gen_q4_0(rows, k, seed=args.seed)
+    a = orc.gen_activations(m, k, seed=args.seed + 1)
+    with ThreadPoolExecutor(cores) as pool:
+        for _ in range(max(args.warmup, 1)):
+            _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
+        el = time.perf_counter() - t0
+    t_full = el / args.steps * (n / rows)      # extrapolate the slice to all N rows
+    value = m / t_full
+    out = {"metric": "Q4_K GEMM tokens/s (M / avg GEMM time) at K=N=5120" if args.fmt == "q4k"
+           else "Q4_0 GEMM tokens/s (M / avg GEMM time)",
+           "value": round(value, 2), "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(el / args.steps * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+           "data": "synthetic (seeded numpy RNG, BASELINE config distributions)",
+           "config": {"workload": f"{args.fmt}_gemm_m{m}_k{k}_n{n}", "format": args.fmt, "M": m, "N": n, "K": k,
+                      "parallelism": "host CPU"},
+           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"each step: {rows} of {n} weight rows (dequant + fp32 matmul, "
+                                      f"{cores} threads), extrapolated to N={n}"},
+           "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out))
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_busfill(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,226 @@
+"""bus-fill on B200: Python host API over the C ABI in include/busfill.h.
+
+The kernels live in ``busfill_b200/lib/libbusfill.so`` (built in-tree by
+``python -m busfill_b200.build``). Every call here goes through that C ABI via
+ctypes; there is no CPU or PyTorch fallback -- if the library is missing or the
+device is not sm_100, calls raise :class:`BusfillError`.
+
+Layouts (see include/busfill.h):
+* Q4_0 split planes, the reference's kernel ABI (kernels/busfill_v1a.cu:43-45):
+  ``wq`` uint8 [N, K/2], ``ws`` fp16 [N, K/32].
+* Q4_K: llama.cpp ``block_q4_K`` rows, uint8 [N, K/256*144].
+* activations fp16 [M, K]; outputs fp16 [M, N] (``busfill_q4``: fp32).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+__all__ = [
+    "BusfillError", "load_library", "library_path", "header_functions",
+    "gemm_q4_0", "gemm_q4k", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
+    "stream_status", "set_pdl", "probe_umma", "version",
+]
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+_ROOT = os.path.dirname(_PKG)
+_HEADER = os.path.join(_ROOT, "include", "busfill.h")
+_LIB = None
+
+STATUS = {
+    0: "BUSFILL_OK", -1: "BUSFILL_ERR_INVALID_ARG", -2: "BUSFILL_ERR_SHAPE", -3: "BUSFILL_ERR_ALIGNMENT",
+    -4: "BUSFILL_ERR_UNSUPPORTED_DEVICE", -5: "BUSFILL_ERR_LAUNCH", -6: "BUSFILL_ERR_ALLOC",
+    -7: "BUSFILL_ERR_DEVICE_TIMEOUT", -8: "BUSFILL_ERR_CUDA",
+}
+
+
+class BusfillError(RuntimeError):
+    """A busfill C-ABI call returned a non-zero status."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        text = _LIB.busfill_status_string(status).decode() if _LIB is not None else ""
+        super().__init__(f"{where}: {STATUS.get(status, status)} ({text})")
+
+
+def library_path() -> str:
+    return os.environ.get("BUSFILL_LIB", os.path.join(_PKG, "lib", "libbusfill.so"))
+
+
+def header_functions(path: str = _HEADER):
+    """Names of the functions include/busfill.h declares."""
+    src = open(path).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return re.findall(r"^\s*BUSFILL_API\s+(?:const\s+)?\w+\**\s+\**(busfill_\w+)\s*\(", src, flags=re.M)
+
+
+_P = ctypes.c_void_p
+_I = ctypes.c_int
+_SIGS = {
+    "busfill_gemm_q4_0": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
+    "busfill_dequant_q4_0_ggml": [_P, _P, _I, _I, _P],
+    "busfill_dequant_q4k": [_P, _P, _I, _I, _P],
+    "busfill_stream_status": [_P],
+    "busfill_status_string": [_I],
+    "busfill_version": [],
+    "busfill_set_option": [_I, _I],
+    "busfill_probe_umma": [_P, _P, _P, _I, _P],
+}
+
+
+def load_library(path: str | None = None):
+    """Load libbusfill.so (once) and declare argument types. Raises if absent."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = path or library_path()
+    if not os.path.exists(p):
+        raise RuntimeError(f"libbusfill.so not found at {p}; build it with `python -m busfill_b200.build`")
+    lib = ctypes.CDLL(p)
+    for name, args in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_char_p if name == "busfill_status_string" else ctypes.c_int
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def _lib():
+    if _LIB is None:
+        load_library()
+    return _LIB
+
+
+def version() -> int:
+    return _lib().busfill_version()
+
+
+def set_pdl(enabled: bool) -> None:
+    """Enable/disable programmatic dependent launch for the GEMMs (default on)."""
+    _check(_lib().busfill_set_option(1, 1 if enabled else 0), "busfill_set_option")
+
+
+# ---------------------------------------------------------------------------
+# torch-tensor wrappers
+# ---------------------------------------------------------------------------
+def _torch():
+    import torch
+    return torch
+
+
+def _check(status: int, where: str):
+    if status != 0:
+        raise BusfillError(status, where)
+
+
+def _stream(stream):
+    torch = _torch()
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _need(t, dtype, name, ndim=2):
+    torch = _torch()
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise TypeError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.dim() != ndim or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous {ndim}-D tensor")
+
+
+def gemm_q4_0(wq, ws, a, out=None, stream=None):
+    """C[M, N] = A[M, K] @ deq(Wq, Ws)[N, K]^T for reference split-plane Q4_0; fp16 out."""
+    torch = _torch()
+    _need(wq, torch.uint8, "wq"); _need(ws, torch.float16, "ws"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = wq.shape[0]
+    if wq.shape[1] * 2 != k or ws.shape != (n, k // 32):
+        raise ValueError(f"shape mismatch: wq {tuple(wq.shape)}, ws {tuple(ws.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q4_0(_ptr(wq), _ptr(ws), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
+           "busfill_gemm_q4_0")
+    return out
+
+
+def gemm_q4k(blocks, a, out=None, stream=None):
+    """C[M, N] = A[M, K] @ deq(W)[N, K]^T for llama.cpp block_q4_K rows; fp16 out."""
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = blocks.shape[0]
+    if k % 256 or blocks.shape[1] != k // 256 * 144:
+        raise ValueError(f"shape mismatch: blocks {tuple(blocks.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q4k(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)), "busfill_gemm_q4k")
+    return out
+
+
+def busfill_q4(A, Wq, Ws, C, Bsz, K, N, stream=None):
+    """The reference kernel surface busfill_q4(A, Wq, Ws, C, Bsz, K, N)
+    (kernels/busfill_v1a.cu:41-46): fp32 C [Bsz, N], all Bsz rows computed."""
+    torch = _torch()
+    _need(A, torch.float16, "A"); _need(Wq, torch.uint8, "Wq"); _need(Ws, torch.float16, "Ws")
+    _need(C, torch.float32, "C")
+    _check(_lib().busfill_q4(_ptr(A), _ptr(Wq), _ptr(Ws), _ptr(C), Bsz, K, N, _stream(stream)), "busfill_q4")
+    return C
+
+
+def dequant_q4_0(wq, ws, out=None, stream=None):
+    torch = _torch()
+    _need(wq, torch.uint8, "wq"); _need(ws, torch.float16, "ws")
+    n, k = wq.shape[0], wq.shape[1] * 2
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.float16, device=wq.device)
+    _check(_lib().busfill_dequant_q4_0(_ptr(wq), _ptr(ws), _ptr(out), n, k, _stream(stream)),
+           "busfill_dequant_q4_0")
+    return out
+
+
+def dequant_q4_0_ggml(blocks, k, out=None, stream=None):
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks")
+    n = blocks.shape[0]
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.float16, device=blocks.device)
+    _check(_lib().busfill_dequant_q4_0_ggml(_ptr(blocks), _ptr(out), n, k, _stream(stream)),
+           "busfill_dequant_q4_0_ggml")
+    return out
+
+
+def dequant_q4k(blocks, k, out=None, stream=None):
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks")
+    n = blocks.shape[0]
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.float16, device=blocks.device)
+    _check(_lib().busfill_dequant_q4k(_ptr(blocks), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q4k")
+    return out
+
+
+def stream_status(stream=None) -> int:
+    """Synchronize the stream and return the device-side status code (0 = ok)."""
+    return _lib().busfill_stream_status(_stream(stream))
+
+
+def probe_umma(a, b, nb, stream=None):
+    """tcgen05 operand-layout probe: returns fp32 [128, nb] = a[128,64] @ b[nb,64]^T."""
+    torch = _torch()
+    _need(a, torch.float16, "a"); _need(b, torch.float16, "b")
+    d = torch.empty((128, nb), dtype=torch.float32, device=a.device)
+    _check(_lib().busfill_probe_umma(_ptr(a), _ptr(b), _ptr(d), nb, _stream(stream)), "busfill_probe_umma")
+    return d

@@ -1,0 +1,392 @@
+// Host side of the C ABI declared in include/busfill.h: argument checks,
+// TMA descriptor encoding, the per-(device, stream) split-K workspace and the
+// kernel launches (programmatic dependent launch by default).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "busfill.h"
+#include "decode_gemm.cuh"
+#include "dequant.cuh"
+
+using namespace busfill;
+
+namespace {
+
+constexpr int kVersion = 100;  // 0.1.0
+std::atomic<int> g_use_pdl{1};
+
+// ---------------------------------------------------------------------------
+// device properties (cached)
+// ---------------------------------------------------------------------------
+struct DeviceInfo {
+  int sm_count = 0;
+  int major = 0, minor = 0;
+  bool ok = false;
+};
+
+std::mutex g_mu;
+std::map<int, DeviceInfo> g_devices;
+
+int current_device(DeviceInfo* out, int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_devices.find(dev);
+  if (it == g_devices.end()) {
+    DeviceInfo di;
+    if (cudaDeviceGetAttribute(&di.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&di.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&di.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return BUSFILL_ERR_CUDA;
+    di.ok = (di.major == 10 && di.minor == 0);  // the kernels are built for sm_100a only
+    it = g_devices.emplace(dev, di).first;
+  }
+  *out = it->second;
+  *dev_out = dev;
+  return it->second.ok ? BUSFILL_OK : BUSFILL_ERR_UNSUPPORTED_DEVICE;
+}
+
+// ---------------------------------------------------------------------------
+// TMA descriptors (driver entry point fetched through the runtime, so the
+// library does not link libcuda directly)
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = []() -> EncodeTiledFn {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0, uint64_t dim1,
+                  uint64_t row_stride_bytes, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {dim0, dim1};
+  const cuuint64_t strides[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box0, box1};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------------------
+// workspace: [error word | counters | split-K partials], one per (device,
+// stream) so that calls on different streams never share counters.
+// Counters are zeroed at allocation and returned to zero by every call.
+// ---------------------------------------------------------------------------
+struct Workspace {
+  uint8_t* base = nullptr;
+  size_t counters_cap = 0;   // number of counters
+  size_t partials_cap = 0;   // bytes
+  unsigned* error() const { return reinterpret_cast<unsigned*>(base); }
+  unsigned* counters() const { return reinterpret_cast<unsigned*>(base + 256); }
+  float* partials() const { return reinterpret_cast<float*>(base + 256 + ((counters_cap * 4 + 255) / 256) * 256); }
+};
+
+std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+int get_workspace(int dev, cudaStream_t s, size_t ncounters, size_t partial_bytes, Workspace* out) {
+  // caller holds g_mu
+  Workspace& w = g_ws[{dev, s}];
+  if (w.base && w.counters_cap >= ncounters && w.partials_cap >= partial_bytes) {
+    *out = w;
+    return BUSFILL_OK;
+  }
+  const size_t nc = std::max<size_t>(std::max(ncounters, w.counters_cap), 1024);
+  const size_t pb = std::max(partial_bytes, w.partials_cap);
+  if (w.base) {
+    // the old buffer may still be read by work queued on this stream
+    if (cudaStreamSynchronize(s) != cudaSuccess) return BUSFILL_ERR_CUDA;
+    cudaFree(w.base);
+    w.base = nullptr;
+  }
+  Workspace nw;
+  nw.counters_cap = nc;
+  nw.partials_cap = pb;
+  const size_t head = 256 + ((nc * 4 + 255) / 256) * 256;
+  if (cudaMalloc(&nw.base, head + pb) != cudaSuccess) {
+    cudaGetLastError();
+    w = Workspace{};
+    return BUSFILL_ERR_ALLOC;
+  }
+  if (cudaMemsetAsync(nw.base, 0, head, s) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  w = nw;
+  *out = w;
+  return BUSFILL_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelExC(&cfg, func, args);
+}
+
+// ---------------------------------------------------------------------------
+// decode GEMM launch
+// ---------------------------------------------------------------------------
+template <WFmt FMT, int NB, typename OutT>
+int launch_decode_nb(const DeviceInfo& di, const CUtensorMap& tw, const CUtensorMap& tws, const CUtensorMap& ta,
+                     const DecodeParams& p, cudaStream_t s) {
+  auto kern = decode_gemm_kernel<FMT, NB, OutT>;
+  constexpr int smem = DecodeSmem<NB>::kAlloc;
+  static std::once_flag attr_once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(attr_once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
+  const int grid = std::min(p.units, di.sm_count);
+  void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tws), const_cast<CUtensorMap*>(&ta),
+                  const_cast<DecodeParams*>(&p)};
+  if (launch(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, s, args,
+             g_use_pdl.load() != 0) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_LAUNCH;
+  }
+  return BUSFILL_OK;
+}
+
+int max_contributors(int tiles, int S, int units, int grid) {
+  int best = 1;
+  for (int t = 0; t < tiles; ++t) {
+    const int a = streamk_cta_of((long long)t * S, units, grid);
+    const int b = streamk_cta_of((long long)t * S + S - 1, units, grid);
+    best = std::max(best, b - a + 1);
+  }
+  return best;
+}
+
+template <WFmt FMT, typename OutT>
+int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M, int N, int K,
+              cudaStream_t s) {
+  if (!w || !a || !c || (FMT == WFmt::Q4_0 && !ws)) return BUSFILL_ERR_INVALID_ARG;
+  if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(w) || !aligned16(a) || (ws && !aligned16(ws))) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev = 0;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+
+  const int S = K / kUnitK;
+  const int T = (N + kTileRows - 1) / kTileRows;
+  const long long U64 = (long long)T * S;
+  if (U64 > (1LL << 30)) return BUSFILL_ERR_SHAPE;
+  const int U = (int)U64;
+  const int grid = std::min(U, di.sm_count);
+  const int slots = max_contributors(T, S, U, grid);
+
+  CUtensorMap tw, tws, ta;
+  std::memset(&tws, 0, sizeof(tws));
+  if constexpr (FMT == WFmt::Q4K) {
+    const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    tws = tw;  // unused by the Q4_K kernel
+  } else {
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                      kTileRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return BUSFILL_ERR_CUDA;
+    if (!make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)K / 32, (uint64_t)N, (uint64_t)K / 16, 8,
+                      kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+  }
+
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (int m0 = 0; m0 < M; m0 += 64) {
+    const int mc = std::min(64, M - m0);
+    const int nb = mc <= 16 ? 16 : (mc <= 32 ? 32 : 64);
+    Workspace wsp;
+    st = get_workspace(dev, s, (size_t)T, (size_t)T * slots * kTileRows * nb * sizeof(float), &wsp);
+    if (st != BUSFILL_OK) return st;
+    const uint16_t* a_chunk = a + (size_t)m0 * K;
+    if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_chunk, (uint64_t)K, (uint64_t)mc, (uint64_t)K * 2,
+                      kChunkK, (uint32_t)nb, CU_TENSOR_MAP_SWIZZLE_128B))
+      return BUSFILL_ERR_CUDA;
+    DecodeParams p;
+    p.c = reinterpret_cast<OutT*>(c) + (size_t)m0 * N;
+    p.partials = wsp.partials();
+    p.counters = wsp.counters();
+    p.error = wsp.error();
+    p.M = mc;
+    p.N = N;
+    p.K = K;
+    p.tiles = T;
+    p.units_per_tile = S;
+    p.units = U;
+    p.max_slots = slots;
+    if (nb == 16) st = launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s);
+    else if (nb == 32) st = launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
+    else st = launch_decode_nb<FMT, 64, OutT>(di, tw, tws, ta, p, s);
+    if (st != BUSFILL_OK) return st;
+  }
+  return BUSFILL_OK;
+}
+
+int grid_for(long long work, int sm_count) {
+  const long long g = (work + 255) / 256;
+  return (int)std::max<long long>(1, std::min<long long>(g, (long long)sm_count * 8));
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int busfill_version(void) { return kVersion; }
+
+const char* busfill_status_string(int status) {
+  switch (status) {
+    case BUSFILL_OK: return "ok";
+    case BUSFILL_ERR_INVALID_ARG: return "invalid argument (NULL pointer or unknown option)";
+    case BUSFILL_ERR_SHAPE: return "unsupported shape (need M>=1, N>=1, K a positive multiple of 256)";
+    case BUSFILL_ERR_ALIGNMENT: return "pointer not 16-byte aligned";
+    case BUSFILL_ERR_UNSUPPORTED_DEVICE: return "current device is not sm_100 (B200)";
+    case BUSFILL_ERR_LAUNCH: return "kernel launch failed";
+    case BUSFILL_ERR_ALLOC: return "workspace allocation failed";
+    case BUSFILL_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired (kernel gave up)";
+    case BUSFILL_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int busfill_set_option(int option, int value) {
+  if (option == BUSFILL_OPT_PDL) {
+    g_use_pdl.store(value ? 1 : 0);
+    return BUSFILL_OK;
+  }
+  return BUSFILL_ERR_INVALID_ARG;
+}
+
+int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                      void* stream) {
+  return gemm_impl<WFmt::Q4_0, __half>(wq, ws, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
+  return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_q4(const uint16_t* A, const uint8_t* Wq, const uint16_t* Ws, float* C, int Bsz, int K, int N,
+               void* stream) {
+  return gemm_impl<WFmt::Q4_0, float>(Wq, Ws, A, C, Bsz, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_dequant_q4_0(const uint8_t* wq, const uint16_t* ws, uint16_t* out, int N, int K, void* stream) {
+  if (!wq || !ws || !out) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 32 || K % 32 != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(wq) || !aligned16(out)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nb = (long long)N * (K / 32);
+  dequant_q4_0_planes_kernel<<<grid_for(nb, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      wq, reinterpret_cast<const __half*>(ws), reinterpret_cast<__half*>(out), nb);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_dequant_q4_0_ggml(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream) {
+  if (!blocks || !out) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 32 || K % 32 != 0) return BUSFILL_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(blocks) & 1u) || !aligned16(out)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nb = (long long)N * (K / 32);
+  dequant_q4_0_ggml_kernel<<<grid_for(nb, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      blocks, reinterpret_cast<__half*>(out), nb);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream) {
+  if (!blocks || !out) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 256 || K % 256 != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(blocks) || !aligned16(out)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nc = (long long)N * (K / 256) * 4;
+  dequant_q4k_kernel<<<grid_for(nc, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      blocks, reinterpret_cast<__half*>(out), nc);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_stream_status(void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_ws.find({dev, s});
+  if (it == g_ws.end() || !it->second.base) return BUSFILL_OK;
+  unsigned err = 0;
+  if (cudaMemcpy(&err, it->second.error(), sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return BUSFILL_ERR_CUDA;
+  if (err == 0) return BUSFILL_OK;
+  // a kernel gave up part way: clear the error word and the split-K counters
+  const size_t head = 256 + ((it->second.counters_cap * 4 + 255) / 256) * 256;
+  if (cudaMemset(it->second.base, 0, head) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  return BUSFILL_ERR_DEVICE_TIMEOUT;
+}
+
+int busfill_probe_umma(const uint16_t* a, const uint16_t* b, float* d, int nb, void* stream) {
+  if (!a || !b || !d) return BUSFILL_ERR_INVALID_ARG;
+  if (nb != 16 && nb != 32 && nb != 64) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(d)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  Workspace wsp;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = get_workspace(dev, s, 1, 0, &wsp);
+  }
+  if (st != BUSFILL_OK) return st;
+  const __half* ah = reinterpret_cast<const __half*>(a);
+  const __half* bh = reinterpret_cast<const __half*>(b);
+  if (nb == 16) umma_probe_kernel<16><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
+  else if (nb == 32) umma_probe_kernel<32><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
+  else umma_probe_kernel<64><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+/*
+ * busfill.h -- C ABI of the B200 (sm_100a) batched dequant-fused 4-bit-weight
+ * GEMM.  C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 activations, fp32
+ * accumulation.
+ *
+ * Conventions for every entry point:
+ *   - all array pointers are DEVICE pointers owned by the caller;
+ *   - fp16 data is passed as uint16_t (IEEE binary16 bit patterns);
+ *   - `stream` is a cudaStream_t (NULL = the legacy default stream);
+ *   - calls are asynchronous on `stream` and never synchronize; errors that
+ *     can only be seen on the device (a bounded wait that expired) are
+ *     reported by busfill_stream_status();
+ *   - the return value is BUSFILL_OK (0) or a negative busfill_status code;
+ *     nothing aborts the process.
+ *
+ * Each entry point names the reference interface it replaces
+ * (thegliffy/bus-fill, file:line).
+ */
+#ifndef BUSFILL_H_
+#define BUSFILL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BUSFILL_API __attribute__((visibility("default")))
+#else
+#define BUSFILL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum busfill_status {
+  BUSFILL_OK = 0,
+  BUSFILL_ERR_INVALID_ARG = -1,        /* NULL pointer or bad option        */
+  BUSFILL_ERR_SHAPE = -2,              /* M/N/K out of the supported range  */
+  BUSFILL_ERR_ALIGNMENT = -3,          /* pointer not 16-byte aligned       */
+  BUSFILL_ERR_UNSUPPORTED_DEVICE = -4, /* current device is not sm_100      */
+  BUSFILL_ERR_LAUNCH = -5,             /* kernel launch failed              */
+  BUSFILL_ERR_ALLOC = -6,              /* workspace allocation failed       */
+  BUSFILL_ERR_DEVICE_TIMEOUT = -7,     /* a bounded device wait expired     */
+  BUSFILL_ERR_CUDA = -8                /* other CUDA runtime error          */
+} busfill_status;
+
+/* ---------------------------------------------------------------------------
+ * GEMMs
+ * ------------------------------------------------------------------------- */
+
+/* Q4_0 in the reference's split-plane layout, fp16 output.
+ *   wq [N, K/2] u8  : byte j of 32-value block b holds element 32b+2j in its
+ *                     low nibble and 32b+2j+1 in its high nibble;
+ *   ws [N, K/32] fp16 scales d;  value = (nibble - 8) * d.
+ *   a  [M, K] fp16 row-major;  c [M, N] fp16 row-major.
+ * Requires K % 256 == 0, M >= 1, N >= 1; wq, ws, a 16-byte aligned.
+ * Replaces busfill_q4 (kernels/busfill_v1a.cu:41-46; launch :151-154), with
+ * fp16 output, any M (the reference computes only rows < 32) and any N. */
+BUSFILL_API int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                      void* stream);
+
+/* Q4_K: llama.cpp block_q4_K rows, K/256 blocks of 144 bytes per weight row
+ * (fp16 d, fp16 dmin, 12 bytes of packed 6-bit sub-block scales and mins,
+ * 128 nibble bytes); value = d*sc*q - dmin*m.  a [M, K] fp16, c [M, N] fp16.
+ * Requires K % 256 == 0; blocks and a 16-byte aligned.
+ * The reference has no Q4_K kernel; this is the Q4_K counterpart of
+ * busfill_q4 (kernels/busfill_v1a.cu:41-46) that its docstring announces
+ * (kernels/q4k_batched.py:7-8). */
+BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
+
+/* Reference-compatible surface: the arguments and fp32 output of
+ * busfill_q4(A, Wq, Ws, C, Bsz, K, N) (kernels/busfill_v1a.cu:41-46) plus a
+ * stream, as a host function instead of a <<<N/32, 128>>> launch
+ * (kernels/busfill_v1a.cu:151-154). Every row b < Bsz is computed (the
+ * reference silently skips rows >= 32). */
+BUSFILL_API int busfill_q4(const uint16_t* A, const uint8_t* Wq, const uint16_t* Ws, float* C, int Bsz, int K, int N,
+               void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Dequantization to fp16 [N, K] row-major (bit-exact)
+ * ------------------------------------------------------------------------- */
+
+/* fp16_rn((q - 8) * d): the dequant of kernels/busfill_v0.cu:74-81 (which
+ * kernels/busfill_v1a.cu:6-20 reproduces bit for bit). K % 32 == 0. */
+BUSFILL_API int busfill_dequant_q4_0(const uint8_t* wq, const uint16_t* ws, uint16_t* out, int N, int K, void* stream);
+
+/* llama.cpp block_q4_0 rows (18-byte blocks), same value rule. K % 32 == 0.
+ * No reference counterpart: the layout the reference's comment names
+ * (kernels/busfill_v0.cu:18-20). */
+BUSFILL_API int busfill_dequant_q4_0_ggml(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream);
+
+/* fp16_rn(fp32(d)*sc*q - fp32(dmin)*m) per llama.cpp block_q4_K. K % 256 == 0.
+ * No reference counterpart (the reference has no Q4_K code). */
+BUSFILL_API int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Status, options, diagnostics
+ * ------------------------------------------------------------------------- */
+
+/* Synchronizes `stream`, then reports (and clears) the device-side error word
+ * of the workspace bound to this stream: BUSFILL_OK, BUSFILL_ERR_DEVICE_TIMEOUT
+ * or BUSFILL_ERR_CUDA. The reference has no error reporting at all
+ * (kernels/busfill_v1a.cu:155-158 only prints launch/sync strings). */
+BUSFILL_API int busfill_stream_status(void* stream);
+
+/* Human-readable text for a busfill_status value. */
+BUSFILL_API const char* busfill_status_string(int status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+BUSFILL_API int busfill_version(void);
+
+/* Options (process-wide). BUSFILL_OPT_PDL: 1 (default) launches the GEMMs with
+ * programmatic dependent launch so back-to-back calls on one stream overlap
+ * the next call's weight streaming with the previous call's tail; 0 disables. */
+#define BUSFILL_OPT_PDL 1
+BUSFILL_API int busfill_set_option(int option, int value);
+
+/* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the
+ * spirit of kernels/frag_probe.cu:1-48: d[128, nb] = a[128, 64] * b[nb, 64]^T
+ * with a in tensor memory and b in 128-byte-swizzled shared memory.
+ * nb in {16, 32, 64}; one CTA; fp32 out. */
+BUSFILL_API int busfill_probe_umma(const uint16_t* a, const uint16_t* b, float* d, int nb, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BUSFILL_H_ */

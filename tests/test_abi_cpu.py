@@ -1,0 +1,201 @@
+"""CPU-side checks of the C ABI and of the kernels' host/bit-level logic.
+
+No GPU: the library is loaded and its exports and status strings checked; the
+dequant instruction chains of busfill_b200/csrc/decode_gemm.cuh are emulated
+bit for bit in numpy and compared with the oracle; the stream-K partition
+arithmetic is checked exhaustively on small sizes.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+import busfill_b200 as bf
+from oracle import q4_oracle as orc
+
+
+def test_library_loads_and_exports_every_header_function():
+    names = bf.header_functions()
+    assert len(names) >= 10
+    lib = bf.load_library()
+    for n in names:
+        assert hasattr(lib, n), n
+    raw = ctypes.CDLL(bf.library_path())
+    for n in names:
+        getattr(raw, n)  # raises AttributeError if not exported
+
+
+def test_status_strings_and_version():
+    lib = bf.load_library()
+    assert bf.version() >= 100
+    for code, name in bf.STATUS.items():
+        s = lib.busfill_status_string(code)
+        assert isinstance(s, bytes) and len(s) > 0
+    assert lib.busfill_status_string(12345) == b"unknown status"
+
+
+def test_set_option_rejects_unknown():
+    lib = bf.load_library()
+    assert lib.busfill_set_option(99, 1) == -1
+    assert lib.busfill_set_option(1, 1) == 0
+
+
+def test_null_pointer_rejected_before_any_device_work():
+    lib = bf.load_library()
+    # argument validation happens before the device is touched
+    assert lib.busfill_gemm_q4k(None, None, None, 8, 128, 256, None) == -1
+    assert lib.busfill_gemm_q4_0(None, None, None, None, 8, 128, 256, None) == -1
+    assert lib.busfill_dequant_q4k(None, None, 4, 256, None) == -1
+    assert lib.busfill_probe_umma(None, None, None, 16, None) == -1
+
+
+# ---------------------------------------------------------------------------
+# bit-level emulation of the device dequant chains
+# ---------------------------------------------------------------------------
+def prmt(a, b, sel):
+    a = np.asarray(a, dtype=np.uint64)
+    b = np.asarray(b, dtype=np.uint64)
+    src = [(a >> (8 * i)) & 0xFF for i in range(4)] + [(b >> (8 * i)) & 0xFF for i in range(4)]
+    out = np.zeros_like(a)
+    for i in range(4):
+        idx = (sel >> (4 * i)) & 0x7
+        out |= src[idx] << (8 * i)
+    return out.astype(np.uint32)
+
+
+def lop3_and_or(a, b, c):
+    return ((np.asarray(a, np.uint32) & np.uint32(b)) | np.uint32(c)).astype(np.uint32)
+
+
+def h2(u):
+    """uint32 -> (lo, hi) float16 halves."""
+    u = np.asarray(u, dtype=np.uint32)
+    return (u & 0xFFFF).astype(np.uint16).view(np.float16), (u >> 16).astype(np.uint16).view(np.float16)
+
+
+def rn16(x64):
+    return np.asarray(x64, dtype=np.float64).astype(np.float16)
+
+
+def hfma(x, y, z):
+    return rn16(np.float64(x) * np.float64(y) + np.float64(z))
+
+
+@pytest.mark.filterwarnings("ignore:overflow encountered")
+def test_q4_0_block_chain_matches_reference_dequant_for_all_fp16_scales():
+    # kernel: t = prmt(w, w>>4, ((4+x)<<8)|x); v = lop3(t & 0x000F000F | 0x64006400);
+    #         out = hmul2(hsub2(v, 1032), d)  ==  fp16_rn((q-8)*d)  (busfill_v0.cu:74-81)
+    d_bits = np.arange(0, 0x7C00, dtype=np.uint32)          # every finite non-negative fp16
+    d_bits = np.concatenate([d_bits, d_bits | 0x8000])       # and negative
+    d = d_bits.astype(np.uint16).view(np.float16)
+    for byte in range(256):
+        w = np.full(d.shape, byte * 0x01010101, dtype=np.uint32)
+        for x in range(4):
+            t = prmt(w, w >> np.uint32(4), ((4 + x) << 8) | x)
+            v = lop3_and_or(t, 0x000F000F, 0x64006400)
+            lo, hi = h2(v)
+            assert np.all(lo.astype(np.float64) == 1024 + (byte & 15))
+            assert np.all(hi.astype(np.float64) == 1024 + (byte >> 4))
+        q_lo, q_hi = byte & 15, byte >> 4
+        got_lo = rn16((np.float16(1024 + q_lo) - np.float16(1032)).astype(np.float64) * d.astype(np.float64))
+        want_lo = (np.float32(q_lo - 8) * d.astype(np.float32)).astype(np.float16)
+        assert np.array_equal(got_lo.view(np.uint16), want_lo.view(np.uint16))
+        got_hi = rn16((np.float16(1024 + q_hi) - np.float16(1032)).astype(np.float64) * d.astype(np.float64))
+        want_hi = (np.float32(q_hi - 8) * d.astype(np.float32)).astype(np.float16)
+        assert np.array_equal(got_hi.view(np.uint16), want_hi.view(np.uint16))
+
+
+def test_q4_0_block_chain_column_order_is_natural():
+    rng = np.random.default_rng(0)
+    blk = rng.integers(0, 256, size=16, dtype=np.uint8)
+    words = blk.view(np.uint32)
+    cols = []
+    for i in range(4):
+        w = np.uint32(words[i])
+        for x in range(4):
+            t = prmt(w, w >> np.uint32(4), ((4 + x) << 8) | x)
+            lo, hi = h2(lop3_and_or(t, 0x000F000F, 0x64006400))
+            cols.append((float(lo) - 1024, float(hi) - 1024))
+    nib = orc.unpack_q4_0_planes(blk.reshape(1, 16))[0]
+    # column c holds elements (2c, 2c+1)
+    assert [v for pair in cols for v in pair] == [float(v) for v in nib]
+
+
+def test_q4k_chunk_chain_gives_exact_sc_times_q():
+    # lo: hfma2(1024+q, sc, -1024*sc) == sc*q ; hi: hfma2(1024+16q, sc/16, -64*sc) == sc*q
+    for sc in range(64):
+        s16 = np.float16(sc)
+        for q in range(16):
+            lo = hfma(np.float16(1024 + q), s16, np.float16(-1024.0 * sc))
+            hi = hfma(np.float16(1024 + 16 * q), np.float16(sc / 16.0), np.float16(-64.0 * sc))
+            assert float(lo) == sc * q and float(hi) == sc * q
+            # the constants themselves are exact fp16 values
+            assert float(np.float16(-1024.0 * sc)) == -1024.0 * sc
+            assert float(np.float16(sc / 16.0)) == sc / 16.0
+
+
+def test_q4k_chunk_extraction_and_order():
+    rng = np.random.default_rng(1)
+    chunk = rng.integers(0, 256, size=32, dtype=np.uint8)
+    words = chunk.view(np.uint32)
+    lo_cols, hi_cols = [], []
+    for i in range(8):
+        w = np.uint32(words[i])
+        t0 = prmt(w, w, 0x0100)
+        t1 = prmt(w, w, 0x0302)
+        for t in (t0, t1):
+            a, b = h2(lop3_and_or(t, 0x000F000F, 0x64006400))
+            lo_cols += [float(a) - 1024, float(b) - 1024]
+            a, b = h2(lop3_and_or(t, 0x00F000F0, 0x64006400))
+            hi_cols += [(float(a) - 1024) / 16, (float(b) - 1024) / 16]
+    assert lo_cols == [float(v & 15) for v in chunk]      # sub-block 2c, elements 0..31
+    assert hi_cols == [float(v >> 4) for v in chunk]      # sub-block 2c+1
+
+
+def test_q4k_scale_words_match_oracle_unpack():
+    rng = np.random.default_rng(2)
+    s = rng.integers(0, 256, size=(4096, 12), dtype=np.uint8)
+    y = s[:, 0:4].copy().view(np.uint32)[:, 0]
+    z = s[:, 4:8].copy().view(np.uint32)[:, 0]
+    w = s[:, 8:12].copy().view(np.uint32)[:, 0]
+    sc_lo = y & 0x3F3F3F3F
+    m_lo = z & 0x3F3F3F3F
+    sc_hi = (w & 0x0F0F0F0F) | ((y >> 2) & 0x30303030)
+    m_hi = ((w >> 4) & 0x0F0F0F0F) | ((z >> 2) & 0x30303030)
+    sc, m = orc.unpack_q4k_scales(s)
+    for j in range(8):
+        word_sc = sc_lo if j < 4 else sc_hi
+        word_m = m_lo if j < 4 else m_hi
+        assert np.array_equal((word_sc >> (8 * (j % 4))) & 0xFF, sc[:, j])
+        assert np.array_equal((word_m >> (8 * (j % 4))) & 0xFF, m[:, j])
+    # six_bit_pair_to_h2: prmt(word, 0x64646464, 0x4140 / 0x4342) -> {1024+v0, 1024+v1}
+    for cpair, sel in ((0, 0x4140), (1, 0x4342)):
+        a, b = h2(prmt(sc_lo, np.uint32(0x64646464), sel))
+        assert np.array_equal(a.astype(np.float64) - 1024, sc[:, 2 * cpair].astype(np.float64))
+        assert np.array_equal(b.astype(np.float64) - 1024, sc[:, 2 * cpair + 1].astype(np.float64))
+
+
+# ---------------------------------------------------------------------------
+# stream-K partition arithmetic (decode_gemm.cuh: streamk_first_unit / streamk_cta_of)
+# ---------------------------------------------------------------------------
+def first_unit(c, units, grid):
+    return (c * units) // grid
+
+
+def cta_of(u, units, grid):
+    return ((u + 1) * grid + units - 1) // units - 1
+
+
+@pytest.mark.parametrize("units", [1, 2, 3, 7, 40, 148, 149, 800, 801, 3000])
+def test_streamk_partition_is_consistent(units):
+    for grid in sorted({1, 2, 5, 37, 148, min(units, 148)}):
+        if grid > units:
+            continue
+        owner = np.empty(units, dtype=np.int64)
+        for c in range(grid):
+            a, b = first_unit(c, units, grid), first_unit(c + 1, units, grid)
+            assert b - a >= 1  # no CTA is idle when grid <= units
+            owner[a:b] = c
+        assert first_unit(grid, units, grid) == units
+        for u in range(units):
+            assert cta_of(u, units, grid) == owner[u]
