@@ -42,7 +42,7 @@ FALLBACK_BF16_TFLOPS = 1590.0
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["busfill", "reference"], default="busfill")
     ap.add_argument("--fmt", choices=["q4k", "q4_0"], default="q4k")
@@ -210,6 +210,11 @@ def run_busfill(args):
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
+        gemm(weights[0], stream)                  # one call first: fail fast on a device-side error
+    st0, bits0 = bf.stream_status_bits(stream)
+    if st0 != 0:
+        raise SystemExit(f"device-side error on the first call: status {st0}, error bits {bits0:#x}")
+    with torch.cuda.stream(stream):
         for _ in range(max(args.warmup, 3)):      # W untimed warm-up steps (also sizes the workspace)
             one_step(stream)
     stream.synchronize()
@@ -223,8 +228,9 @@ def run_busfill(args):
                 fn(stream)
         return g
 
-    def time_graph(g, sampler=None):
-        g.replay()                                 # upload / first-replay cost, untimed
+    def time_graph(g, replays=1, sampler=None):
+        with torch.cuda.stream(stream):            # CUDAGraph.replay() launches on the current stream
+            g.replay()                             # upload / first-replay cost, untimed
         stream.synchronize()
         if world > 1:
             dist.barrier()
@@ -232,9 +238,10 @@ def run_busfill(args):
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         ctx = sampler if sampler is not None else _Null()
-        with ctx:
+        with ctx, torch.cuda.stream(stream):
             e0.record(stream)
-            g.replay()
+            for _ in range(replays):
+                g.replay()
             e1.record(stream)
             e1.synchronize()
         torch.cuda.synchronize(dev)
@@ -247,9 +254,10 @@ def run_busfill(args):
         return ms
 
     steps = args.steps
-    g_main = capture(steps)
+    spg = max(d for d in range(1, min(steps, 100) + 1) if steps % d == 0)   # steps per graph
+    g_main = capture(spg)
     sampler = ClockSampler(local)
-    ms = time_graph(g_main, sampler)
+    ms = time_graph(g_main, steps // spg, sampler)
     del g_main
     if bf.stream_status(stream) != 0:
         raise SystemExit("device-side error in the timed region")
@@ -280,8 +288,8 @@ def run_busfill(args):
             "weight_copies": R, "weight_set_bytes": R * wbytes,
             "l2": f"inputs larger than L2: {R} rotating weight copies, {R * wbytes / 1e6:.0f} MB > 2x L2 "
                   f"({l2 / 1e6:.0f} MB)",
-            "timing": "CUDA graph of steps*R back-to-back GEMM launches (PDL on), CUDA events on the "
-                      "launching stream, max over ranks",
+            "timing": f"CUDA graph of {spg} steps x {R} back-to-back GEMM launches (PDL on), replayed "
+                      f"{steps // spg}x; CUDA events on the launching stream, max over ranks",
         },
         "gpu_launches": launches,
         "roofline": {
@@ -308,6 +316,19 @@ def run_busfill(args):
         dist.destroy_process_group()
 
 
+def _time_on(torch, g, st):
+    """Replay graph g on stream st once untimed, then once between CUDA events on st."""
+    with torch.cuda.stream(st):
+        g.replay()
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
 class _Null:
     def __enter__(self):
         return self
@@ -320,7 +341,7 @@ def isolated_no_pdl(bf, capture, time_graph, steps, R, M):
     bf.set_pdl(False)
     try:
         g = capture(steps)
-        ms = time_graph(g)
+        ms = time_graph(g, 1)
         del g
     finally:
         bf.set_pdl(True)
@@ -364,14 +385,7 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         with torch.cuda.graph(g, stream=st):
             for _ in range(nsteps):
                 step()
-        g.replay()
-        st.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        g.replay()
-        e1.record(st)
-        e1.synchronize()
-        ms = e0.elapsed_time(e1)
+        ms = _time_on(torch, g, st)
         assert bf.stream_status(st) == 0
         us = ms * 1e3 / (nsteps * R)
         gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
@@ -409,14 +423,7 @@ def cublas_comparator(torch, bf, dev, l2, weights, a, args):
     with torch.cuda.graph(g, stream=st):
         for _ in range(nsteps):
             step()
-    g.replay()
-    st.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    g.replay()
-    e1.record(st)
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / (nsteps * R)
+    us = _time_on(torch, g, st) * 1e3 / (nsteps * R)
     del g, ws
     torch.cuda.empty_cache()
     m = a.shape[0]

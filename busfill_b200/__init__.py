@@ -20,7 +20,7 @@ import re
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
-    "stream_status", "set_pdl", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "set_pdl", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -65,6 +65,8 @@ _SIGS = {
     "busfill_dequant_q4_0_ggml": [_P, _P, _I, _I, _P],
     "busfill_dequant_q4k": [_P, _P, _I, _I, _P],
     "busfill_stream_status": [_P],
+    "busfill_stream_status_ex": [_P, ctypes.POINTER(ctypes.c_uint)],
+    "busfill_last_failure_detail": [],
     "busfill_status_string": [_I],
     "busfill_version": [],
     "busfill_set_option": [_I, _I],
@@ -84,7 +86,8 @@ def load_library(path: str | None = None):
     for name, args in _SIGS.items():
         fn = getattr(lib, name)
         fn.argtypes = args
-        fn.restype = ctypes.c_char_p if name == "busfill_status_string" else ctypes.c_int
+        fn.restype = (ctypes.c_char_p if name == "busfill_status_string"
+                      else ctypes.c_uint if name == "busfill_last_failure_detail" else ctypes.c_int)
     if path is None:
         _LIB = lib
     return lib
@@ -215,6 +218,14 @@ def dequant_q4k(blocks, k, out=None, stream=None):
 def stream_status(stream=None) -> int:
     """Synchronize the stream and return the device-side status code (0 = ok)."""
     return _lib().busfill_stream_status(_stream(stream))
+
+
+def stream_status_bits(stream=None):
+    """(status, error_bits): the device error word names the kernel roles whose
+    bounded wait expired (see include/busfill.h)."""
+    bits = ctypes.c_uint(0)
+    st = _lib().busfill_stream_status_ex(_stream(stream), ctypes.byref(bits))
+    return st, bits.value
 
 
 def probe_umma(a, b, nb, stream=None):

@@ -21,6 +21,8 @@ using namespace busfill;
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
+// detail word of the last device failure read by busfill_stream_status_ex
+std::atomic<unsigned> g_last_detail{0};
 std::atomic<int> g_use_pdl{1};
 
 // ---------------------------------------------------------------------------
@@ -222,9 +224,9 @@ int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, 
   }
 
   std::lock_guard<std::mutex> lk(g_mu);
-  for (int m0 = 0; m0 < M; m0 += 64) {
-    const int mc = std::min(64, M - m0);
-    const int nb = mc <= 16 ? 16 : (mc <= 32 ? 32 : 64);
+  for (int m0 = 0; m0 < M; m0 += 32) {
+    const int mc = std::min(32, M - m0);
+    const int nb = mc <= 16 ? 16 : 32;
     Workspace wsp;
     st = get_workspace(dev, s, (size_t)T, (size_t)T * slots * kTileRows * nb * sizeof(float), &wsp);
     if (st != BUSFILL_OK) return st;
@@ -245,8 +247,7 @@ int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, 
     p.units = U;
     p.max_slots = slots;
     if (nb == 16) st = launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s);
-    else if (nb == 32) st = launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
-    else st = launch_decode_nb<FMT, 64, OutT>(di, tw, tws, ta, p, s);
+    else st = launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
     if (st != BUSFILL_OK) return st;
   }
   return BUSFILL_OK;
@@ -265,6 +266,8 @@ int grid_for(long long work, int sm_count) {
 extern "C" {
 
 int busfill_version(void) { return kVersion; }
+
+unsigned busfill_last_failure_detail(void) { return g_last_detail.load(); }
 
 const char* busfill_status_string(int status) {
   switch (status) {
@@ -345,7 +348,10 @@ int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N, int K, void
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
 }
 
-int busfill_stream_status(void* stream) {
+int busfill_stream_status(void* stream) { return busfill_stream_status_ex(stream, nullptr); }
+
+int busfill_stream_status_ex(void* stream, unsigned* bits) {
+  if (bits) *bits = 0;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (cudaStreamSynchronize(s) != cudaSuccess) {
     cudaGetLastError();
@@ -356,9 +362,14 @@ int busfill_stream_status(void* stream) {
   std::lock_guard<std::mutex> lk(g_mu);
   auto it = g_ws.find({dev, s});
   if (it == g_ws.end() || !it->second.base) return BUSFILL_OK;
-  unsigned err = 0;
-  if (cudaMemcpy(&err, it->second.error(), sizeof(err), cudaMemcpyDeviceToHost) != cudaSuccess)
+  unsigned err2[2] = {0, 0};
+  if (cudaMemcpy(err2, it->second.error(), sizeof(err2), cudaMemcpyDeviceToHost) != cudaSuccess)
     return BUSFILL_ERR_CUDA;
+  const unsigned err = err2[0];
+  if (bits) {
+    bits[0] = err;
+    g_last_detail = err2[1];
+  }
   if (err == 0) return BUSFILL_OK;
   // a kernel gave up part way: clear the error word and the split-K counters
   const size_t head = 256 + ((it->second.counters_cap * 4 + 255) / 256) * 256;

@@ -1,43 +1,62 @@
-// Batched dequant-fused 4-bit-weight GEMM for small batches (M <= 64) on
-// sm_100a:  C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 in, fp32 accumulate.
+// Batched dequant-fused 4-bit-weight GEMM for small batches (M <= 32 per
+// launch) on sm_100a:  C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 in, fp32
+// accumulate.
 //
 // Replaces the reference kernel `busfill_q4` (kernels/busfill_v1a.cu:41-104,
-// launched <<<N/32, 128>>> at kernels/busfill_v1a.cu:151-154), which is an
-// sm_70 mma.m8n8k4 loop capped at 32 batch rows.
+// launched <<<N/32, 128>>> at kernels/busfill_v1a.cu:151-154), an sm_70
+// mma.m8n8k4 loop capped at 32 batch rows.
 //
-// Design (one persistent CTA per SM, 12 warps):
-//   warp 0      TMA producer for the weight stream: one 2D box of 128 weight
-//               rows x one 256-value unit per stage (18 KB) into a 6-stage
-//               shared-memory ring. Weights do not depend on earlier kernels,
-//               so this starts before griddepcontrol.wait (PDL overlap).
-//   warp 2      TMA producer for activations: one 64-value x NB-row box per
-//               chunk, 128-byte swizzled (the UMMA K-major SW128 layout).
-//   warps 4-11  dequant: thread (warp%4, lane) owns weight row 32*(warp%4)+lane
-//               and writes its fp16 operand straight into TMEM with
-//               tcgen05.st (the tensor core reads A from TMEM); the same warps
-//               run the per-unit epilogue from TMEM.
-//   warp 1      TMEM allocator + the single MMA-issuing thread:
-//               tcgen05.mma.cta_group::1.kind::f16, M=128 weight rows, N=NB
-//               batch rows (swap-AB), K=16 per instruction.
+// Shape of the computation. Work is cut into units of 128 weight rows x 256 K
+// (one Q4_K super-block, eight Q4_0 blocks), each unit into four 64-value
+// chunks. The tensor core runs swap-AB: the 128 weight rows are the MMA M
+// dimension, read from tensor memory (TMEM); the batch rows (padded to NB)
+// are N, read from shared memory (K-major, 128-byte swizzle).
 //
-// Work split: the GEMM is cut into units of (128 weight rows) x (256 K).
-// CTA c of G takes units [floor(c*U/G), floor((c+1)*U/G)) in tile-major
-// order ("stream-K"), so every SM streams the same number of weight bytes.
-// A tile split across CTAs is reduced deterministically: each contributor
-// stores its fp32 partial in its slot, the last arriver (by an atomic
-// counter) sums the slots in slot order and writes C, then resets the counter.
+// Synchronisation is per unit, not per chunk: measured on B200, every
+// mbarrier probe on the MMA-issuing warp's path costs 40-75 cycles while an
+// N=32 MMA issues in ~17, so the MMA warp waits once per unit (`ready`),
+// issues the unit's 16 (Q4_K: 17) MMAs back to back and commits once
+// (`udone`), which releases the unit's operand and activation slots and
+// publishes its accumulator. Three unit slots are kept in flight.
+//
+// Warp roles (16 warps, one persistent CTA per SM):
+//   0      weight TMA producer: one 2D box of 128 rows x one unit (18 KB) per
+//          stage into a 6-stage ring. Weights do not depend on earlier kernels,
+//          so this runs before griddepcontrol.wait (programmatic dependent
+//          launch lets it overlap the previous kernel's tail).
+//   1      activation TMA producer: four 64-value x NB-row boxes per unit
+//          (128-byte swizzle); TMEM allocator.
+//   2      activation stage: waits for a unit's activations, computes (Q4_K)
+//          the 32-value sub-block sums Asum, then marks the activations ready.
+//   3      MMA issuer (converged warp, one elected thread issues).
+//   4-11   dequant: thread (warp%4, lane) owns weight row 32*(warp%4)+lane and
+//          writes its fp16 operand into TMEM with tcgen05.st; warp group g =
+//          (warp-4)/4 handles chunks {g, g+2} of every unit.
+//   12-15  epilogue: row 32*(warp%4)+lane, all NB batch columns; prepares the
+//          per-unit scales ahead of time, folds accumulators, flushes.
 //
 // Numerics.
-//   Q4_0: the operand is fp16_rn((q-8)*d), bit-identical to the reference
-//   dequant (kernels/busfill_v0.cu:74-81): lop3 magic bias 0x6400 gives the
-//   exact fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
-//   Q4_K: w = d*sc*q - dmin*m. The operand is P = sc*q, made exactly in fp16
-//   by one hfma2 ((1024+q)*sc - 1024*sc; the high nibble arrives as 1024+16q
-//   and uses sc/16 and 64*sc, both exact). A second operand holds m broadcast
-//   over its 32-value sub-block. Per unit the tensor core accumulates
-//   X = sum A*P and Y = sum A*m in fp32; the epilogue adds d*X - dmin*Y in
-//   fp32. All products are exact, so the result equals an fp32-accumulated
-//   matmul of the exact dequantized weights up to summation order.
+//   Q4_0: operand fp16_rn((q-8)*d), bit-identical to the reference dequant
+//   (kernels/busfill_v0.cu:74-81): the lop3 magic bias 0x6400 gives the exact
+//   fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
+//   Q4_K: w = d*sc*q - dmin*m. Operand P = sc*q, exact in fp16 from one hfma2
+//   ((1024+q)*sc - 1024*sc; high nibbles arrive as 1024+16q and use sc/16 and
+//   64*sc, both exact). Per unit the epilogue adds d * X in fp32. The min
+//   term sum_k A*dmin*m = sum_j (dmin*m_j) * Asum_j is one K=16 MMA per unit:
+//   dmin*m_j (exact in fp32, 17 significant bits) is split into fp16 hi + lo
+//   summing to it exactly, and Asum_j is the fp16 pairwise sum of the 32
+//   activations of sub-block j (the only rounding the Q4_K path adds beyond
+//   fp32 accumulation).
+//
+// Work split ("stream-K"): CTA c of G takes units [floor(c*U/G),
+// floor((c+1)*U/G)) in tile-major order, so every SM streams the same number
+// of weight bytes. A tile split across CTAs is reduced deterministically: each
+// contributor stores its fp32 partial in its slot, the last arriver (atomic
+// counter, release/acquire) sums the slots in slot order, writes C and resets
+// the counter.
+//
+// Every wait is bounded (ptx.cuh: kWaitTimeoutNs): a kernel that cannot make
+// progress records an error bit and winds down instead of hanging the GPU.
 #pragma once
 
 #include <cuda.h>
@@ -51,18 +70,24 @@ namespace busfill {
 enum class WFmt : int { Q4_0 = 0, Q4K = 1 };
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
-constexpr int kUnitK = 256;          // K per unit: one Q4_K super-block / eight Q4_0 blocks
-constexpr int kChunkK = 64;          // K per TMEM operand stage and per activation box
+constexpr int kUnitK = 256;          // K per unit
+constexpr int kChunkK = 64;          // K per activation box / 32 TMEM operand columns
 constexpr int kChunksPerUnit = kUnitK / kChunkK;
 constexpr int kQ4KBlockBytes = 144;
 constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
 constexpr int kQ40ScaleOffset = 16384;
 constexpr int kWStages = 6;
-constexpr int kXStages = 8;
-constexpr int kAStages = 4;          // TMEM operand stages, 64 columns each
-constexpr int kThreads = 384;
-constexpr int kFirstDequantWarp = 4;
-constexpr int kDequantThreads = 256;
+constexpr int kSlots = 3;            // units in flight between dequant/activations and the MMA
+constexpr int kDStages = 4;          // per-unit row scales prepared ahead by the epilogue
+constexpr int kPrepAhead = 2;        // units the epilogue prepares ahead of its fold
+constexpr int kThreads = 512;
+constexpr int kWarpWProducer = 0;
+constexpr int kWarpXProducer = 1;
+constexpr int kWarpXStage = 2;
+constexpr int kWarpMma = 3;
+constexpr int kWarpDequant0 = 4;
+constexpr int kWarpEpilogue0 = 12;
+constexpr int kEpilogueThreads = 128;
 constexpr int kTmemCols = 512;
 
 // device error word bits (OR-ed; 0 = no error)
@@ -72,6 +97,7 @@ constexpr unsigned kErrMma = 4u;
 constexpr unsigned kErrDequant = 8u;
 constexpr unsigned kErrEpilogue = 16u;
 constexpr unsigned kErrTeardown = 32u;
+constexpr unsigned kErrXStage = 64u;
 
 struct DecodeParams {
   void* c;              // [M, N] row-major, OutT
@@ -93,14 +119,34 @@ __host__ __device__ __forceinline__ int streamk_cta_of(long long u, long long un
   return (int)(((u + 1) * grid + units - 1) / units - 1);
 }
 
+// TMEM column map (512 columns allocated)
+template <int NB>
+struct DecodeTmem {
+  static constexpr int kX = 0;                           // X[b] at b*NB, b = 0, 1
+  static constexpr int kY = 2 * NB;                      // Y (Q4_K), one buffer
+  static constexpr int kM = kY + NB;                     // (dmin*m) operand, 8 columns per slot
+  static constexpr int kA = 128;                         // unit operand slots, 128 columns each
+  static_assert(kM + kSlots * 8 <= kA && kA + kSlots * 128 <= kTmemCols, "TMEM budget");
+};
+
 template <int NB>
 struct DecodeSmem {
-  static constexpr int kXStageBytes = NB * 128;
+  static constexpr int kXChunkBytes = NB * 128;                      // one 64-value activation box
+  static constexpr int kXSlotBytes = kChunksPerUnit * kXChunkBytes;  // one unit of activations
   static constexpr int kWOff = 0;
   static constexpr int kXOff = kWOff + kWStages * kWStageBytes;
-  static constexpr int kBarOff = kXOff + kXStages * kXStageBytes;
-  // barriers: wfull, wempty, xfull, xempty, afull, aempty, accfull[2], accempty[2], final
-  static constexpr int kNumBars = 2 * kWStages + 2 * kXStages + 2 * kAStages + 4 + 1;
+  static constexpr int kSOff = kXOff + kSlots * kXSlotBytes;         // Asum B tiles, one per slot
+  static constexpr int kDOff = kSOff + kSlots * kXChunkBytes;
+  static constexpr int kBarOff = kDOff + kDStages * kTileRows * 4;
+  // barrier slots
+  static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
+  static constexpr int bXFull = bWEmpty + kWStages;        // activations landed (TMA tx)
+  static constexpr int bReady = bXFull + kSlots;           // unit operands + activations ready for the MMA
+  static constexpr int bUDone = bReady + kSlots;           // unit's MMAs complete (commit)
+  static constexpr int bAccEmpty = bUDone + kSlots;        // X[b] read by the epilogue
+  static constexpr int bYEmpty = bAccEmpty + 2;
+  static constexpr int bFinal = bYEmpty + 1;
+  static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
@@ -159,8 +205,31 @@ __device__ __forceinline__ __half2 six_bit_pair_to_h2(uint32_t word, int cpair) 
   return __hsub2(u32_as_h2(v), k1024);
 }
 
-__device__ __forceinline__ void named_bar_sync_dequant() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kDequantThreads) : "memory");
+// dmin * m (exact in fp32) -> (hi, lo) fp16 with hi + lo == dmin * m exactly
+// for normal-range products (hi = fp16_rn(x); x - hi has <= 6 significant bits)
+__device__ __forceinline__ void split_hi_lo(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn(x - __half2float(hi));
+}
+
+__device__ __forceinline__ void named_bar_sync_epilogue() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+}
+
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// packed fp32 pair FMA (sm_100): d = a*b + c
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(r)
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
+        "l"(*reinterpret_cast<unsigned long long*>(&c)));
+  return *reinterpret_cast<float2*>(&r);
 }
 
 template <typename OutT>
@@ -170,6 +239,20 @@ __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_
 template <>
 __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
+// Per-unit schedule facts every role derives the same way.
+struct UnitInfo {
+  int tile, sb;
+  bool seg_first, seg_last;   // first / last unit of this CTA's run within the tile
+};
+__device__ __forceinline__ UnitInfo unit_info(int u, int u0, int u1, int S) {
+  UnitInfo r;
+  r.tile = u / S;
+  r.sb = u - r.tile * S;
+  r.seg_first = (u == u0) || (r.sb == 0);
+  r.seg_last = (u == u1 - 1) || (r.sb == S - 1);
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -177,29 +260,22 @@ template <WFmt FMT, int NB, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                        const __grid_constant__ CUtensorMap tmap_a, const DecodeParams p) {
-  static_assert(NB == 16 || NB == 32 || NB == 64, "batch tile");
+  static_assert(NB == 16 || NB == 32, "batch tile");
   using L = DecodeSmem<NB>;
-  constexpr int HALF = NB / 2;  // batch columns per epilogue group
+  using TM = DecodeTmem<NB>;
+  constexpr bool kQ4K = (FMT == WFmt::Q4K);
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
-  constexpr int kAccCols = 2 * NB;            // X (and Y for Q4_K) per accumulator buffer
-  constexpr int kAOff = 2 * kAccCols;         // operand stages start after 2 accumulators
-  static_assert(kAOff + kAStages * 64 <= kTmemCols, "TMEM budget");
+  // ready[s] arrivals: 8 dequant warps + the activation-stage warp (+ 4 epilogue warps for Q4_K)
+  constexpr uint32_t kReadyCount = kQ4K ? 13u : 9u;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBarOff;
-  auto BAR_WFULL = [&](int s) { return bar0 + 8u * s; };
-  auto BAR_WEMPTY = [&](int s) { return bar0 + 8u * (kWStages + s); };
-  auto BAR_XFULL = [&](int s) { return bar0 + 8u * (2 * kWStages + s); };
-  auto BAR_XEMPTY = [&](int s) { return bar0 + 8u * (2 * kWStages + kXStages + s); };
-  auto BAR_AFULL = [&](int s) { return bar0 + 8u * (2 * kWStages + 2 * kXStages + s); };
-  auto BAR_AEMPTY = [&](int s) { return bar0 + 8u * (2 * kWStages + 2 * kXStages + kAStages + s); };
-  auto BAR_ACCFULL = [&](int b) { return bar0 + 8u * (2 * kWStages + 2 * kXStages + 2 * kAStages + b); };
-  auto BAR_ACCEMPTY = [&](int b) { return bar0 + 8u * (2 * kWStages + 2 * kXStages + 2 * kAStages + 2 + b); };
-  const uint32_t BAR_FINAL = bar0 + 8u * (2 * kWStages + 2 * kXStages + 2 * kAStages + 4);
+  auto BAR = [&](int slot) { return bar0 + 8u * (uint32_t)slot; };
   uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base, [1] last-arriver flag
+  float* dring = reinterpret_cast<float*>(smem + L::kDOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -208,21 +284,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int u1 = streamk_first_unit(blockIdx.x + 1, p.units, gridDim.x);
   const int nunits = u1 - u0;
 
+  // Every role waits with the whole warp; a wait that times out in any lane
+  // counts as a failure for the warp, which then stops issuing work.
+  bool ok = true;
+  int diag_unit = -1;                  // unit being processed, for the failure record
+  auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (!ok) return false;
+    const bool got = mbar_wait(bar, parity);
+    ok = __all_sync(0xffffffffu, got);
+    if (!ok && lane == 0) {
+      // first failure in the grid: warp, unit, barrier slot, parity
+      const unsigned rec = 0x80000000u | ((unsigned)warp << 24) | ((unsigned)(diag_unit & 0xFFF) << 12) |
+                           (((bar - bar0) / 8u) << 1) | parity;
+      atomicCAS(p.error + 1, 0u, rec);
+    }
+    return ok;
+  };
+  // unit i's slot is free once unit i - kSlots has completed its MMAs
+  auto wait_slot_free = [&](int i) -> bool {
+    if (i < kSlots) return ok;
+    return warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1);
+  };
+
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) { mbar_init(BAR_WFULL(s), 1); mbar_init(BAR_WEMPTY(s), 8); }
-    for (int s = 0; s < kXStages; ++s) { mbar_init(BAR_XFULL(s), 1); mbar_init(BAR_XEMPTY(s), 1); }
-    for (int s = 0; s < kAStages; ++s) { mbar_init(BAR_AFULL(s), 4); mbar_init(BAR_AEMPTY(s), 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(BAR_ACCFULL(b), 1); mbar_init(BAR_ACCEMPTY(b), 8); }
-    mbar_init(BAR_FINAL, 1);
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(BAR(L::bWFull + s), 1);
+      mbar_init(BAR(L::bWEmpty + s), kQ4K ? 12 : 8);   // dequant warps (+ epilogue warps reading scales)
+    }
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(BAR(L::bXFull + s), 1);
+      mbar_init(BAR(L::bReady + s), kReadyCount);
+      mbar_init(BAR(L::bUDone + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) mbar_init(BAR(L::bAccEmpty + b), 4);
+    mbar_init(BAR(L::bYEmpty), 4);
+    mbar_init(BAR(L::bFinal), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmap_w);
     if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
     tma_prefetch_desc(&tmap_a);
   }
-  if (warp == 1) {
+  if (warp == kWarpXProducer) {
     tmem_alloc(sbase + L::kMiscOff, kTmemCols);
     tmem_relinquish();
   }
+  __syncwarp();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -231,278 +337,183 @@ __global__ void __launch_bounds__(kThreads, 1)
   // retire and begin streaming their weights before our tail completes.
   if (threadIdx.x == 0) pdl_launch_dependents();
 
-  if (warp == 0) {
+  if (warp == kWarpWProducer) {
     // ---------------- weight producer ----------------
-    if (lane == 0) {
-      bool ok = true;
-      int issued = 0;
-      for (int i = 0; i < nunits; ++i) {
-        const int s = i % kWStages;
-        if (!mbar_wait(BAR_WEMPTY(s), ((i / kWStages) & 1) ^ 1)) { ok = false; break; }
-        const int u = u0 + i;
-        const int tile = u / S, sb = u - tile * S;
-        const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
-        mbar_arrive_expect_tx(BAR_WFULL(s), kWStageBytes);
-        if constexpr (FMT == WFmt::Q4K) {
-          tma_load_2d(dst, &tmap_w, sb * kQ4KBlockBytes, tile * kTileRows, BAR_WFULL(s), kPolicyEvictFirst);
-        } else {
-          tma_load_2d(dst, &tmap_w, sb * 128, tile * kTileRows, BAR_WFULL(s), kPolicyEvictFirst);
-          tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, sb * 8, tile * kTileRows, BAR_WFULL(s), kPolicyEvictFirst);
-        }
-        issued = i + 1;
-      }
-      if (!ok) atomicOr(p.error, kErrWeightProducer);
-      // never leave the CTA with copies in flight
-      for (int i = issued > kWStages ? issued - kWStages : 0; i < issued; ++i)
-        if (!mbar_wait(BAR_WFULL(i % kWStages), (i / kWStages) & 1)) atomicOr(p.error, kErrTeardown);
-    }
-  } else if (warp == 2) {
-    // ---------------- activation producer ----------------
-    if (lane == 0) {
-      pdl_wait_prerequisites();  // activations may be the previous kernel's output
-      bool ok = true;
-      int issued = 0;
-      const int total = nunits * kChunksPerUnit;
-      for (int j = 0; j < total; ++j) {
-        const int s = j % kXStages;
-        if (!mbar_wait(BAR_XEMPTY(s), ((j / kXStages) & 1) ^ 1)) { ok = false; break; }
-        const int u = u0 + j / kChunksPerUnit;
-        const int sb = u % S;
-        mbar_arrive_expect_tx(BAR_XFULL(s), L::kXStageBytes);
-        tma_load_2d(sbase + L::kXOff + s * L::kXStageBytes, &tmap_a, sb * kUnitK + (j % kChunksPerUnit) * kChunkK, 0,
-                    BAR_XFULL(s), kPolicyEvictLast);
-        issued = j + 1;
-      }
-      if (!ok) atomicOr(p.error, kErrActProducer);
-      for (int j = issued > kXStages ? issued - kXStages : 0; j < issued; ++j)
-        if (!mbar_wait(BAR_XFULL(j % kXStages), (j / kXStages) & 1)) atomicOr(p.error, kErrTeardown);
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      bool ok = true;
-      int accq = 0;        // accumulator buffers handed out so far
-      int prev_tile = -1;
-      int acc = 0;
-      for (int i = 0; i < nunits && ok; ++i) {
-        const int u = u0 + i;
-        const int tile = u / S;
-        const bool fresh = (FMT == WFmt::Q4K) || (tile != prev_tile);
-        const bool closes = (FMT == WFmt::Q4K) || (i == nunits - 1) || ((u + 1) / S != tile);
-        prev_tile = tile;
-        if (fresh) {
-          acc = accq & 1;
-          if (!mbar_wait(BAR_ACCEMPTY(acc), ((accq >> 1) & 1) ^ 1)) { ok = false; break; }
-          tc_fence_after();
-        }
-        const uint32_t d_x = tmem + acc * kAccCols;
-        const uint32_t d_y = d_x + NB;
-        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
-          const int j = i * kChunksPerUnit + cc;
-          const int as = j % kAStages, xs = j % kXStages;
-          if (!mbar_wait(BAR_AFULL(as), (j / kAStages) & 1)) { ok = false; break; }
-          if (!mbar_wait(BAR_XFULL(xs), (j / kXStages) & 1)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_t = tmem + kAOff + as * 64;
-          const uint32_t b_s = sbase + L::kXOff + xs * L::kXStageBytes;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const uint64_t bdesc = make_sdesc_sw128(b_s + 32 * t);
-            const uint32_t accum = (fresh && cc == 0 && t == 0) ? 0u : 1u;
-            mma_f16_ts(d_x, a_t + 8 * t, bdesc, kIdesc, accum);
-            if constexpr (FMT == WFmt::Q4K) mma_f16_ts(d_y, a_t + 32 + 8 * t, bdesc, kIdesc, accum);
-          }
-          tc_commit(BAR_AEMPTY(as));
-          tc_commit(BAR_XEMPTY(xs));
-        }
-        if (!ok) break;
-        if (closes) {
-          tc_commit(BAR_ACCFULL(acc));
-          ++accq;
-        }
-      }
-      if (!ok) atomicOr(p.error, kErrMma);
-      tc_commit(BAR_FINAL);  // fires once every MMA issued above has completed
-    }
-  } else if (warp >= kFirstDequantWarp) {
-    // ---------------- dequant + epilogue ----------------
-    const int q = warp & 3;                          // TMEM lane quarter this warp may touch
-    const int g = (warp - kFirstDequantWarp) >> 2;   // group: chunks {g, g+2}, batch half g
-    const int r = q * 32 + lane;                     // weight row within the tile
-    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    bool ok = true;
-    float accv[HALF];
-#pragma unroll
-    for (int t = 0; t < HALF; ++t) accv[t] = 0.f;
-    float pend_d = 0.f, pend_dmin = 0.f;  // Q4_K scales of the unit awaiting its epilogue
-    int accq = 0;                          // Q4_0: accumulator buffers consumed
-
-    auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
-      if (!ok) return false;
-      const bool got = mbar_wait(bar, parity);
-      ok = __all_sync(0xffffffffu, got);
-      return ok;
-    };
-
-    // write this thread's finished segment (tile) result
-    auto flush = [&](int tile) {
-      pdl_wait_prerequisites();  // C / workspace may still be in use by the previous kernel
-      const int tfirst = tile * S, tlast = tile * S + S - 1;
-      const int first_cta = streamk_cta_of(tfirst, p.units, gridDim.x);
-      const int last_cta = streamk_cta_of(tlast, p.units, gridDim.x);
-      const int n = tile * kTileRows + r;
-      OutT* C = reinterpret_cast<OutT*>(p.c);
-      if (first_cta == last_cta) {
-        if (ok && n < p.N) {
-#pragma unroll
-          for (int t = 0; t < HALF; ++t) {
-            const int b = g * HALF + t;
-            if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(accv[t]);
-          }
-        }
-        return;
-      }
-      const int slot = (int)blockIdx.x - first_cta;
-      const int ncontrib = last_cta - first_cta + 1;
-      float* mine = p.partials + (((size_t)tile * p.max_slots + slot) * kTileRows + r) * NB + g * HALF;
-#pragma unroll
-      for (int t = 0; t < HALF; t += 4)
-        *reinterpret_cast<float4*>(mine + t) = make_float4(accv[t], accv[t + 1], accv[t + 2], accv[t + 3]);
-      __threadfence();
-      named_bar_sync_dequant();
-      if (threadIdx.x == kFirstDequantWarp * 32) {
-        const unsigned old = atomicAdd(&p.counters[tile], 1u);
-        misc[1] = (old == (unsigned)(ncontrib - 1)) ? 1u : 0u;
-      }
-      named_bar_sync_dequant();
-      if (misc[1] != 0u) {
-        __threadfence();
-        float sum[HALF];
-#pragma unroll
-        for (int t = 0; t < HALF; ++t) sum[t] = 0.f;
-        for (int s = 0; s < ncontrib; ++s) {
-          if (s == slot) {
-#pragma unroll
-            for (int t = 0; t < HALF; ++t) sum[t] += accv[t];
-          } else {
-            const float* other = p.partials + (((size_t)tile * p.max_slots + s) * kTileRows + r) * NB + g * HALF;
-#pragma unroll
-            for (int t = 0; t < HALF; t += 4) {
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(other + t));
-              sum[t] += v.x; sum[t + 1] += v.y; sum[t + 2] += v.z; sum[t + 3] += v.w;
-            }
-          }
-        }
-        if (ok && n < p.N) {
-#pragma unroll
-          for (int t = 0; t < HALF; ++t) {
-            const int b = g * HALF + t;
-            if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(sum[t]);
-          }
-        }
-        if (threadIdx.x == kFirstDequantWarp * 32) p.counters[tile] = 0u;  // ready for the next call
-      }
-    };
-
-    // epilogue for unit i (runs one unit behind the dequant)
-    auto finish = [&](int i) {
-      const int u = u0 + i;
-      const int tile = u / S;
-      const bool closes = (i == nunits - 1) || ((u + 1) / S != tile);
-      if constexpr (FMT == WFmt::Q4K) {
-        const int acc = i & 1;
-        if (warp_wait(BAR_ACCFULL(acc), (i >> 1) & 1)) {
-          tc_fence_after();
-          const uint32_t cx = tmem + lane_off + acc * kAccCols + g * HALF;
-          constexpr int CH = HALF < 16 ? HALF : 16;
-#pragma unroll
-          for (int c0 = 0; c0 < HALF; c0 += CH) {
-            uint32_t xr[CH], yr[CH];
-            tmem_ld_cols<CH>(cx + c0, xr);
-            tmem_ld_cols<CH>(cx + NB + c0, yr);
-            tc_wait_ld();
-#pragma unroll
-            for (int t = 0; t < CH; ++t) {
-              accv[c0 + t] = fmaf(pend_d, __uint_as_float(xr[t]), accv[c0 + t]);
-              accv[c0 + t] = fmaf(-pend_dmin, __uint_as_float(yr[t]), accv[c0 + t]);
-            }
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(BAR_ACCEMPTY(acc));
-        }
-      } else {
-        if (closes) {
-          const int acc = accq & 1;
-          if (warp_wait(BAR_ACCFULL(acc), (accq >> 1) & 1)) {
-            tc_fence_after();
-            const uint32_t cx = tmem + lane_off + acc * kAccCols + g * HALF;
-            constexpr int CH = HALF < 16 ? HALF : 16;
-#pragma unroll
-            for (int c0 = 0; c0 < HALF; c0 += CH) {
-              uint32_t xr[CH];
-              tmem_ld_cols<CH>(cx + c0, xr);
-              tc_wait_ld();
-#pragma unroll
-              for (int t = 0; t < CH; ++t) accv[c0 + t] = __uint_as_float(xr[t]);
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(BAR_ACCEMPTY(acc));
-          }
-          ++accq;
-        }
-      }
-      if (closes) {
-        flush(tile);
-#pragma unroll
-        for (int t = 0; t < HALF; ++t) accv[t] = 0.f;
-      }
-    };
-
+    int issued = 0;
     for (int i = 0; i < nunits; ++i) {
-      const int ws = i % kWStages;
-      const bool have_w = warp_wait(BAR_WFULL(ws), (i / kWStages) & 1);
-      const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
-      float cur_d = 0.f, cur_dmin = 0.f;
-      uint32_t sc_lo = 0, sc_hi = 0, m_lo = 0, m_hi = 0;
-      if constexpr (FMT == WFmt::Q4K) {
-        if (have_w) {
-          const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
-          cur_d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
-          cur_dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-          sc_lo = hdr.y & 0x3F3F3F3Fu;
-          m_lo = hdr.z & 0x3F3F3F3Fu;
-          sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-          m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+      const int s = i % kWStages;
+      if (!warp_wait(BAR(L::bWEmpty + s), ((i / kWStages) & 1) ^ 1)) break;
+      const int u = u0 + i;
+      const int tile = u / S, sb = u - tile * S;
+      const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
+        if constexpr (kQ4K) {
+          tma_load_2d(dst, &tmap_w, sb * kQ4KBlockBytes, tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+        } else {
+          tma_load_2d(dst, &tmap_w, sb * 128, tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+          tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, sb * 8, tile * kTileRows, BAR(L::bWFull + s),
+                      kPolicyEvictFirst);
         }
+      }
+      __syncwarp();
+      issued = i + 1;
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrWeightProducer);
+    // never leave the CTA with copies in flight
+    ok = true;
+    for (int i = issued > kWStages ? issued - kWStages : 0; i < issued; ++i)
+      if (!warp_wait(BAR(L::bWFull + i % kWStages), (i / kWStages) & 1)) {
+        if (lane == 0) atomicOr(p.error, kErrTeardown);
+        break;
+      }
+  } else if (warp == kWarpXProducer) {
+    // ---------------- activation producer ----------------
+    pdl_wait_prerequisites();  // activations may be the previous kernel's output
+    int issued = 0;
+    for (int i = 0; i < nunits; ++i) {
+      if (!wait_slot_free(i)) break;
+      const int s = i % kSlots;
+      const int sb = (u0 + i) % S;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(BAR(L::bXFull + s), L::kXSlotBytes);
+#pragma unroll
+        for (int cc = 0; cc < kChunksPerUnit; ++cc)
+          tma_load_2d(sbase + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes, &tmap_a,
+                      sb * kUnitK + cc * kChunkK, 0, BAR(L::bXFull + s), kPolicyEvictLast);
+      }
+      __syncwarp();
+      issued = i + 1;
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrActProducer);
+    ok = true;
+    for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
+      if (!warp_wait(BAR(L::bXFull + i % kSlots), (i / kSlots) & 1)) {
+        if (lane == 0) atomicOr(p.error, kErrTeardown);
+        break;
+      }
+  } else if (warp == kWarpXStage) {
+    // ---------------- activation stage (+ Q4_K sub-block sums) ----------------
+    const int b = lane;                  // batch row (lanes >= NB idle)
+    for (int i = 0; i < nunits; ++i) {
+      diag_unit = i;
+      const int s = i % kSlots;
+      if (!warp_wait(BAR(L::bXFull + s), (i / kSlots) & 1)) break;
+      if constexpr (kQ4K) {
+        // Asum[b][j], j = 0..7: fp16 pairwise sums of 32 activations. The B
+        // tile row b holds k 0..7 = Asum[b][0..7] and k 8..15 = the same again.
+        uint32_t sums[4];
+#pragma unroll
+        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+          __half s2[2] = {__float2half(0.f), __float2half(0.f)};
+          if (b < NB) {
+            const uint8_t* row =
+                smem + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes + (b >> 3) * 1024 + (b & 7) * 128;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {   // sub-block 2cc+h = 16-byte chunks 4h..4h+3
+              uint4 v[4];
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                v[c] = *reinterpret_cast<const uint4*>(row + ((((uint32_t)(4 * h + c)) ^ (uint32_t)(b & 7)) << 4));
+              __half2 a0 = __hadd2(u32_as_h2(v[0].x), u32_as_h2(v[0].y));
+              __half2 a1 = __hadd2(u32_as_h2(v[0].z), u32_as_h2(v[0].w));
+              __half2 a2 = __hadd2(u32_as_h2(v[1].x), u32_as_h2(v[1].y));
+              __half2 a3 = __hadd2(u32_as_h2(v[1].z), u32_as_h2(v[1].w));
+              __half2 a4 = __hadd2(u32_as_h2(v[2].x), u32_as_h2(v[2].y));
+              __half2 a5 = __hadd2(u32_as_h2(v[2].z), u32_as_h2(v[2].w));
+              __half2 a6 = __hadd2(u32_as_h2(v[3].x), u32_as_h2(v[3].y));
+              __half2 a7 = __hadd2(u32_as_h2(v[3].z), u32_as_h2(v[3].w));
+              a0 = __hadd2(a0, a1); a2 = __hadd2(a2, a3); a4 = __hadd2(a4, a5); a6 = __hadd2(a6, a7);
+              a0 = __hadd2(a0, a2); a4 = __hadd2(a4, a6);
+              a0 = __hadd2(a0, a4);
+              s2[h] = __hadd(__low2half(a0), __high2half(a0));
+            }
+          }
+          sums[cc] = h2_as_u32(__halves2half2(s2[0], s2[1]));
+        }
+        if (b < NB) {
+          uint8_t* row = smem + L::kSOff + s * L::kXChunkBytes + (b >> 3) * 1024 + (b & 7) * 128;
+          const uint4 v = make_uint4(sums[0], sums[1], sums[2], sums[3]);
+          *reinterpret_cast<uint4*>(row + ((0u ^ (uint32_t)(b & 7)) << 4)) = v;
+          *reinterpret_cast<uint4*>(row + ((1u ^ (uint32_t)(b & 7)) << 4)) = v;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(L::bReady + s));
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrXStage);
+  } else if (warp == kWarpMma) {
+    // ---------------- MMA issuer (converged warp, one elected thread issues) ----------------
+    int yuses = 0;         // Q4_K segments started (Y buffer uses)
+    for (int i = 0; i < nunits; ++i) {
+      diag_unit = i;
+      const UnitInfo ui = unit_info(u0 + i, u0, u1, S);
+      const int s = i % kSlots;
+      // every unit accumulates into X[i & 1]; the epilogue folds it into
+      // registers, so the MMA is never more than two units ahead of it
+      if (!warp_wait(BAR(L::bAccEmpty + (i & 1)), ((i >> 1) & 1) ^ 1)) break;
+      if (kQ4K && ui.seg_first) {
+        if (!warp_wait(BAR(L::bYEmpty), (yuses & 1) ^ 1)) break;
+        ++yuses;
+      }
+      if (!warp_wait(BAR(L::bReady + s), (i / kSlots) & 1)) break;
+      tc_fence_after();
+      const uint32_t d_x = tmem + TM::kX + (uint32_t)((i & 1) * NB);
+      const uint32_t a_t = tmem + TM::kA + s * 128;
+      const uint32_t b_s = sbase + L::kXOff + s * L::kXSlotBytes;
+      if (elect_one()) {
+#pragma unroll
+        for (int cc = 0; cc < kChunksPerUnit; ++cc)
+#pragma unroll
+          for (int t = 0; t < 4; ++t)
+            mma_f16_ts(d_x, a_t + cc * 32 + 8 * t, make_sdesc_sw128(b_s + cc * L::kXChunkBytes + 32 * t), kIdesc,
+                       (cc == 0 && t == 0) ? 0u : 1u);
+        if constexpr (kQ4K)
+          mma_f16_ts(tmem + TM::kY, tmem + TM::kM + s * 8, make_sdesc_sw128(sbase + L::kSOff + s * L::kXChunkBytes),
+                     kIdesc, ui.seg_first ? 0u : 1u);
+        tc_commit(BAR(L::bUDone + s));  // frees slot s; publishes X (and Y) for this unit
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrMma);
+    if (elect_one()) tc_commit(BAR(L::bFinal));  // fires once every MMA issued above has completed
+    __syncwarp();
+  } else if (warp < kWarpEpilogue0) {
+    // ---------------- dequant ----------------
+    const int q = warp & 3;                        // TMEM lane quarter this warp may touch
+    const int g = (warp - kWarpDequant0) >> 2;     // group: chunks {g, g+2}
+    const int r = q * 32 + lane;                   // weight row within the tile
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int i = 0; i < nunits; ++i) {
+      diag_unit = i;
+      const int ws = i % kWStages;
+      if (!warp_wait(BAR(L::bWFull + ws), (i / kWStages) & 1)) break;
+      if (!wait_slot_free(i)) break;
+      tc_fence_after();
+      const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
+      const uint32_t a_slot = tmem + lane_off + TM::kA + (i % kSlots) * 128;
+      uint32_t sc_lo = 0, sc_hi = 0;
+      if constexpr (kQ4K) {
+        const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
+        sc_lo = hdr.y & 0x3F3F3F3Fu;
+        sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
       }
 #pragma unroll 1
       for (int k2 = 0; k2 < 2; ++k2) {
         const int cc = g + 2 * k2;
-        const int j = i * kChunksPerUnit + cc;
-        const int as = j % kAStages;
-        if (!have_w || !warp_wait(BAR_AEMPTY(as), ((j / kAStages) & 1) ^ 1)) continue;
-        tc_fence_after();
         uint32_t P[32];
-        const uint32_t a_t = tmem + lane_off + kAOff + as * 64;
-        if constexpr (FMT == WFmt::Q4K) {
+        if constexpr (kQ4K) {
           const uint8_t* qs = stage + r * kQ4KBlockBytes + 16 + cc * 32;
           const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
           const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-          const uint32_t scw = (cc < 2) ? sc_lo : sc_hi;
-          const uint32_t mw = (cc < 2) ? m_lo : m_hi;
-          const __half2 S2 = six_bit_pair_to_h2(scw, cc & 1);  // {sc[2cc], sc[2cc+1]}
-          const __half2 M2 = six_bit_pair_to_h2(mw, cc & 1);   // {m[2cc],  m[2cc+1]}
+          const __half2 S2 = six_bit_pair_to_h2(cc < 2 ? sc_lo : sc_hi, cc & 1);  // {sc[2cc], sc[2cc+1]}
           const __half2 mlo = __low2half2(S2);
           const __half2 alo = __hmul2(mlo, __float2half2_rn(-1024.f));
           const __half2 shi = __high2half2(S2);
           const __half2 mhi = __hmul2(shi, __float2half2_rn(0.0625f));
           const __half2 ahi = __hmul2(shi, __float2half2_rn(-64.f));
           dequant_q4k_chunk(q0, q1, mlo, alo, mhi, ahi, P);
-          tmem_st_x32(a_t, P);
-          tmem_st_x16_bcast(a_t + 32, h2_as_u32(__low2half2(M2)));
-          tmem_st_x16_bcast(a_t + 48, h2_as_u32(__high2half2(M2)));
         } else {
           const uint8_t* wrow = stage + r * 128;
           const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
@@ -512,28 +523,185 @@ __global__ void __launch_bounds__(kThreads, 1)
           const __half2 d01 = u32_as_h2(dd);
           dequant_q4_0_block(b0, __low2half2(d01), P);
           dequant_q4_0_block(b1, __high2half2(d01), P + 16);
-          tmem_st_x32(a_t, P);
         }
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(BAR_AFULL(as));
+        tmem_st_x32(a_slot + cc * 32, P);
       }
+      tc_wait_st();
+      tc_fence_before();
       __syncwarp();
-      if (have_w && lane == 0) mbar_arrive(BAR_WEMPTY(ws));
-      if (i > 0) finish(i - 1);
-      pend_d = cur_d;
-      pend_dmin = cur_dmin;
+      if (lane == 0) {
+        mbar_arrive(BAR(L::bReady + i % kSlots));
+        mbar_arrive(BAR(L::bWEmpty + ws));
+      }
     }
-    if (nunits > 0) finish(nunits - 1);
     if (!ok && lane == 0) atomicOr(p.error, kErrDequant);
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    float acc[NB];
+#pragma unroll
+    for (int t = 0; t < NB; ++t) acc[t] = 0.f;
+
+    // Q4_K: read unit i's scales for this row while its weight stage is
+    // resident; keep d for the fold and store dmin*m (split hi + lo) as the
+    // min-term operand in TMEM slot i % kSlots.
+    auto prep = [&](int i) {
+      const int ws = i % kWStages;
+      if (!warp_wait(BAR(L::bWFull + ws), (i / kWStages) & 1)) return;
+      const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::kWOff + ws * kWStageBytes + r * kQ4KBlockBytes);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(L::bWEmpty + ws));
+      dring[(i % kDStages) * kTileRows + r] = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+      const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+      const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+      const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+      uint32_t mv[8];
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        const uint32_t word = jp < 2 ? m_lo : m_hi;
+        const int sh = 16 * (jp & 1);
+        __half h0, l0, h1, l1;
+        split_hi_lo(dmin * (float)((word >> sh) & 0xFFu), h0, l0);
+        split_hi_lo(dmin * (float)((word >> (sh + 8)) & 0xFFu), h1, l1);
+        mv[jp] = h2_as_u32(__halves2half2(h0, h1));
+        mv[4 + jp] = h2_as_u32(__halves2half2(l0, l1));
+      }
+      if (!wait_slot_free(i)) return;
+      tc_fence_after();
+      tmem_st_x8(tmem + lane_off + TM::kM + (i % kSlots) * 8, mv);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(L::bReady + i % kSlots));
+    };
+
+    // acc += scale * X[buf]; the unit's MMAs (udone) must have completed
+    auto fold_x = [&](int i, int buf, float scale) {
+      if (!warp_wait(BAR(L::bUDone + i % kSlots), (i / kSlots) & 1)) return;
+      tc_fence_after();
+      const float2 sc2 = make_float2(scale, scale);
+#pragma unroll
+      for (int h = 0; h < NB; h += 16) {
+        uint32_t x[16];
+        tmem_ld_x16(tmem + lane_off + TM::kX + (uint32_t)(buf * NB + h), x);
+        tc_wait_ld();
+#pragma unroll
+        for (int t = 0; t < 16; t += 2) {
+          const float2 v = ffma2(sc2, make_float2(__uint_as_float(x[t]), __uint_as_float(x[t + 1])),
+                                 make_float2(acc[h + t], acc[h + t + 1]));
+          acc[h + t] = v.x;
+          acc[h + t + 1] = v.y;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
+    };
+
+    // write this thread's finished segment (tile) result
+    auto flush = [&](int tile) {
+      pdl_wait_prerequisites();  // C / workspace may still be in use by the previous kernel
+      const int first_cta = streamk_cta_of((long long)tile * S, p.units, gridDim.x);
+      const int last_cta = streamk_cta_of((long long)tile * S + S - 1, p.units, gridDim.x);
+      const int n = tile * kTileRows + r;
+      OutT* C = reinterpret_cast<OutT*>(p.c);
+      if (first_cta == last_cta) {
+        if (ok && n < p.N) {
+#pragma unroll
+          for (int t = 0; t < NB; ++t)
+            if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
+        }
+        return;
+      }
+      const int slot = (int)blockIdx.x - first_cta;
+      const int ncontrib = last_cta - first_cta + 1;
+      float* base = p.partials + (size_t)tile * p.max_slots * kTileRows * NB;
+      float* mine = base + ((size_t)slot * kTileRows + r) * NB;
+#pragma unroll
+      for (int t = 0; t < NB; t += 4) *reinterpret_cast<float4*>(mine + t) = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+      named_bar_sync_epilogue();
+      if (threadIdx.x == kWarpEpilogue0 * 32) {
+        // release: this CTA's partial stores (ordered by the barrier) become
+        // visible before the counter moves; acquire: the last arriver sees all
+        const unsigned old = atom_add_acq_rel_gpu(&p.counters[tile], 1u);
+        misc[1] = (old == (unsigned)(ncontrib - 1)) ? 1u : 0u;
+      }
+      named_bar_sync_epilogue();
+      if (misc[1] != 0u) {
+        float sum[NB];
+#pragma unroll
+        for (int t = 0; t < NB; ++t) sum[t] = 0.f;
+        // every slot, this CTA's own included, is summed from memory in slot
+        // order, so the result does not depend on which CTA arrived last
+        for (int s = 0; s < ncontrib; ++s) {
+          const float4* part = reinterpret_cast<const float4*>(base + ((size_t)s * kTileRows + r) * NB);
+#pragma unroll
+          for (int h = 0; h < NB / 4; h += 4) {
+            float4 v[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) v[t] = __ldcg(part + h + t);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int o = 4 * (h + t);
+              sum[o] += v[t].x; sum[o + 1] += v[t].y; sum[o + 2] += v[t].z; sum[o + 3] += v[t].w;
+            }
+          }
+        }
+        if (ok && n < p.N) {
+#pragma unroll
+          for (int t = 0; t < NB; ++t)
+            if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(sum[t]);
+        }
+        if (threadIdx.x == kWarpEpilogue0 * 32) p.counters[tile] = 0u;  // ready for the next call
+      }
+    };
+
+    if constexpr (kQ4K) {
+      for (int i = 0; i < nunits && i < kPrepAhead; ++i) prep(i);
+    }
+    for (int i = 0; i < nunits; ++i) {
+      diag_unit = i;
+      const UnitInfo ui = unit_info(u0 + i, u0, u1, S);
+      // Every unit is folded, in order: a waiter on a parity barrier must not
+      // skip phases (a wait for phase n+1 posted before phase n completed
+      // would see the stale parity as complete).
+      if constexpr (kQ4K) {
+        if (i + kPrepAhead < nunits) prep(i + kPrepAhead);
+        fold_x(i, i & 1, dring[(i % kDStages) * kTileRows + r]);
+        if (ui.seg_last && ok) {
+          // Y of this segment is complete: its last MMA was committed with unit i
+#pragma unroll
+          for (int h = 0; h < NB; h += 16) {
+            uint32_t y[16];
+            tmem_ld_x16(tmem + lane_off + TM::kY + h, y);
+            tc_wait_ld();
+#pragma unroll
+            for (int t = 0; t < 16; ++t) acc[h + t] -= __uint_as_float(y[t]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(BAR(L::bYEmpty));
+        }
+      } else {
+        fold_x(i, i & 1, 1.0f);
+      }
+      if (ui.seg_last) {
+        flush(ui.tile);
+#pragma unroll
+        for (int t = 0; t < NB; ++t) acc[t] = 0.f;
+      }
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrEpilogue);
   }
 
   // ---------------- teardown ----------------
+  __syncwarp();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kWarpXProducer) {
     bool done = true;
-    if (lane == 0) done = mbar_wait(BAR_FINAL, 0);
+    if (lane == 0) done = mbar_wait(BAR(L::bFinal), 0);
     done = __shfl_sync(0xffffffffu, done ? 1 : 0, 0) != 0;
     if (!done && lane == 0) atomicOr(p.error, kErrTeardown);
     tc_fence_after();

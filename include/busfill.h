@@ -103,6 +103,18 @@ BUSFILL_API int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N,
  * (kernels/busfill_v1a.cu:155-158 only prints launch/sync strings). */
 BUSFILL_API int busfill_stream_status(void* stream);
 
+/* As busfill_stream_status, and also stores the device error word (0 when
+ * clean) in *bits if bits is not NULL: one bit per kernel role whose bounded
+ * wait expired (1 weight producer, 2 activation producer, 4 MMA issuer,
+ * 8 dequant, 16 epilogue, 32 teardown, 64 activation stage). */
+BUSFILL_API int busfill_stream_status_ex(void* stream, unsigned* bits);
+
+/* Detail word of the first bounded wait that expired in the last failing
+ * call seen by busfill_stream_status_ex (0 if none): bit 31 set, bits 24-30
+ * the warp index, bits 12-23 the unit index within that CTA's range, bits
+ * 1-11 the barrier slot, bit 0 the awaited phase parity. For diagnostics. */
+BUSFILL_API unsigned busfill_last_failure_detail(void);
+
 /* Human-readable text for a busfill_status value. */
 BUSFILL_API const char* busfill_status_string(int status);
 

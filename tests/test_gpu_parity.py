@@ -133,6 +133,8 @@ SHAPES = [
     (33, 256, 512), (48, 130, 256), (64, 512, 1536), (65, 256, 512), (130, 384, 768),
     (1, 128, 16384),   # one tile split over 64 CTAs (deep split-K fix-up)
     (8, 256, 8192),
+    (5, 3840, 5120),   # ~4 units per CTA: operand-slot reuse, two segments per CTA
+    (2, 1024, 40960),  # ~9 units per CTA, tiles split over ~18 CTAs
 ]
 
 
