@@ -31,7 +31,7 @@ _LIB = None
 STATUS = {
     0: "BUSFILL_OK", -1: "BUSFILL_ERR_INVALID_ARG", -2: "BUSFILL_ERR_SHAPE", -3: "BUSFILL_ERR_ALIGNMENT",
     -4: "BUSFILL_ERR_UNSUPPORTED_DEVICE", -5: "BUSFILL_ERR_LAUNCH", -6: "BUSFILL_ERR_ALLOC",
-    -7: "BUSFILL_ERR_DEVICE_TIMEOUT", -8: "BUSFILL_ERR_CUDA",
+    -7: "BUSFILL_ERR_DEVICE_TIMEOUT", -8: "BUSFILL_ERR_CUDA", -9: "BUSFILL_ERR_SCRATCH_LIMIT",
 }
 
 
@@ -60,6 +60,7 @@ _I = ctypes.c_int
 _SIGS = {
     "busfill_gemm_q4_0": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
     "busfill_dequant_q4_0_ggml": [_P, _P, _I, _I, _P],
@@ -170,6 +171,22 @@ def gemm_q4k(blocks, a, out=None, stream=None):
         out = torch.empty((m, n), dtype=torch.float16, device=a.device)
     _need(out, torch.float16, "out")
     _check(_lib().busfill_gemm_q4k(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)), "busfill_gemm_q4k")
+    return out
+
+
+def gemm_q4k_noalloc(blocks, a, out, stream=None):
+    """gemm_q4k through busfill_gemm_q4k_noalloc: the library allocates no
+    device memory (its split-K scratch is a fixed 8 MiB array in the library
+    image), so `out` must be given. Calls whose kernels overlap on the GPU
+    share that array and race."""
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks"); _need(a, torch.float16, "a"); _need(out, torch.float16, "out")
+    m, k = a.shape
+    n = blocks.shape[0]
+    if k % 256 or blocks.shape[1] != k // 256 * 144 or tuple(out.shape) != (m, n):
+        raise ValueError(f"shape mismatch: blocks {tuple(blocks.shape)}, a {tuple(a.shape)}, out {tuple(out.shape)}")
+    _check(_lib().busfill_gemm_q4k_noalloc(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
+           "busfill_gemm_q4k_noalloc")
     return out
 
 

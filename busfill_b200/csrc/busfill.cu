@@ -18,6 +18,14 @@
 
 using namespace busfill;
 
+// Scratch of busfill_gemm_q4k_noalloc: [error + detail words | split-K tile
+// counters | split-K partial sums], 8 MiB on every GPU that loads this
+// library, held until the process exits. Host code must not use this name as
+// a pointer: in host code it is only a stand-in for the device array, so the
+// device address is looked up with cudaGetSymbolAddress (static_scratch()).
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
 namespace {
 
 constexpr int kVersion = 100;  // 0.1.0
@@ -258,6 +266,98 @@ int grid_for(long long work, int sm_count) {
   return (int)std::max<long long>(1, std::min<long long>(g, (long long)sm_count * 8));
 }
 
+// ---------------------------------------------------------------------------
+// statically allocated scratch (busfill_gemm_q4k_noalloc)
+// ---------------------------------------------------------------------------
+constexpr size_t kStaticCountersOffset = 256;
+constexpr size_t kStaticMaxTiles = 2048;  // N <= 262144
+constexpr size_t kStaticPartialsOffset = kStaticCountersOffset + kStaticMaxTiles * sizeof(unsigned);
+constexpr size_t kStaticPartialsBytes = kStaticScratchBytes - kStaticPartialsOffset;
+static_assert(kStaticPartialsOffset % 256 == 0, "partials must stay 256-byte aligned");
+
+constexpr int kMaxDevices = 64;
+uint8_t* g_static_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on `dev`, which must be the current
+// device. Looked up once per device; a failed lookup is retried next call.
+int static_scratch(int dev, uint8_t** out) {
+  if (dev < 0 || dev >= kMaxDevices) return BUSFILL_ERR_UNSUPPORTED_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) {
+      cudaGetLastError();
+      return BUSFILL_ERR_CUDA;
+    }
+    g_static_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_static_ptr[dev];
+  return BUSFILL_OK;
+}
+
+int gemm_q4k_static(const uint8_t* w, const uint16_t* a, uint16_t* c, int M, int N, int K, cudaStream_t s) {
+  if (!w || !a || !c) return BUSFILL_ERR_INVALID_ARG;
+  if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(w) || !aligned16(a)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev = 0;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+
+  const int S = K / kUnitK;
+  const long long T64 = ((long long)N + kTileRows - 1) / kTileRows;
+  if (T64 > (long long)kStaticMaxTiles) return BUSFILL_ERR_SCRATCH_LIMIT;
+  const int T = (int)T64;
+  const long long U64 = T64 * S;
+  if (U64 > (1LL << 30)) return BUSFILL_ERR_SHAPE;
+  const int U = (int)U64;
+  const int grid = std::min(U, di.sm_count);
+  const int slots = max_contributors(T, S, U, grid);
+  const int nb_max = M <= 16 ? 16 : 32;
+  if ((size_t)T * slots * kTileRows * nb_max * sizeof(float) > kStaticPartialsBytes) return BUSFILL_ERR_SCRATCH_LIMIT;
+
+  uint8_t* scratch = nullptr;
+  st = static_scratch(dev, &scratch);
+  if (st != BUSFILL_OK) return st;
+
+  CUtensorMap tw, ta;
+  const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
+  if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return BUSFILL_ERR_CUDA;
+
+  // the error words and the counters must start at zero; a previous call that
+  // gave up part way may have left them set
+  if (cudaMemsetAsync(scratch, 0, kStaticCountersOffset + (size_t)T * sizeof(unsigned), s) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  for (int m0 = 0; m0 < M; m0 += 32) {
+    const int mc = std::min(32, M - m0);
+    const int nb = mc <= 16 ? 16 : 32;
+    const uint16_t* a_chunk = a + (size_t)m0 * K;
+    if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_chunk, (uint64_t)K, (uint64_t)mc, (uint64_t)K * 2,
+                      kChunkK, (uint32_t)nb, CU_TENSOR_MAP_SWIZZLE_128B))
+      return BUSFILL_ERR_CUDA;
+    DecodeParams p;
+    p.c = reinterpret_cast<__half*>(c) + (size_t)m0 * N;
+    p.partials = reinterpret_cast<float*>(scratch + kStaticPartialsOffset);
+    p.counters = reinterpret_cast<unsigned*>(scratch + kStaticCountersOffset);
+    p.error = reinterpret_cast<unsigned*>(scratch);
+    p.M = mc;
+    p.N = N;
+    p.K = K;
+    p.tiles = T;
+    p.units_per_tile = S;
+    p.units = U;
+    p.max_slots = slots;
+    if (nb == 16) st = launch_decode_nb<WFmt::Q4K, 16, __half>(di, tw, tw, ta, p, s);
+    else st = launch_decode_nb<WFmt::Q4K, 32, __half>(di, tw, tw, ta, p, s);
+    if (st != BUSFILL_OK) return st;
+  }
+  return BUSFILL_OK;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -280,6 +380,8 @@ const char* busfill_status_string(int status) {
     case BUSFILL_ERR_ALLOC: return "workspace allocation failed";
     case BUSFILL_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired (kernel gave up)";
     case BUSFILL_ERR_CUDA: return "CUDA runtime error";
+    case BUSFILL_ERR_SCRATCH_LIMIT:
+      return "problem needs more scratch than the 8 MiB static array of busfill_gemm_q4k_noalloc holds";
     default: return "unknown status";
   }
 }
@@ -299,6 +401,11 @@ int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, 
 
 int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
   return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4k_noalloc(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                             void* stream) {
+  return gemm_q4k_static(blocks, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int busfill_q4(const uint16_t* A, const uint8_t* Wq, const uint16_t* Ws, float* C, int Bsz, int K, int N,

@@ -41,7 +41,9 @@ typedef enum busfill_status {
   BUSFILL_ERR_LAUNCH = -5,             /* kernel launch failed              */
   BUSFILL_ERR_ALLOC = -6,              /* workspace allocation failed       */
   BUSFILL_ERR_DEVICE_TIMEOUT = -7,     /* a bounded device wait expired     */
-  BUSFILL_ERR_CUDA = -8                /* other CUDA runtime error          */
+  BUSFILL_ERR_CUDA = -8,               /* other CUDA runtime error          */
+  BUSFILL_ERR_SCRATCH_LIMIT = -9       /* beyond busfill_gemm_q4k_noalloc's
+                                          static scratch                    */
 } busfill_status;
 
 /* ---------------------------------------------------------------------------
@@ -67,6 +69,40 @@ BUSFILL_API int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const u
  * busfill_q4 (kernels/busfill_v1a.cu:41-46) that its docstring announces
  * (kernels/q4k_batched.py:7-8). */
 BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
+
+/* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
+ * in the reference.
+ *
+ * busfill_gemm_q4k cudaMallocs a split-K workspace on first use of each
+ * stream (and grows it, after a stream synchronize, for larger shapes).
+ * Some callers can't allow that: a host whose own pool already holds nearly
+ * all device memory, where an outside cudaMalloc fails or fragments it; an
+ * operator or plugin interface that hands a kernel only its inputs and
+ * outputs; a latency-bound loop where cudaMalloc or cudaFree would stall the
+ * device.  This entry point keeps its scratch (split-K partial sums, tile
+ * counters, error word) in one 8 MiB array compiled into the library, which
+ * every GPU that loads the library holds until the process exits.  The
+ * caller still passes the inputs and the output; arguments, layout and
+ * results are those of busfill_gemm_q4k.
+ *
+ *   - Limit: N <= 262144 and T * slots * 128 * nb * 4 bytes of partials
+ *     <= 8 MiB - 8448 (T = ceil(N/128) row tiles, slots = most CTAs that
+ *     share one tile, nb = 16 when M <= 16 else 32).  On a 148-SM B200
+ *     every N <= 32640 fits, for any K and M.  Larger problems return
+ *     BUSFILL_ERR_SCRATCH_LIMIT and launch nothing.
+ *   - The first call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture begins.
+ *   - Every call on every stream shares the one array, and each call clears
+ *     its counters and error word (a cudaMemsetAsync on `stream`) before its
+ *     kernels run.  Calls on one stream are ordered and safe; calls whose
+ *     kernels overlap on the GPU (other streams, other host threads) race on
+ *     the array and give wrong results.
+ *   - A device-side wait that expires is recorded in the array, not in the
+ *     per-stream word that busfill_stream_status reads, so it is not reported
+ *     there; the output of such a call is undefined. */
+BUSFILL_API int busfill_gemm_q4k_noalloc(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                                         void* stream);
 
 /* Reference-compatible surface: the arguments and fp32 output of
  * busfill_q4(A, Wq, Ws, C, Bsz, K, N) (kernels/busfill_v1a.cu:41-46) plus a
