@@ -31,7 +31,7 @@ _LIB = None
 STATUS = {
     0: "BUSFILL_OK", -1: "BUSFILL_ERR_INVALID_ARG", -2: "BUSFILL_ERR_SHAPE", -3: "BUSFILL_ERR_ALIGNMENT",
     -4: "BUSFILL_ERR_UNSUPPORTED_DEVICE", -5: "BUSFILL_ERR_LAUNCH", -6: "BUSFILL_ERR_ALLOC",
-    -7: "BUSFILL_ERR_DEVICE_TIMEOUT", -8: "BUSFILL_ERR_CUDA", -9: "BUSFILL_ERR_SCRATCH_LIMIT",
+    -7: "BUSFILL_ERR_DEVICE_TIMEOUT", -8: "BUSFILL_ERR_CUDA",
 }
 
 
@@ -109,6 +109,12 @@ def set_pdl(enabled: bool) -> None:
     _check(_lib().busfill_set_option(1, 1 if enabled else 0), "busfill_set_option")
 
 
+def set_ksplit(csize: int) -> None:
+    """Force the number of CTAs (cluster size, 1..8) that split each 128-row
+    tile along K; 0 restores the library's own choice."""
+    _check(_lib().busfill_set_option(2, int(csize)), "busfill_set_option")
+
+
 # ---------------------------------------------------------------------------
 # torch-tensor wrappers
 # ---------------------------------------------------------------------------
@@ -176,9 +182,9 @@ def gemm_q4k(blocks, a, out=None, stream=None):
 
 def gemm_q4k_noalloc(blocks, a, out, stream=None):
     """gemm_q4k through busfill_gemm_q4k_noalloc: the library allocates no
-    device memory (its split-K scratch is a fixed 8 MiB array in the library
+    device memory (its error words are a fixed 256-byte array in the library
     image), so `out` must be given. Calls whose kernels overlap on the GPU
-    share that array and race."""
+    share that array and race on it."""
     torch = _torch()
     _need(blocks, torch.uint8, "blocks"); _need(a, torch.float16, "a"); _need(out, torch.float16, "out")
     m, k = a.shape

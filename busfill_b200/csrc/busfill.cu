@@ -1,6 +1,7 @@
 // Host side of the C ABI declared in include/busfill.h: argument checks,
-// TMA descriptor encoding, the per-(device, stream) split-K workspace and the
-// kernel launches (programmatic dependent launch by default).
+// TMA descriptor encoding, the choice of the K split (cluster size), the
+// per-(device, stream) error words and the kernel launches (programmatic
+// dependent launch by default).
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -18,12 +19,12 @@
 
 using namespace busfill;
 
-// Scratch of busfill_gemm_q4k_noalloc: [error + detail words | split-K tile
-// counters | split-K partial sums], 8 MiB on every GPU that loads this
-// library, held until the process exits. Host code must not use this name as
-// a pointer: in host code it is only a stand-in for the device array, so the
-// device address is looked up with cudaGetSymbolAddress (static_scratch()).
-constexpr size_t kStaticScratchBytes = size_t(8) << 20;
+// Scratch of busfill_gemm_q4k_noalloc: the device error word and the first
+// failure record, 256 bytes on every GPU that loads this library, held until
+// the process exits. Host code must not use this name as a pointer: in host
+// code it is only a stand-in for the device array, so the device address is
+// looked up with cudaGetSymbolAddress (static_scratch()).
+constexpr size_t kStaticScratchBytes = 256;
 static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 namespace {
@@ -32,6 +33,7 @@ constexpr int kVersion = 100;  // 0.1.0
 // detail word of the last device failure read by busfill_stream_status_ex
 std::atomic<unsigned> g_last_detail{0};
 std::atomic<int> g_use_pdl{1};
+std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 
 // ---------------------------------------------------------------------------
 // device properties (cached)
@@ -97,64 +99,53 @@ bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint
 }
 
 // ---------------------------------------------------------------------------
-// workspace: [error word | counters | split-K partials], one per (device,
-// stream) so that calls on different streams never share counters.
-// Counters are zeroed at allocation and returned to zero by every call.
+// per-(device, stream) device words: [0] error bits, [1] first failure record.
+// Zeroed at allocation; busfill_stream_status clears them after a failure.
 // ---------------------------------------------------------------------------
-struct Workspace {
-  uint8_t* base = nullptr;
-  size_t counters_cap = 0;   // number of counters
-  size_t partials_cap = 0;   // bytes
-  unsigned* error() const { return reinterpret_cast<unsigned*>(base); }
-  unsigned* counters() const { return reinterpret_cast<unsigned*>(base + 256); }
-  float* partials() const { return reinterpret_cast<float*>(base + 256 + ((counters_cap * 4 + 255) / 256) * 256); }
-};
+constexpr size_t kErrorWordsBytes = 256;
 
-std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+std::map<std::pair<int, cudaStream_t>, unsigned*> g_err;
 
-int get_workspace(int dev, cudaStream_t s, size_t ncounters, size_t partial_bytes, Workspace* out) {
+int get_error_words(int dev, cudaStream_t s, unsigned** out) {
   // caller holds g_mu
-  Workspace& w = g_ws[{dev, s}];
-  if (w.base && w.counters_cap >= ncounters && w.partials_cap >= partial_bytes) {
-    *out = w;
-    return BUSFILL_OK;
+  unsigned*& w = g_err[{dev, s}];
+  if (!w) {
+    if (cudaMalloc(&w, kErrorWordsBytes) != cudaSuccess) {
+      cudaGetLastError();
+      w = nullptr;
+      return BUSFILL_ERR_ALLOC;
+    }
+    if (cudaMemsetAsync(w, 0, kErrorWordsBytes, s) != cudaSuccess) return BUSFILL_ERR_CUDA;
   }
-  const size_t nc = std::max<size_t>(std::max(ncounters, w.counters_cap), 1024);
-  const size_t pb = std::max(partial_bytes, w.partials_cap);
-  if (w.base) {
-    // the old buffer may still be read by work queued on this stream
-    if (cudaStreamSynchronize(s) != cudaSuccess) return BUSFILL_ERR_CUDA;
-    cudaFree(w.base);
-    w.base = nullptr;
-  }
-  Workspace nw;
-  nw.counters_cap = nc;
-  nw.partials_cap = pb;
-  const size_t head = 256 + ((nc * 4 + 255) / 256) * 256;
-  if (cudaMalloc(&nw.base, head + pb) != cudaSuccess) {
-    cudaGetLastError();
-    w = Workspace{};
-    return BUSFILL_ERR_ALLOC;
-  }
-  if (cudaMemsetAsync(nw.base, 0, head, s) != cudaSuccess) return BUSFILL_ERR_CUDA;
-  w = nw;
   *out = w;
   return BUSFILL_OK;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl) {
+cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStream_t s, void** args, bool pdl,
+                   int cluster = 1) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelExC(&cfg, func, args);
 }
 
@@ -162,57 +153,121 @@ cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStr
 // decode GEMM launch
 // ---------------------------------------------------------------------------
 template <WFmt FMT, int NB, typename OutT>
+const void* decode_kernel_ptr() {
+  return reinterpret_cast<const void*>(decode_gemm_kernel<FMT, NB, OutT>);
+}
+
+// Raise the kernel's dynamic shared memory limit, once per device.
+template <WFmt FMT, int NB, typename OutT>
+bool decode_smem_attr(int dev) {
+  static std::once_flag once[64];
+  static cudaError_t err[64];
+  std::call_once(once[dev & 63], [&] {
+    err[dev & 63] = cudaFuncSetAttribute(decode_kernel_ptr<FMT, NB, OutT>(),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<NB>::kAlloc);
+  });
+  return err[dev & 63] == cudaSuccess;
+}
+
+// Largest number of clusters of `csize` CTAs that can be resident at once
+// (one CTA per SM); cached per device, kernel and cluster size.
+template <WFmt FMT, int NB, typename OutT>
+int max_active_clusters(int dev, int csize, int sm_count) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({dev, csize});
+  if (it != cache.end()) return it->second;
+  int v = sm_count / csize;
+  if (!decode_smem_attr<FMT, NB, OutT>(dev)) return v;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(csize * std::max(1, sm_count / csize)));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = DecodeSmem<NB>::kAlloc;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, decode_kernel_ptr<FMT, NB, OutT>(), &cfg) == cudaSuccess && n > 0)
+    v = std::min(v, n);
+  else
+    cudaGetLastError();
+  cache[{dev, csize}] = v;
+  return v;
+}
+
+struct DecodeSchedule {
+  int csize = 1;      // CTAs per cluster = K split of every tile
+  int nclusters = 1;  // clusters in the grid
+};
+
+// Pick the K split c (1..8) with the shortest estimated weight-streaming time:
+// each active CTA moves at most kSmGBs (one SM's TMA rate on 144-byte weight
+// rows, measured on B200) and all of them together at most kHbmGBs; a cluster
+// takes ceil(T / G) tiles of ceil(S / c) units each. Ties go to the smaller c.
+template <WFmt FMT, int NB, typename OutT>
+DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count) {
+  constexpr double kSmGBs = 57.0;
+  constexpr double kHbmGBs = 6500.0;
+  DecodeSchedule best;
+  double best_ns = 1e300;
+  const int forced = g_force_ksplit.load();
+  for (int c = 1; c <= std::min(8, S); ++c) {
+    if (forced > 0 && forced <= S && c != forced) continue;
+    const int cap = c == 1 ? sm_count : max_active_clusters<FMT, NB, OutT>(dev, c, sm_count);
+    const int ncl = std::min(T, cap);
+    if (ncl < 1) continue;
+    const long long rounds = (T + ncl - 1) / ncl;
+    const long long units = rounds * ((S + c - 1) / c);
+    const double rate = std::min(kSmGBs, kHbmGBs / (double)(ncl * c));
+    const double ns = (double)units * kWStageBytes / rate;
+    if (ns < best_ns * 0.999) {
+      best_ns = ns;
+      best.csize = c;
+      best.nclusters = ncl;
+    }
+  }
+  return best;
+}
+
+template <WFmt FMT, int NB, typename OutT>
 int launch_decode_nb(const DeviceInfo& di, const CUtensorMap& tw, const CUtensorMap& tws, const CUtensorMap& ta,
                      const DecodeParams& p, cudaStream_t s) {
-  auto kern = decode_gemm_kernel<FMT, NB, OutT>;
+  const void* kern = decode_kernel_ptr<FMT, NB, OutT>();
   constexpr int smem = DecodeSmem<NB>::kAlloc;
-  static std::once_flag attr_once[64];
-  static cudaError_t attr_err[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  std::call_once(attr_once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  });
-  if (attr_err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
-  const int grid = std::min(p.units, di.sm_count);
+  if (!decode_smem_attr<FMT, NB, OutT>(dev)) return BUSFILL_ERR_LAUNCH;
+  const int grid = p.nclusters * p.csize;
   void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tws), const_cast<CUtensorMap*>(&ta),
                   const_cast<DecodeParams*>(&p)};
-  if (launch(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), smem, s, args,
-             g_use_pdl.load() != 0) != cudaSuccess) {
+  if (launch(kern, dim3(grid), dim3(kThreads), smem, s, args, g_use_pdl.load() != 0, p.csize) != cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_LAUNCH;
   }
   return BUSFILL_OK;
 }
 
-int max_contributors(int tiles, int S, int units, int grid) {
-  int best = 1;
-  for (int t = 0; t < tiles; ++t) {
-    const int a = streamk_cta_of((long long)t * S, units, grid);
-    const int b = streamk_cta_of((long long)t * S + S - 1, units, grid);
-    best = std::max(best, b - a + 1);
-  }
-  return best;
-}
-
-template <WFmt FMT, typename OutT>
-int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M, int N, int K,
-              cudaStream_t s) {
+// Checks shared by every GEMM entry point.
+template <WFmt FMT>
+int check_gemm_args(const uint8_t* w, const uint16_t* ws, const uint16_t* a, const void* c, int M, int N, int K) {
   if (!w || !a || !c || (FMT == WFmt::Q4_0 && !ws)) return BUSFILL_ERR_INVALID_ARG;
   if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
   if (!aligned16(w) || !aligned16(a) || (ws && !aligned16(ws))) return BUSFILL_ERR_ALIGNMENT;
-  DeviceInfo di;
-  int dev = 0;
-  int st = current_device(&di, &dev);
-  if (st != BUSFILL_OK) return st;
+  return BUSFILL_OK;
+}
 
+// Launches the decode kernel once per 32 rows of A; `error` points at the two
+// device words the kernels report failures to.
+template <WFmt FMT, typename OutT>
+int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
+               int M, int N, int K, unsigned* error, cudaStream_t s) {
   const int S = K / kUnitK;
   const int T = (N + kTileRows - 1) / kTileRows;
-  const long long U64 = (long long)T * S;
-  if (U64 > (1LL << 30)) return BUSFILL_ERR_SHAPE;
-  const int U = (int)U64;
-  const int grid = std::min(U, di.sm_count);
-  const int slots = max_contributors(T, S, U, grid);
 
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
@@ -231,34 +286,48 @@ int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, 
       return BUSFILL_ERR_CUDA;
   }
 
-  std::lock_guard<std::mutex> lk(g_mu);
   for (int m0 = 0; m0 < M; m0 += 32) {
     const int mc = std::min(32, M - m0);
     const int nb = mc <= 16 ? 16 : 32;
-    Workspace wsp;
-    st = get_workspace(dev, s, (size_t)T, (size_t)T * slots * kTileRows * nb * sizeof(float), &wsp);
-    if (st != BUSFILL_OK) return st;
+    const DecodeSchedule sch = nb == 16 ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count)
+                                        : choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count);
     const uint16_t* a_chunk = a + (size_t)m0 * K;
     if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_chunk, (uint64_t)K, (uint64_t)mc, (uint64_t)K * 2,
                       kChunkK, (uint32_t)nb, CU_TENSOR_MAP_SWIZZLE_128B))
       return BUSFILL_ERR_CUDA;
     DecodeParams p;
     p.c = reinterpret_cast<OutT*>(c) + (size_t)m0 * N;
-    p.partials = wsp.partials();
-    p.counters = wsp.counters();
-    p.error = wsp.error();
+    p.error = error;
     p.M = mc;
     p.N = N;
     p.K = K;
     p.tiles = T;
     p.units_per_tile = S;
-    p.units = U;
-    p.max_slots = slots;
-    if (nb == 16) st = launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s);
-    else st = launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
+    p.csize = sch.csize;
+    p.nclusters = sch.nclusters;
+    const int st = nb == 16 ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
+                            : launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
     if (st != BUSFILL_OK) return st;
   }
   return BUSFILL_OK;
+}
+
+template <WFmt FMT, typename OutT>
+int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M, int N, int K,
+              cudaStream_t s) {
+  int st = check_gemm_args<FMT>(w, ws, a, c, M, N, K);
+  if (st != BUSFILL_OK) return st;
+  DeviceInfo di;
+  int dev = 0;
+  st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  unsigned* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = get_error_words(dev, s, &err);
+  }
+  if (st != BUSFILL_OK) return st;
+  return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, err, s);
 }
 
 int grid_for(long long work, int sm_count) {
@@ -269,12 +338,6 @@ int grid_for(long long work, int sm_count) {
 // ---------------------------------------------------------------------------
 // statically allocated scratch (busfill_gemm_q4k_noalloc)
 // ---------------------------------------------------------------------------
-constexpr size_t kStaticCountersOffset = 256;
-constexpr size_t kStaticMaxTiles = 2048;  // N <= 262144
-constexpr size_t kStaticPartialsOffset = kStaticCountersOffset + kStaticMaxTiles * sizeof(unsigned);
-constexpr size_t kStaticPartialsBytes = kStaticScratchBytes - kStaticPartialsOffset;
-static_assert(kStaticPartialsOffset % 256 == 0, "partials must stay 256-byte aligned");
-
 constexpr int kMaxDevices = 64;
 uint8_t* g_static_ptr[kMaxDevices] = {};
 
@@ -296,66 +359,22 @@ int static_scratch(int dev, uint8_t** out) {
 }
 
 int gemm_q4k_static(const uint8_t* w, const uint16_t* a, uint16_t* c, int M, int N, int K, cudaStream_t s) {
-  if (!w || !a || !c) return BUSFILL_ERR_INVALID_ARG;
-  if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
-  if (!aligned16(w) || !aligned16(a)) return BUSFILL_ERR_ALIGNMENT;
+  int st = check_gemm_args<WFmt::Q4K>(w, nullptr, a, c, M, N, K);
+  if (st != BUSFILL_OK) return st;
   DeviceInfo di;
   int dev = 0;
-  int st = current_device(&di, &dev);
+  st = current_device(&di, &dev);
   if (st != BUSFILL_OK) return st;
-
-  const int S = K / kUnitK;
-  const long long T64 = ((long long)N + kTileRows - 1) / kTileRows;
-  if (T64 > (long long)kStaticMaxTiles) return BUSFILL_ERR_SCRATCH_LIMIT;
-  const int T = (int)T64;
-  const long long U64 = T64 * S;
-  if (U64 > (1LL << 30)) return BUSFILL_ERR_SHAPE;
-  const int U = (int)U64;
-  const int grid = std::min(U, di.sm_count);
-  const int slots = max_contributors(T, S, U, grid);
-  const int nb_max = M <= 16 ? 16 : 32;
-  if ((size_t)T * slots * kTileRows * nb_max * sizeof(float) > kStaticPartialsBytes) return BUSFILL_ERR_SCRATCH_LIMIT;
-
   uint8_t* scratch = nullptr;
   st = static_scratch(dev, &scratch);
   if (st != BUSFILL_OK) return st;
-
-  CUtensorMap tw, ta;
-  const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
-  if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
-                    CU_TENSOR_MAP_SWIZZLE_NONE))
-    return BUSFILL_ERR_CUDA;
-
-  // the error words and the counters must start at zero; a previous call that
-  // gave up part way may have left them set
-  if (cudaMemsetAsync(scratch, 0, kStaticCountersOffset + (size_t)T * sizeof(unsigned), s) != cudaSuccess) {
+  // the error words must start at zero; a previous call that gave up part way
+  // may have left them set
+  if (cudaMemsetAsync(scratch, 0, kStaticScratchBytes, s) != cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_CUDA;
   }
-  for (int m0 = 0; m0 < M; m0 += 32) {
-    const int mc = std::min(32, M - m0);
-    const int nb = mc <= 16 ? 16 : 32;
-    const uint16_t* a_chunk = a + (size_t)m0 * K;
-    if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_chunk, (uint64_t)K, (uint64_t)mc, (uint64_t)K * 2,
-                      kChunkK, (uint32_t)nb, CU_TENSOR_MAP_SWIZZLE_128B))
-      return BUSFILL_ERR_CUDA;
-    DecodeParams p;
-    p.c = reinterpret_cast<__half*>(c) + (size_t)m0 * N;
-    p.partials = reinterpret_cast<float*>(scratch + kStaticPartialsOffset);
-    p.counters = reinterpret_cast<unsigned*>(scratch + kStaticCountersOffset);
-    p.error = reinterpret_cast<unsigned*>(scratch);
-    p.M = mc;
-    p.N = N;
-    p.K = K;
-    p.tiles = T;
-    p.units_per_tile = S;
-    p.units = U;
-    p.max_slots = slots;
-    if (nb == 16) st = launch_decode_nb<WFmt::Q4K, 16, __half>(di, tw, tw, ta, p, s);
-    else st = launch_decode_nb<WFmt::Q4K, 32, __half>(di, tw, tw, ta, p, s);
-    if (st != BUSFILL_OK) return st;
-  }
-  return BUSFILL_OK;
+  return run_decode<WFmt::Q4K, __half>(di, dev, w, nullptr, a, c, M, N, K, reinterpret_cast<unsigned*>(scratch), s);
 }
 
 }  // namespace
@@ -380,8 +399,6 @@ const char* busfill_status_string(int status) {
     case BUSFILL_ERR_ALLOC: return "workspace allocation failed";
     case BUSFILL_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired (kernel gave up)";
     case BUSFILL_ERR_CUDA: return "CUDA runtime error";
-    case BUSFILL_ERR_SCRATCH_LIMIT:
-      return "problem needs more scratch than the 8 MiB static array of busfill_gemm_q4k_noalloc holds";
     default: return "unknown status";
   }
 }
@@ -389,6 +406,11 @@ const char* busfill_status_string(int status) {
 int busfill_set_option(int option, int value) {
   if (option == BUSFILL_OPT_PDL) {
     g_use_pdl.store(value ? 1 : 0);
+    return BUSFILL_OK;
+  }
+  if (option == BUSFILL_OPT_KSPLIT) {
+    if (value < 0 || value > 8) return BUSFILL_ERR_INVALID_ARG;
+    g_force_ksplit.store(value);
     return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;
@@ -467,20 +489,18 @@ int busfill_stream_status_ex(void* stream, unsigned* bits) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return BUSFILL_ERR_CUDA;
   std::lock_guard<std::mutex> lk(g_mu);
-  auto it = g_ws.find({dev, s});
-  if (it == g_ws.end() || !it->second.base) return BUSFILL_OK;
+  auto it = g_err.find({dev, s});
+  if (it == g_err.end() || !it->second) return BUSFILL_OK;
   unsigned err2[2] = {0, 0};
-  if (cudaMemcpy(err2, it->second.error(), sizeof(err2), cudaMemcpyDeviceToHost) != cudaSuccess)
-    return BUSFILL_ERR_CUDA;
+  if (cudaMemcpy(err2, it->second, sizeof(err2), cudaMemcpyDeviceToHost) != cudaSuccess) return BUSFILL_ERR_CUDA;
   const unsigned err = err2[0];
   if (bits) {
     bits[0] = err;
     g_last_detail = err2[1];
   }
   if (err == 0) return BUSFILL_OK;
-  // a kernel gave up part way: clear the error word and the split-K counters
-  const size_t head = 256 + ((it->second.counters_cap * 4 + 255) / 256) * 256;
-  if (cudaMemset(it->second.base, 0, head) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  // a kernel gave up part way: clear the words for the next call
+  if (cudaMemset(it->second, 0, kErrorWordsBytes) != cudaSuccess) return BUSFILL_ERR_CUDA;
   return BUSFILL_ERR_DEVICE_TIMEOUT;
 }
 
@@ -493,17 +513,17 @@ int busfill_probe_umma(const uint16_t* a, const uint16_t* b, float* d, int nb, v
   int st = current_device(&di, &dev);
   if (st != BUSFILL_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  Workspace wsp;
+  unsigned* err = nullptr;
   {
     std::lock_guard<std::mutex> lk(g_mu);
-    st = get_workspace(dev, s, 1, 0, &wsp);
+    st = get_error_words(dev, s, &err);
   }
   if (st != BUSFILL_OK) return st;
   const __half* ah = reinterpret_cast<const __half*>(a);
   const __half* bh = reinterpret_cast<const __half*>(b);
-  if (nb == 16) umma_probe_kernel<16><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
-  else if (nb == 32) umma_probe_kernel<32><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
-  else umma_probe_kernel<64><<<1, 128, 0, s>>>(ah, bh, d, wsp.error());
+  if (nb == 16) umma_probe_kernel<16><<<1, 128, 0, s>>>(ah, bh, d, err);
+  else if (nb == 32) umma_probe_kernel<32><<<1, 128, 0, s>>>(ah, bh, d, err);
+  else umma_probe_kernel<64><<<1, 128, 0, s>>>(ah, bh, d, err);
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
 }
 

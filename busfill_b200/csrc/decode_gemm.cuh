@@ -19,7 +19,7 @@
 // (`udone`), which releases the unit's operand and activation slots and
 // publishes its accumulator. Three unit slots are kept in flight.
 //
-// Warp roles (16 warps, one persistent CTA per SM):
+// Warp roles (16 warps, one CTA per SM):
 //   0      weight TMA producer: one 2D box of 128 rows x one unit (18 KB) per
 //          stage into a 6-stage ring. Weights do not depend on earlier kernels,
 //          so this runs before griddepcontrol.wait (programmatic dependent
@@ -48,12 +48,15 @@
 //   activations of sub-block j (the only rounding the Q4_K path adds beyond
 //   fp32 accumulation).
 //
-// Work split ("stream-K"): CTA c of G takes units [floor(c*U/G),
-// floor((c+1)*U/G)) in tile-major order, so every SM streams the same number
-// of weight bytes. A tile split across CTAs is reduced deterministically: each
-// contributor stores its fp32 partial in its slot, the last arriver (atomic
-// counter, release/acquire) sums the slots in slot order, writes C and resets
-// the counter.
+// Work split: a tile of 128 weight rows is split along K over the c CTAs of
+// a thread-block cluster (rank k takes units [k*S/c, (k+1)*S/c) of every
+// tile); cluster g of G takes tiles g, g+G, g+2G, ... The host picks c so
+// that the CTAs that stream weights have the most bandwidth each (one SM's
+// TMA engine moves ~57 GB/s of these 144-byte rows, so 120 CTAs stream as
+// fast as 148 at K = N = 5120). At the end of each tile the non-zero ranks
+// write their fp32 partial sums into their own shared memory and signal rank
+// 0, which reads them through distributed shared memory, adds them in rank
+// order (deterministic) and writes C. No global scratch, no atomics.
 //
 // Every wait is bounded (ptx.cuh: kWaitTimeoutNs): a kernel that cannot make
 // progress records an error bit and winds down instead of hanging the GPU.
@@ -101,23 +104,16 @@ constexpr unsigned kErrXStage = 64u;
 
 struct DecodeParams {
   void* c;              // [M, N] row-major, OutT
-  float* partials;      // [tiles][max_slots][128][NB] fp32 split-K partials
-  unsigned* counters;   // [tiles] arrival counters, zero between calls
-  unsigned* error;      // device error word
+  unsigned* error;      // device error word (+1: first failure record)
   int M, N, K;
   int tiles;            // T = ceil(N / 128)
   int units_per_tile;   // S = K / 256
-  int units;            // U = T * S
-  int max_slots;        // max CTAs contributing to one tile
+  int csize;            // CTAs per cluster: the K split of every tile (1..8)
+  int nclusters;        // G; cluster g takes tiles g, g + G, ...; G <= T
 };
 
-__host__ __device__ __forceinline__ int streamk_first_unit(long long cta, long long units, long long grid) {
-  return (int)((cta * units) / grid);
-}
-// CTA whose unit range contains unit u: max{c : floor(c*U/G) <= u}.
-__host__ __device__ __forceinline__ int streamk_cta_of(long long u, long long units, long long grid) {
-  return (int)(((u + 1) * grid + units - 1) / units - 1);
-}
+// Units [first, last) of every tile that cluster rank `rank` of `csize` takes.
+__host__ __device__ __forceinline__ int ksplit_begin(int rank, int S, int csize) { return rank * S / csize; }
 
 // TMEM column map (512 columns allocated)
 template <int NB>
@@ -137,7 +133,8 @@ struct DecodeSmem {
   static constexpr int kXOff = kWOff + kWStages * kWStageBytes;
   static constexpr int kSOff = kXOff + kSlots * kXSlotBytes;         // Asum B tiles, one per slot
   static constexpr int kDOff = kSOff + kSlots * kXChunkBytes;
-  static constexpr int kBarOff = kDOff + kDStages * kTileRows * 4;
+  static constexpr int kRedOff = kDOff + kDStages * kTileRows * 4;   // [128][NB] fp32 partial (cluster reduction)
+  static constexpr int kBarOff = kRedOff + kTileRows * NB * 4;
   // barrier slots
   static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
   static constexpr int bXFull = bWEmpty + kWStages;        // activations landed (TMA tx)
@@ -145,7 +142,9 @@ struct DecodeSmem {
   static constexpr int bUDone = bReady + kSlots;           // unit's MMAs complete (commit)
   static constexpr int bAccEmpty = bUDone + kSlots;        // X[b] read by the epilogue
   static constexpr int bYEmpty = bAccEmpty + 2;
-  static constexpr int bFinal = bYEmpty + 1;
+  static constexpr int bRedFull = bYEmpty + 1;             // rank 0: partials of the other ranks written
+  static constexpr int bRedEmpty = bRedFull + 1;           // rank k > 0: rank 0 has read this rank's partial
+  static constexpr int bFinal = bRedEmpty + 1;
   static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 64;
@@ -212,16 +211,6 @@ __device__ __forceinline__ void split_hi_lo(float x, __half& hi, __half& lo) {
   lo = __float2half_rn(x - __half2float(hi));
 }
 
-__device__ __forceinline__ void named_bar_sync_epilogue() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
-}
-
-__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
-  unsigned old;
-  asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
-}
-
 // packed fp32 pair FMA (sm_100): d = a*b + c
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   unsigned long long r;
@@ -239,17 +228,20 @@ __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_
 template <>
 __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
-// Per-unit schedule facts every role derives the same way.
+// Per-unit schedule facts every role derives the same way: unit i of this CTA
+// is unit sb0 + i % len of its cluster's (i / len)-th tile.
 struct UnitInfo {
-  int tile, sb;
-  bool seg_first, seg_last;   // first / last unit of this CTA's run within the tile
+  int tile, sb, seg;
+  bool seg_first, seg_last;   // first / last unit of this CTA's part of the tile
 };
-__device__ __forceinline__ UnitInfo unit_info(int u, int u0, int u1, int S) {
+__device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, int nclusters) {
   UnitInfo r;
-  r.tile = u / S;
-  r.sb = u - r.tile * S;
-  r.seg_first = (u == u0) || (r.sb == 0);
-  r.seg_last = (u == u1 - 1) || (r.sb == S - 1);
+  r.seg = i / len;
+  const int j = i - r.seg * len;
+  r.tile = g + r.seg * nclusters;
+  r.sb = sb0 + j;
+  r.seg_first = (j == 0);
+  r.seg_last = (j == len - 1);
   return r;
 }
 
@@ -280,17 +272,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.units_per_tile;
-  const int u0 = streamk_first_unit(blockIdx.x, p.units, gridDim.x);
-  const int u1 = streamk_first_unit(blockIdx.x + 1, p.units, gridDim.x);
-  const int nunits = u1 - u0;
+  const int csize = p.csize;
+  // clusters tile the 1-D grid in blockIdx order: rank = blockIdx.x % csize
+  const int crank = (int)(blockIdx.x % (unsigned)csize);
+  const int g = (int)(blockIdx.x / (unsigned)csize);
+  const int sb0 = ksplit_begin(crank, S, csize);
+  const int len = ksplit_begin(crank + 1, S, csize) - sb0;
+  const int ntiles = (p.tiles - g + p.nclusters - 1) / p.nclusters;
+  const int nunits = ntiles * len;
 
   // Every role waits with the whole warp; a wait that times out in any lane
   // counts as a failure for the warp, which then stops issuing work.
   bool ok = true;
   int diag_unit = -1;                  // unit being processed, for the failure record
-  auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+  auto warp_wait = [&](uint32_t bar, uint32_t parity, bool cluster_scope = false) -> bool {
     if (!ok) return false;
-    const bool got = mbar_wait(bar, parity);
+    const bool got = cluster_scope ? mbar_wait_cluster(bar, parity) : mbar_wait(bar, parity);
     ok = __all_sync(0xffffffffu, got);
     if (!ok && lane == 0) {
       // first failure in the grid: warp, unit, barrier slot, parity
@@ -318,6 +315,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) mbar_init(BAR(L::bAccEmpty + b), 4);
     mbar_init(BAR(L::bYEmpty), 4);
+    mbar_init(BAR(L::bRedFull), csize > 1 ? 4u * (uint32_t)(csize - 1) : 1u);   // 4 epilogue warps per other rank
+    mbar_init(BAR(L::bRedEmpty), 4);                                             // rank 0's 4 epilogue warps
     mbar_init(BAR(L::bFinal), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmap_w);
@@ -331,6 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  // the other CTAs of the cluster arrive on our barriers: they must be initialised first
+  if (csize > 1) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = misc[0];
   // Let the next kernel on the stream launch now: its CTAs take SMs as ours
@@ -343,8 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nunits; ++i) {
       const int s = i % kWStages;
       if (!warp_wait(BAR(L::bWEmpty + s), ((i / kWStages) & 1) ^ 1)) break;
-      const int u = u0 + i;
-      const int tile = u / S, sb = u - tile * S;
+      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
+      const int tile = ui.tile, sb = ui.sb;
       const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
       if (elect_one()) {
         mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
@@ -374,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < nunits; ++i) {
       if (!wait_slot_free(i)) break;
       const int s = i % kSlots;
-      const int sb = (u0 + i) % S;
+      const int sb = sb0 + i % len;
       if (elect_one()) {
         mbar_arrive_expect_tx(BAR(L::bXFull + s), L::kXSlotBytes);
 #pragma unroll
@@ -448,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int yuses = 0;         // Q4_K segments started (Y buffer uses)
     for (int i = 0; i < nunits; ++i) {
       diag_unit = i;
-      const UnitInfo ui = unit_info(u0 + i, u0, u1, S);
+      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
       const int s = i % kSlots;
       // every unit accumulates into X[i & 1]; the epilogue folds it into
       // registers, so the MMA is never more than two units ahead of it
@@ -600,61 +601,54 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
     };
 
-    // write this thread's finished segment (tile) result
-    auto flush = [&](int tile) {
-      pdl_wait_prerequisites();  // C / workspace may still be in use by the previous kernel
-      const int first_cta = streamk_cta_of((long long)tile * S, p.units, gridDim.x);
-      const int last_cta = streamk_cta_of((long long)tile * S + S - 1, p.units, gridDim.x);
+    // Finish tile `tile` (this CTA's segment `seg`). One CTA per tile: write C.
+    // Otherwise ranks k > 0 leave their partial in their own shared memory
+    // ([row][NB] fp32, 16-byte chunks swizzled by row) and signal rank 0; rank 0
+    // adds them in rank order through distributed shared memory and writes C.
+    auto flush = [&](int tile, int seg) {
       const int n = tile * kTileRows + r;
       OutT* C = reinterpret_cast<OutT*>(p.c);
-      if (first_cta == last_cta) {
-        if (ok && n < p.N) {
+      constexpr int kChunks = NB / 4;
+      const uint32_t my_row = sbase + L::kRedOff + (uint32_t)(r * NB * 4);
+      const int swz = r & (kChunks - 1);
+      if (csize > 1 && crank != 0) {
+        // our buffer is free once rank 0 has read the previous segment's partial
+        if (seg > 0) warp_wait(BAR(L::bRedEmpty), (uint32_t)((seg - 1) & 1), true);
 #pragma unroll
-          for (int t = 0; t < NB; ++t)
-            if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
+        for (int j = 0; j < kChunks; ++j) {
+          const uint32_t a = my_row + (uint32_t)((j ^ swz) << 4);
+          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(acc[4 * j]), "f"(acc[4 * j + 1]),
+                       "f"(acc[4 * j + 2]), "f"(acc[4 * j + 3])
+                       : "memory");
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(BAR(L::bRedFull), 0));
         return;
       }
-      const int slot = (int)blockIdx.x - first_cta;
-      const int ncontrib = last_cta - first_cta + 1;
-      float* base = p.partials + (size_t)tile * p.max_slots * kTileRows * NB;
-      float* mine = base + ((size_t)slot * kTileRows + r) * NB;
+      if (csize > 1) {
+        warp_wait(BAR(L::bRedFull), (uint32_t)(seg & 1), true);
+        for (int k = 1; k < csize; ++k) {
+          const uint32_t src = mapa_shared(my_row, (uint32_t)k);
+          float4 v[kChunks];
 #pragma unroll
-      for (int t = 0; t < NB; t += 4) *reinterpret_cast<float4*>(mine + t) = make_float4(acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
-      named_bar_sync_epilogue();
-      if (threadIdx.x == kWarpEpilogue0 * 32) {
-        // release: this CTA's partial stores (ordered by the barrier) become
-        // visible before the counter moves; acquire: the last arriver sees all
-        const unsigned old = atom_add_acq_rel_gpu(&p.counters[tile], 1u);
-        misc[1] = (old == (unsigned)(ncontrib - 1)) ? 1u : 0u;
-      }
-      named_bar_sync_epilogue();
-      if (misc[1] != 0u) {
-        float sum[NB];
+          for (int j = 0; j < kChunks; ++j) v[j] = ld_dsmem_f4(src + (uint32_t)((j ^ swz) << 4));
 #pragma unroll
-        for (int t = 0; t < NB; ++t) sum[t] = 0.f;
-        // every slot, this CTA's own included, is summed from memory in slot
-        // order, so the result does not depend on which CTA arrived last
-        for (int s = 0; s < ncontrib; ++s) {
-          const float4* part = reinterpret_cast<const float4*>(base + ((size_t)s * kTileRows + r) * NB);
-#pragma unroll
-          for (int h = 0; h < NB / 4; h += 4) {
-            float4 v[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = __ldcg(part + h + t);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const int o = 4 * (h + t);
-              sum[o] += v[t].x; sum[o + 1] += v[t].y; sum[o + 2] += v[t].z; sum[o + 3] += v[t].w;
-            }
+          for (int j = 0; j < kChunks; ++j) {
+            acc[4 * j] += v[j].x;
+            acc[4 * j + 1] += v[j].y;
+            acc[4 * j + 2] += v[j].z;
+            acc[4 * j + 3] += v[j].w;
           }
         }
-        if (ok && n < p.N) {
+        __syncwarp();
+        if (lane == 0)
+          for (int k = 1; k < csize; ++k) mbar_arrive_remote(mapa_shared(BAR(L::bRedEmpty), (uint32_t)k));
+      }
+      pdl_wait_prerequisites();  // C may still be read by the previous kernel
+      if (ok && n < p.N) {
 #pragma unroll
-          for (int t = 0; t < NB; ++t)
-            if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(sum[t]);
-        }
-        if (threadIdx.x == kWarpEpilogue0 * 32) p.counters[tile] = 0u;  // ready for the next call
+        for (int t = 0; t < NB; ++t)
+          if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
       }
     };
 
@@ -663,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < nunits; ++i) {
       diag_unit = i;
-      const UnitInfo ui = unit_info(u0 + i, u0, u1, S);
+      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
       // Every unit is folded, in order: a waiter on a parity barrier must not
       // skip phases (a wait for phase n+1 posted before phase n completed
       // would see the stale parity as complete).
@@ -688,7 +682,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fold_x(i, i & 1, 1.0f);
       }
       if (ui.seg_last) {
-        flush(ui.tile);
+        flush(ui.tile, ui.seg);
 #pragma unroll
         for (int t = 0; t < NB; ++t) acc[t] = 0.f;
       }
@@ -699,6 +693,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------- teardown ----------------
   __syncwarp();
   __syncthreads();
+  // no CTA may leave while another CTA of its cluster can still read its
+  // shared memory or arrive on its barriers
+  if (csize > 1) cluster_sync_all();
   if (warp == kWarpXProducer) {
     bool done = true;
     if (lane == 0) done = mbar_wait(BAR(L::bFinal), 0);

@@ -41,9 +41,7 @@ typedef enum busfill_status {
   BUSFILL_ERR_LAUNCH = -5,             /* kernel launch failed              */
   BUSFILL_ERR_ALLOC = -6,              /* workspace allocation failed       */
   BUSFILL_ERR_DEVICE_TIMEOUT = -7,     /* a bounded device wait expired     */
-  BUSFILL_ERR_CUDA = -8,               /* other CUDA runtime error          */
-  BUSFILL_ERR_SCRATCH_LIMIT = -9       /* beyond busfill_gemm_q4k_noalloc's
-                                          static scratch                    */
+  BUSFILL_ERR_CUDA = -8                /* other CUDA runtime error          */
 } busfill_status;
 
 /* ---------------------------------------------------------------------------
@@ -73,31 +71,26 @@ BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint1
 /* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
  * in the reference.
  *
- * busfill_gemm_q4k cudaMallocs a split-K workspace on first use of each
- * stream (and grows it, after a stream synchronize, for larger shapes).
- * Some callers can't allow that: a host whose own pool already holds nearly
- * all device memory, where an outside cudaMalloc fails or fragments it; an
- * operator or plugin interface that hands a kernel only its inputs and
- * outputs; a latency-bound loop where cudaMalloc or cudaFree would stall the
- * device.  This entry point keeps its scratch (split-K partial sums, tile
- * counters, error word) in one 8 MiB array compiled into the library, which
- * every GPU that loads the library holds until the process exits.  The
- * caller still passes the inputs and the output; arguments, layout and
- * results are those of busfill_gemm_q4k.
+ * busfill_gemm_q4k cudaMallocs a small per-stream buffer (the device error
+ * words) on first use of each stream.  Some callers can't allow that: a host
+ * whose own pool already holds nearly all device memory, where an outside
+ * cudaMalloc fails or fragments it; an operator or plugin interface that
+ * hands a kernel only its inputs and outputs; a latency-bound loop where
+ * cudaMalloc would stall the device.  This entry point keeps its scratch
+ * (the error word and the first failure record) in one 256-byte array
+ * compiled into the library, which every GPU that loads the library holds
+ * until the process exits.  The split-K partial sums live in shared memory,
+ * so no problem size needs more scratch.  The caller still passes the inputs
+ * and the output; arguments, layout and results are those of
+ * busfill_gemm_q4k.
  *
- *   - Limit: N <= 262144 and T * slots * 128 * nb * 4 bytes of partials
- *     <= 8 MiB - 8448 (T = ceil(N/128) row tiles, slots = most CTAs that
- *     share one tile, nb = 16 when M <= 16 else 32).  On a 148-SM B200
- *     every N <= 32640 fits, for any K and M.  Larger problems return
- *     BUSFILL_ERR_SCRATCH_LIMIT and launch nothing.
  *   - The first call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
  *     before any stream capture begins.
  *   - Every call on every stream shares the one array, and each call clears
- *     its counters and error word (a cudaMemsetAsync on `stream`) before its
- *     kernels run.  Calls on one stream are ordered and safe; calls whose
+ *     it (a cudaMemsetAsync on `stream`) before its kernels run.  Calls whose
  *     kernels overlap on the GPU (other streams, other host threads) race on
- *     the array and give wrong results.
+ *     the array: a failure of one can be cleared or misattributed by another.
  *   - A device-side wait that expires is recorded in the array, not in the
  *     per-stream word that busfill_stream_status reads, so it is not reported
  *     there; the output of such a call is undefined. */
@@ -157,10 +150,16 @@ BUSFILL_API const char* busfill_status_string(int status);
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 BUSFILL_API int busfill_version(void);
 
-/* Options (process-wide). BUSFILL_OPT_PDL: 1 (default) launches the GEMMs with
- * programmatic dependent launch so back-to-back calls on one stream overlap
- * the next call's weight streaming with the previous call's tail; 0 disables. */
+/* Options (process-wide).
+ *   BUSFILL_OPT_PDL: 1 (default) launches the GEMMs with programmatic
+ *     dependent launch so back-to-back calls on one stream overlap the next
+ *     call's weight streaming with the previous call's tail; 0 disables.
+ *   BUSFILL_OPT_KSPLIT: 0 (default) lets the library choose how many CTAs (a
+ *     thread-block cluster of 1..8) split the K range of each 128-row tile;
+ *     1..8 forces that split where K/256 allows it (a tuning and test knob).
+ * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
+#define BUSFILL_OPT_KSPLIT 2
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the

@@ -2,8 +2,8 @@
 
 No GPU: the library is loaded and its exports and status strings checked; the
 dequant instruction chains of busfill_b200/csrc/decode_gemm.cuh are emulated
-bit for bit in numpy and compared with the oracle; the stream-K partition
-arithmetic is checked exhaustively on small sizes.
+bit for bit in numpy and compared with the oracle; the cluster K split
+and tile assignment are checked to cover every unit exactly once.
 """
 import ctypes
 
@@ -176,26 +176,42 @@ def test_q4k_scale_words_match_oracle_unpack():
 
 
 # ---------------------------------------------------------------------------
-# stream-K partition arithmetic (decode_gemm.cuh: streamk_first_unit / streamk_cta_of)
+# cluster K split and tile assignment (decode_gemm.cuh: ksplit_begin, unit_info)
 # ---------------------------------------------------------------------------
-def first_unit(c, units, grid):
-    return (c * units) // grid
+def ksplit_begin(rank, S, c):
+    return rank * S // c
 
 
-def cta_of(u, units, grid):
-    return ((u + 1) * grid + units - 1) // units - 1
+def unit_info(i, length, sb0, g, nclusters):
+    seg = i // length
+    j = i - seg * length
+    return g + seg * nclusters, sb0 + j, seg, j == 0, j == length - 1
 
 
-@pytest.mark.parametrize("units", [1, 2, 3, 7, 40, 148, 149, 800, 801, 3000])
-def test_streamk_partition_is_consistent(units):
-    for grid in sorted({1, 2, 5, 37, 148, min(units, 148)}):
-        if grid > units:
-            continue
-        owner = np.empty(units, dtype=np.int64)
-        for c in range(grid):
-            a, b = first_unit(c, units, grid), first_unit(c + 1, units, grid)
-            assert b - a >= 1  # no CTA is idle when grid <= units
-            owner[a:b] = c
-        assert first_unit(grid, units, grid) == units
-        for u in range(units):
-            assert cta_of(u, units, grid) == owner[u]
+@pytest.mark.parametrize("S", [1, 2, 3, 7, 20, 32, 64, 68, 160])
+@pytest.mark.parametrize("T", [1, 3, 40, 136, 300])
+def test_cluster_schedule_covers_every_unit_once(S, T):
+    for c in range(1, min(8, S) + 1):
+        for ncl in sorted({1, min(T, 148 // c), min(T, 7)}):
+            seen = np.zeros((T, S), dtype=np.int64)
+            for g in range(ncl):
+                ntiles = (T - g + ncl - 1) // ncl
+                for rank in range(c):
+                    sb0 = ksplit_begin(rank, S, c)
+                    length = ksplit_begin(rank + 1, S, c) - sb0
+                    assert length >= 1  # no idle rank when c <= S
+                    for i in range(ntiles * length):
+                        tile, sb, seg, first, last = unit_info(i, length, sb0, g, ncl)
+                        assert tile % ncl == g and seg == (tile - g) // ncl
+                        assert first == (sb == sb0) and last == (sb == sb0 + length - 1)
+                        seen[tile, sb] += 1
+            assert (seen == 1).all()
+
+
+def test_ksplit_option_values():
+    lib = bf.load_library()
+    for v in range(0, 9):
+        assert lib.busfill_set_option(2, v) == 0
+    assert lib.busfill_set_option(2, 9) == -1
+    assert lib.busfill_set_option(2, -1) == -1
+    assert lib.busfill_set_option(2, 0) == 0

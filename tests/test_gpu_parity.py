@@ -131,10 +131,10 @@ def test_dequant_q4_0_ggml_bit_exact_gguf_golden(golden_dir):
 SHAPES = [
     (1, 128, 256), (3, 256, 512), (8, 640, 1024), (16, 384, 768), (17, 200, 512), (32, 1024, 2048),
     (33, 256, 512), (48, 130, 256), (64, 512, 1536), (65, 256, 512), (130, 384, 768),
-    (1, 128, 16384),   # one tile split over 64 CTAs (deep split-K fix-up)
+    (1, 128, 16384),   # one tile, K split over a cluster of 8
     (8, 256, 8192),
-    (5, 3840, 5120),   # ~4 units per CTA: operand-slot reuse, two segments per CTA
-    (2, 1024, 40960),  # ~9 units per CTA, tiles split over ~18 CTAs
+    (5, 3840, 5120),   # 30 tiles: clusters of 3-4, ~5-7 units per CTA
+    (2, 1024, 40960),  # 8 tiles x 160 units: 20 units per CTA, deep operand-slot reuse
 ]
 
 
@@ -160,6 +160,38 @@ def test_gemm_q4_0_parity(m, n, k):
     cref = orc.gemm_ref(a, orc.dequant_q4_0_planes_f32(wq, ws))
     exact = a.astype(np.float64) @ w16.astype(np.float64).T
     assert_gates(c, cref, exact)
+
+
+# (cluster size, M, N, K): forced K splits, including schedules where every
+# cluster takes several tiles in turn (the reduction buffer is reused)
+KSPLIT_CASES = [
+    (1, 32, 384, 512),
+    (2, 8, 640, 1024),
+    (3, 32, 7680, 768),    # 60 tiles over <= 49 clusters: two tiles per cluster
+    (4, 17, 1280, 1280),   # 5 units over 4 ranks: uneven split
+    (5, 3, 2560, 5120),
+    (8, 5, 3072, 2048),    # 24 tiles over <= 18 clusters
+    (8, 1, 128, 2048),     # one unit per rank
+]
+
+
+@pytest.mark.parametrize("csize,m,n,k", KSPLIT_CASES)
+def test_gemm_forced_ksplit(csize, m, n, k):
+    blocks = orc.gen_q4k(n, k, seed=csize * 11 + m)
+    wq, ws = orc.gen_q4_0(n, k, seed=csize * 13 + m)
+    a = orc.gen_activations(m, k, seed=csize + 7 * m)
+    bf.set_ksplit(csize)
+    try:
+        c = bf.gemm_q4k(cu(blocks), cu(a))
+        c0 = bf.gemm_q4_0(cu(wq), cu(ws), cu(a))
+        check_status()
+    finally:
+        bf.set_ksplit(0)
+    w32 = orc.dequant_q4k_f32(blocks, k)
+    assert_gates(c, orc.gemm_ref(a, w32), a.astype(np.float64) @ w32.astype(np.float64).T)
+    w16 = orc.dequant_q4_0_planes(wq, ws)
+    assert_gates(c0, orc.gemm_ref(a, orc.dequant_q4_0_planes_f32(wq, ws)),
+                 a.astype(np.float64) @ w16.astype(np.float64).T)
 
 
 @pytest.mark.parametrize("m", [1, 8, 32])

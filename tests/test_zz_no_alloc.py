@@ -1,5 +1,5 @@
-"""busfill_gemm_q4k_noalloc: the Q4_K GEMM whose split-K scratch is a static
-array in the library instead of a cudaMalloc'd workspace.
+"""busfill_gemm_q4k_noalloc: the Q4_K GEMM whose device scratch (its error
+words) is a static array in the library instead of a cudaMalloc'd buffer.
 
 Collected last on purpose (file name), so that a run stopping at the first
 failure has run every other test before this one.
@@ -27,9 +27,9 @@ def test_noalloc_rejects_null_pointers_without_device():
 
 @pytest.mark.gpu
 def test_noalloc_matches_gemm_q4k_two_calls_in_a_row():
-    # first: the headline shape, whose row tiles are split over up to five
-    # CTAs (counters and partials in use); second: a shape with more tiles and
-    # a different activation-row count, run right after on the same stream
+    # first: the headline shape (row tiles split along K over a cluster);
+    # second: a shape with more tiles and a different activation-row count,
+    # run right after on the same stream
     cases = [(32, 5120, 5120, 31), (17, 3840, 5120, 32)]
     stream = torch.cuda.current_stream()
     inputs, outs = [], []
@@ -50,17 +50,3 @@ def test_noalloc_matches_gemm_q4k_two_calls_in_a_row():
         assert finite, "non-finite output"
         assert max_abs <= orc.GATE_MAX_ABS, f"max abs diff {max_abs}"
         assert rel <= orc.GATE_REL_L2, f"rel-L2 diff {rel}"
-
-
-@pytest.mark.gpu
-def test_noalloc_rejects_problems_beyond_its_scratch():
-    # N = 65536, K = 4096, M = 32 needs 16 MiB of split-K partials
-    m, n, k = 32, 65536, 4096
-    blocks = torch.zeros((n, k // 256 * 144), dtype=torch.uint8, device=DEV)
-    a = torch.zeros((m, k), dtype=torch.float16, device=DEV)
-    out = torch.full((m, n), 7.0, dtype=torch.float16, device=DEV)
-    with pytest.raises(bf.BusfillError) as e:
-        bf.gemm_q4k_noalloc(blocks, a, out)
-    assert e.value.status == -9
-    torch.cuda.synchronize()
-    assert bool((out == 7.0).all()), "a rejected call wrote to its output"
