@@ -205,7 +205,7 @@ struct DecodeSchedule {
   int nclusters = 1;  // clusters in the grid
 };
 
-// Pick the K split c (1..8) with the shortest estimated weight-streaming time:
+// Pick the K split c (1..max_cluster) with the shortest estimated weight-streaming time:
 // each active CTA moves at most kSmGBs (one SM's TMA rate on 144-byte weight
 // rows, measured on B200) and all of them together at most kHbmGBs; a cluster
 // takes ceil(T / G) tiles of ceil(S / c) units each. Ties go to the smaller c.
@@ -216,8 +216,9 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count) {
   DecodeSchedule best;
   double best_ns = 1e300;
   const int forced = g_force_ksplit.load();
-  for (int c = 1; c <= std::min(8, S); ++c) {
-    if (forced > 0 && forced <= S && c != forced) continue;
+  const int cmax = std::min(max_cluster<NB>(), S);
+  for (int c = 1; c <= cmax; ++c) {
+    if (forced > 0 && forced <= cmax && c != forced) continue;
     const int cap = c == 1 ? sm_count : max_active_clusters<FMT, NB, OutT>(dev, c, sm_count);
     const int ncl = std::min(T, cap);
     if (ncl < 1) continue;

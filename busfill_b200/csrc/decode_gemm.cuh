@@ -10,53 +10,55 @@
 // (one Q4_K super-block, eight Q4_0 blocks), each unit into four 64-value
 // chunks. The tensor core runs swap-AB: the 128 weight rows are the MMA M
 // dimension, read from tensor memory (TMEM); the batch rows (padded to NB)
-// are N, read from shared memory (K-major, 128-byte swizzle).
+// are N, read from shared memory (K-major, 128-byte swizzle). The dequant
+// warps write each unit's fp16 weights into one of three TMEM operand slots;
+// the MMAs of all units of a tile segment accumulate into one fp32 TMEM
+// accumulator, which the epilogue reads once per segment.
 //
-// Synchronisation is per unit, not per chunk: measured on B200, every
-// mbarrier probe on the MMA-issuing warp's path costs 40-75 cycles while an
-// N=32 MMA issues in ~17, so the MMA warp waits once per unit (`ready`),
-// issues the unit's 16 (Q4_K: 17) MMAs back to back and commits once
-// (`udone`), which releases the unit's operand and activation slots and
-// publishes its accumulator. Three unit slots are kept in flight.
+// The per-unit cost is set by barrier latency, not arithmetic: measured on
+// B200, an mbarrier test_wait whose result a warp consumes at once costs it
+// ~175 cycles even when the phase has completed, an arrive ~140, and a warp
+// serialises them. So each dequant warp handles every other unit (two warp
+// groups alternate units, all four chunks each), halving its barrier
+// operations per unit, and the MMA warp tests the next unit's barriers right
+// after issuing the current unit's MMAs, so that test overlaps the issue and
+// it blocks only when the pre-test said "not yet".
 //
 // Warp roles (16 warps, one CTA per SM):
 //   0      weight TMA producer: one 2D box of 128 rows x one unit (18 KB) per
-//          stage into a 6-stage ring. Weights do not depend on earlier kernels,
-//          so this runs before griddepcontrol.wait (programmatic dependent
-//          launch lets it overlap the previous kernel's tail).
+//          stage into a 4- or 6-stage ring; the first ring's worth is issued
+//          before the CTA and cluster set-up. Weights do not depend on earlier
+//          kernels, so none of this waits for griddepcontrol.wait.
 //   1      activation TMA producer: four 64-value x NB-row boxes per unit
-//          (128-byte swizzle); TMEM allocator.
-//   2      activation stage: waits for a unit's activations, computes (Q4_K)
-//          the 32-value sub-block sums Asum, then marks the activations ready.
+//          (128-byte swizzle) into the unit's slot; the copy completes on the
+//          same barrier as the slot's TMEM operands, so the MMA warp waits,
+//          pre-tests and commits one barrier per unit; TMEM allocator.
 //   3      MMA issuer (converged warp, one elected thread issues).
 //   4-11   dequant: thread (warp%4, lane) owns weight row 32*(warp%4)+lane and
 //          writes its fp16 operand into TMEM with tcgen05.st; warp group g =
-//          (warp-4)/4 handles chunks {g, g+2} of every unit.
-//   12-15  epilogue: row 32*(warp%4)+lane, all NB batch columns; prepares the
-//          per-unit scales ahead of time, folds accumulators, flushes.
+//          (warp-4)/4 handles all four chunks of the units i with i%2 == g.
+//   12-15  epilogue: row 32*(warp%4)+lane; once per tile segment it reads the
+//          accumulator and finishes the tile (cluster reduction, C store).
+//   2      idle.
 //
-// Numerics.
+// Numerics (fp32 accumulation of fp16 products in both formats).
 //   Q4_0: operand fp16_rn((q-8)*d), bit-identical to the reference dequant
 //   (kernels/busfill_v0.cu:74-81): the lop3 magic bias 0x6400 gives the exact
 //   fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
-//   Q4_K: w = d*sc*q - dmin*m. Operand P = sc*q, exact in fp16 from one hfma2
-//   ((1024+q)*sc - 1024*sc; high nibbles arrive as 1024+16q and use sc/16 and
-//   64*sc, both exact). Per unit the epilogue adds d * X in fp32. The min
-//   term sum_k A*dmin*m = sum_j (dmin*m_j) * Asum_j is one K=16 MMA per unit:
-//   dmin*m_j (exact in fp32, 17 significant bits) is split into fp16 hi + lo
-//   summing to it exactly, and Asum_j is the fp16 pairwise sum of the 32
-//   activations of sub-block j (the only rounding the Q4_K path adds beyond
-//   fp32 accumulation).
+//   Q4_K: operand q*ds - dm in one hfma2, with ds = fp16_rn(d*sc) and dm =
+//   fp16_rn(dmin*m) per 32-value sub-block and q exact (low nibbles via the
+//   bias 0x6400 = 1024 + q, high nibbles via 0x5400, whose mantissa step is
+//   1/16, = 64 + q). Two fp16 roundings per weight (~3e-4 relative rms); the
+//   bit-exact fp16 dequant is busfill_dequant_q4k.
 //
 // Work split: a tile of 128 weight rows is split along K over the c CTAs of
 // a thread-block cluster (rank k takes units [k*S/c, (k+1)*S/c) of every
 // tile); cluster g of G takes tiles g, g+G, g+2G, ... The host picks c so
-// that the CTAs that stream weights have the most bandwidth each (one SM's
-// TMA engine moves ~57 GB/s of these 144-byte rows, so 120 CTAs stream as
-// fast as 148 at K = N = 5120). At the end of each tile the non-zero ranks
-// write their fp32 partial sums into their own shared memory and signal rank
-// 0, which reads them through distributed shared memory, adds them in rank
-// order (deterministic) and writes C. No global scratch, no atomics.
+// that the CTAs that stream weights have the most bandwidth each. At the end
+// of each tile the non-zero ranks push their fp32 partial sums into rank 0's
+// shared memory (st.async with complete_tx on rank 0's barrier), and rank 0
+// adds them in rank order (deterministic) and writes C. No global scratch, no
+// atomics.
 //
 // Every wait is bounded (ptx.cuh: kWaitTimeoutNs): a kernel that cannot make
 // progress records an error bit and winds down instead of hanging the GPU.
@@ -79,14 +81,10 @@ constexpr int kChunksPerUnit = kUnitK / kChunkK;
 constexpr int kQ4KBlockBytes = 144;
 constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
 constexpr int kQ40ScaleOffset = 16384;
-constexpr int kWStages = 6;
-constexpr int kSlots = 3;            // units in flight between dequant/activations and the MMA
-constexpr int kDStages = 4;          // per-unit row scales prepared ahead by the epilogue
-constexpr int kPrepAhead = 2;        // units the epilogue prepares ahead of its fold
+constexpr int kSlots = 3;            // unit slots (TMEM operands + activations) between the producers and the MMA
 constexpr int kThreads = 512;
 constexpr int kWarpWProducer = 0;
 constexpr int kWarpXProducer = 1;
-constexpr int kWarpXStage = 2;
 constexpr int kWarpMma = 3;
 constexpr int kWarpDequant0 = 4;
 constexpr int kWarpEpilogue0 = 12;
@@ -100,7 +98,6 @@ constexpr unsigned kErrMma = 4u;
 constexpr unsigned kErrDequant = 8u;
 constexpr unsigned kErrEpilogue = 16u;
 constexpr unsigned kErrTeardown = 32u;
-constexpr unsigned kErrXStage = 64u;
 
 struct DecodeParams {
   void* c;              // [M, N] row-major, OutT
@@ -118,37 +115,51 @@ __host__ __device__ __forceinline__ int ksplit_begin(int rank, int S, int csize)
 // TMEM column map (512 columns allocated)
 template <int NB>
 struct DecodeTmem {
-  static constexpr int kX = 0;                           // X[b] at b*NB, b = 0, 1
-  static constexpr int kY = 2 * NB;                      // Y (Q4_K), one buffer
-  static constexpr int kM = kY + NB;                     // (dmin*m) operand, 8 columns per slot
+  static constexpr int kAcc = 0;                         // segment accumulators, b * NB for b = 0, 1
   static constexpr int kA = 128;                         // unit operand slots, 128 columns each
-  static_assert(kM + kSlots * 8 <= kA && kA + kSlots * 128 <= kTmemCols, "TMEM budget");
+  static_assert(2 * NB <= kA && kA + kSlots * 128 <= kTmemCols, "TMEM budget");
 };
+
+// Largest cluster (K split) for a batch tile of NB rows: rank 0 receives the
+// other ranks' [128][NB] fp32 partials in shared memory.
+template <int NB>
+constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
+
+// Weight ring depth: what shared memory leaves next to the activation slots
+// and rank 0's receive buffer. Even, so that stage s is always filled with
+// units of one parity and so waited on by one dequant group in phase order
+// (a group that skipped the other group's phase of a stage could see that
+// stale phase as complete: mbarrier waits only tell parities apart).
+template <int NB>
+constexpr int w_stages() { return NB == 32 ? 6 : 8; }
 
 template <int NB>
 struct DecodeSmem {
   static constexpr int kXChunkBytes = NB * 128;                      // one 64-value activation box
   static constexpr int kXSlotBytes = kChunksPerUnit * kXChunkBytes;  // one unit of activations
   static constexpr int kWOff = 0;
+  static constexpr int kWStages = w_stages<NB>();
+  static_assert(kWStages % 2 == 0, "each weight stage must belong to one dequant group");
   static constexpr int kXOff = kWOff + kWStages * kWStageBytes;
-  static constexpr int kSOff = kXOff + kSlots * kXSlotBytes;         // Asum B tiles, one per slot
-  static constexpr int kDOff = kSOff + kSlots * kXChunkBytes;
-  static constexpr int kRedOff = kDOff + kDStages * kTileRows * 4;   // [128][NB] fp32 partial (cluster reduction)
-  static constexpr int kBarOff = kRedOff + kTileRows * NB * 4;
+  static constexpr int kRedOff = kXOff + kSlots * kXSlotBytes;        // rank 0: [rank-1][128][NB] fp32 partials
+  static constexpr int kRedRankBytes = kTileRows * NB * 4;
+  static constexpr int kBarOff = kRedOff + (max_cluster<NB>() - 1) * kRedRankBytes;
   // barrier slots
   static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
-  static constexpr int bXFull = bWEmpty + kWStages;        // activations landed (TMA tx)
-  static constexpr int bReady = bXFull + kSlots;           // unit operands + activations ready for the MMA
-  static constexpr int bUDone = bReady + kSlots;           // unit's MMAs complete (commit)
-  static constexpr int bAccEmpty = bUDone + kSlots;        // X[b] read by the epilogue
-  static constexpr int bYEmpty = bAccEmpty + 2;
-  static constexpr int bRedFull = bYEmpty + 1;             // rank 0: partials of the other ranks written
+  // unit slot s: operands in TMEM (4 dequant warps) and activations landed
+  // (1 producer arrival + TMA bytes)
+  static constexpr int bReady = bWEmpty + kWStages;
+  static constexpr int bUDone = bReady + kSlots;           // unit's MMAs complete (commit): slot s free
+  static constexpr int bAccFull = bUDone + kSlots;         // segment accumulator b complete (commit)
+  static constexpr int bAccEmpty = bAccFull + 2;           // segment accumulator b read by the epilogue
+  static constexpr int bRedFull = bAccEmpty + 2;           // rank 0: the other ranks' partials landed (tx bytes)
   static constexpr int bRedEmpty = bRedFull + 1;           // rank k > 0: rank 0 has read this rank's partial
   static constexpr int bFinal = bRedEmpty + 1;
   static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
+  static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
 };
 
 // ---------------------------------------------------------------------------
@@ -176,49 +187,27 @@ __device__ __forceinline__ void dequant_q4_0_block(const uint4 b, const __half2 
 
 // Q4_K, one 64-value chunk of a super-block: 32 bytes; byte l holds element l
 // of sub-block 2c (low nibble) and of sub-block 2c+1 (high nibble). Writes
-// P = sc*q exactly: out[0..15] = sub-block 2c, out[16..31] = sub-block 2c+1.
-__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, const __half2 mlo,
-                                                  const __half2 alo, const __half2 mhi, const __half2 ahi,
+// q*ds - dm in one hfma2 per pair: out[0..15] = sub-block 2c (ds_lo, ndm_lo),
+// out[16..31] = sub-block 2c+1 (ds_hi, ndm_hi); ndm = -dm.
+__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, const __half2 ds_lo,
+                                                  const __half2 ndm_lo, const __half2 ds_hi, const __half2 ndm_hi,
                                                   uint32_t* out) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const uint32_t t0 = prmt(w[i], w[i], 0x0100u);  // byte0 = b0, byte2 = b1
     const uint32_t t1 = prmt(w[i], w[i], 0x0302u);  // byte0 = b2, byte2 = b3
-    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024+q, 1024+q}
+    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}: mantissa step 1
     const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
-    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x64006400u);  // {1024+16q, 1024+16q}
-    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x64006400u);
-    out[2 * i] = h2_as_u32(__hfma2(u32_as_h2(l01), mlo, alo));
-    out[2 * i + 1] = h2_as_u32(__hfma2(u32_as_h2(l23), mlo, alo));
-    out[16 + 2 * i] = h2_as_u32(__hfma2(u32_as_h2(h01), mhi, ahi));
-    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(u32_as_h2(h23), mhi, ahi));
+    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}: mantissa step 1/16
+    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
+    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
+    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
+    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
+    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
   }
-}
-
-// two 6-bit values (bytes 2c' and 2c'+1 of `word`) -> exact fp16 pair
-__device__ __forceinline__ __half2 six_bit_pair_to_h2(uint32_t word, int cpair) {
-  const uint32_t sel = cpair ? 0x4342u : 0x4140u;  // {b[2c'], 0x64, b[2c'+1], 0x64}
-  const uint32_t v = prmt(word, 0x64646464u, sel);
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  return __hsub2(u32_as_h2(v), k1024);
-}
-
-// dmin * m (exact in fp32) -> (hi, lo) fp16 with hi + lo == dmin * m exactly
-// for normal-range products (hi = fp16_rn(x); x - hi has <= 6 significant bits)
-__device__ __forceinline__ void split_hi_lo(float x, __half& hi, __half& lo) {
-  hi = __float2half_rn(x);
-  lo = __float2half_rn(x - __half2float(hi));
-}
-
-// packed fp32 pair FMA (sm_100): d = a*b + c
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(r)
-      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
-        "l"(*reinterpret_cast<unsigned long long*>(&c)));
-  return *reinterpret_cast<float2*>(&r);
 }
 
 template <typename OutT>
@@ -257,8 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using TM = DecodeTmem<NB>;
   constexpr bool kQ4K = (FMT == WFmt::Q4K);
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
-  // ready[s] arrivals: 8 dequant warps + the activation-stage warp (+ 4 epilogue warps for Q4_K)
-  constexpr uint32_t kReadyCount = kQ4K ? 13u : 9u;
+  constexpr int kWStages = L::kWStages;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
@@ -266,8 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sbase = smem_u32(smem);
   const uint32_t bar0 = sbase + L::kBarOff;
   auto BAR = [&](int slot) { return bar0 + 8u * (uint32_t)slot; };
-  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base, [1] last-arriver flag
-  float* dring = reinterpret_cast<float*>(smem + L::kDOff);
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);  // [0] tmem base
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -297,31 +284,51 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     return ok;
   };
-  // unit i's slot is free once unit i - kSlots has completed its MMAs
-  auto wait_slot_free = [&](int i) -> bool {
-    if (i < kSlots) return ok;
-    return warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1);
-  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(BAR(L::bWFull + s), 1);
-      mbar_init(BAR(L::bWEmpty + s), kQ4K ? 12 : 8);   // dequant warps (+ epilogue warps reading scales)
+      mbar_init(BAR(L::bWEmpty + s), 4);   // the 4 dequant warps of the unit's group
     }
     for (int s = 0; s < kSlots; ++s) {
-      mbar_init(BAR(L::bXFull + s), 1);
-      mbar_init(BAR(L::bReady + s), kReadyCount);
+      mbar_init(BAR(L::bReady + s), 5);    // the unit's 4 dequant warps + the activation producer (+ TMA bytes)
       mbar_init(BAR(L::bUDone + s), 1);
     }
-    for (int b = 0; b < 2; ++b) mbar_init(BAR(L::bAccEmpty + b), 4);
-    mbar_init(BAR(L::bYEmpty), 4);
-    mbar_init(BAR(L::bRedFull), csize > 1 ? 4u * (uint32_t)(csize - 1) : 1u);   // 4 epilogue warps per other rank
-    mbar_init(BAR(L::bRedEmpty), 4);                                             // rank 0's 4 epilogue warps
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR(L::bAccFull + b), 1);
+      mbar_init(BAR(L::bAccEmpty + b), 4); // the 4 epilogue warps
+    }
+    mbar_init(BAR(L::bRedFull), 1);    // rank 0's expect_tx; the other ranks' st.async bytes complete it
+    mbar_init(BAR(L::bRedEmpty), 4);   // rank 0's 4 epilogue warps
     mbar_init(BAR(L::bFinal), 1);
     fence_mbar_init();
     tma_prefetch_desc(&tmap_w);
     if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
     tma_prefetch_desc(&tmap_a);
+  }
+  // weight TMA for unit i into ring stage i % kWStages (the stage must be free)
+  auto issue_w = [&](int i) {
+    const int s = i % kWStages;
+    const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
+    const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
+    if (elect_one()) {
+      mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
+      if constexpr (kQ4K) {
+        tma_load_2d(dst, &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+      } else {
+        tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+        tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, ui.sb * 8, ui.tile * kTileRows, BAR(L::bWFull + s),
+                    kPolicyEvictFirst);
+      }
+    }
+    __syncwarp();
+  };
+  // The first ring's worth of weights needs nothing but the barriers thread 0
+  // just initialised: start streaming before the CTA- and cluster-wide set-up.
+  const int w_early = nunits < kWStages ? nunits : kWStages;
+  if (warp == kWarpWProducer) {
+    __syncwarp();
+    for (int i = 0; i < w_early; ++i) issue_w(i);
   }
   if (warp == kWarpXProducer) {
     tmem_alloc(sbase + L::kMiscOff, kTmemCols);
@@ -340,24 +347,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == kWarpWProducer) {
     // ---------------- weight producer ----------------
-    int issued = 0;
-    for (int i = 0; i < nunits; ++i) {
-      const int s = i % kWStages;
-      if (!warp_wait(BAR(L::bWEmpty + s), ((i / kWStages) & 1) ^ 1)) break;
-      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
-      const int tile = ui.tile, sb = ui.sb;
-      const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
-      if (elect_one()) {
-        mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
-        if constexpr (kQ4K) {
-          tma_load_2d(dst, &tmap_w, sb * kQ4KBlockBytes, tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
-        } else {
-          tma_load_2d(dst, &tmap_w, sb * 128, tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
-          tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, sb * 8, tile * kTileRows, BAR(L::bWFull + s),
-                      kPolicyEvictFirst);
-        }
-      }
-      __syncwarp();
+    int issued = w_early;
+    for (int i = w_early; i < nunits; ++i) {
+      if (!warp_wait(BAR(L::bWEmpty + i % kWStages), ((i / kWStages) & 1) ^ 1)) break;
+      issue_w(i);
       issued = i + 1;
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrWeightProducer);
@@ -373,159 +366,124 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
     int issued = 0;
     for (int i = 0; i < nunits; ++i) {
-      if (!wait_slot_free(i)) break;
       const int s = i % kSlots;
+      // slot s is free once the MMAs of unit i - kSlots have completed
+      if (i >= kSlots && !warp_wait(BAR(L::bUDone + s), ((i / kSlots) & 1) ^ 1)) break;
       const int sb = sb0 + i % len;
       if (elect_one()) {
-        mbar_arrive_expect_tx(BAR(L::bXFull + s), L::kXSlotBytes);
+        mbar_arrive_expect_tx(BAR(L::bReady + s), L::kXSlotBytes);
 #pragma unroll
         for (int cc = 0; cc < kChunksPerUnit; ++cc)
           tma_load_2d(sbase + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes, &tmap_a,
-                      sb * kUnitK + cc * kChunkK, 0, BAR(L::bXFull + s), kPolicyEvictLast);
+                      sb * kUnitK + cc * kChunkK, 0, BAR(L::bReady + s), kPolicyEvictLast);
       }
       __syncwarp();
       issued = i + 1;
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrActProducer);
+    // never leave the CTA with copies in flight: they complete on bReady (whose
+    // phase also needs the unit's dequant warps)
     ok = true;
     for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i)
-      if (!warp_wait(BAR(L::bXFull + i % kSlots), (i / kSlots) & 1)) {
+      if (!warp_wait(BAR(L::bReady + i % kSlots), (i / kSlots) & 1)) {
         if (lane == 0) atomicOr(p.error, kErrTeardown);
         break;
       }
-  } else if (warp == kWarpXStage) {
-    // ---------------- activation stage (+ Q4_K sub-block sums) ----------------
-    const int b = lane;                  // batch row (lanes >= NB idle)
-    for (int i = 0; i < nunits; ++i) {
-      diag_unit = i;
-      const int s = i % kSlots;
-      if (!warp_wait(BAR(L::bXFull + s), (i / kSlots) & 1)) break;
-      if constexpr (kQ4K) {
-        // Asum[b][j], j = 0..7: fp16 pairwise sums of 32 activations. The B
-        // tile row b holds k 0..7 = Asum[b][0..7] and k 8..15 = the same again.
-        uint32_t sums[4];
-#pragma unroll
-        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
-          __half s2[2] = {__float2half(0.f), __float2half(0.f)};
-          if (b < NB) {
-            const uint8_t* row =
-                smem + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes + (b >> 3) * 1024 + (b & 7) * 128;
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {   // sub-block 2cc+h = 16-byte chunks 4h..4h+3
-              uint4 v[4];
-#pragma unroll
-              for (int c = 0; c < 4; ++c)
-                v[c] = *reinterpret_cast<const uint4*>(row + ((((uint32_t)(4 * h + c)) ^ (uint32_t)(b & 7)) << 4));
-              __half2 a0 = __hadd2(u32_as_h2(v[0].x), u32_as_h2(v[0].y));
-              __half2 a1 = __hadd2(u32_as_h2(v[0].z), u32_as_h2(v[0].w));
-              __half2 a2 = __hadd2(u32_as_h2(v[1].x), u32_as_h2(v[1].y));
-              __half2 a3 = __hadd2(u32_as_h2(v[1].z), u32_as_h2(v[1].w));
-              __half2 a4 = __hadd2(u32_as_h2(v[2].x), u32_as_h2(v[2].y));
-              __half2 a5 = __hadd2(u32_as_h2(v[2].z), u32_as_h2(v[2].w));
-              __half2 a6 = __hadd2(u32_as_h2(v[3].x), u32_as_h2(v[3].y));
-              __half2 a7 = __hadd2(u32_as_h2(v[3].z), u32_as_h2(v[3].w));
-              a0 = __hadd2(a0, a1); a2 = __hadd2(a2, a3); a4 = __hadd2(a4, a5); a6 = __hadd2(a6, a7);
-              a0 = __hadd2(a0, a2); a4 = __hadd2(a4, a6);
-              a0 = __hadd2(a0, a4);
-              s2[h] = __hadd(__low2half(a0), __high2half(a0));
-            }
-          }
-          sums[cc] = h2_as_u32(__halves2half2(s2[0], s2[1]));
-        }
-        if (b < NB) {
-          uint8_t* row = smem + L::kSOff + s * L::kXChunkBytes + (b >> 3) * 1024 + (b & 7) * 128;
-          const uint4 v = make_uint4(sums[0], sums[1], sums[2], sums[3]);
-          *reinterpret_cast<uint4*>(row + ((0u ^ (uint32_t)(b & 7)) << 4)) = v;
-          *reinterpret_cast<uint4*>(row + ((1u ^ (uint32_t)(b & 7)) << 4)) = v;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(L::bReady + s));
-    }
-    if (!ok && lane == 0) atomicOr(p.error, kErrXStage);
   } else if (warp == kWarpMma) {
     // ---------------- MMA issuer (converged warp, one elected thread issues) ----------------
-    int yuses = 0;         // Q4_K segments started (Y buffer uses)
+    // Lean loop: one wait (pre-tested during the previous unit), 16 MMAs, one
+    // commit; unit bookkeeping kept incrementally.
+    const uint64_t bdesc0 = make_sdesc_sw128(sbase + L::kXOff);  // + (byte offset >> 4) per MMA
+    int s = 0, seg = 0, j = 0;
+    uint32_t ph = 0;          // parity of unit i's phase on its slot barriers: (i / kSlots) & 1
+    bool pre = false;         // unit i's slot already seen ready
     for (int i = 0; i < nunits; ++i) {
       diag_unit = i;
-      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
-      const int s = i % kSlots;
-      // every unit accumulates into X[i & 1]; the epilogue folds it into
-      // registers, so the MMA is never more than two units ahead of it
-      if (!warp_wait(BAR(L::bAccEmpty + (i & 1)), ((i >> 1) & 1) ^ 1)) break;
-      if (kQ4K && ui.seg_first) {
-        if (!warp_wait(BAR(L::bYEmpty), (yuses & 1) ^ 1)) break;
-        ++yuses;
-      }
-      if (!warp_wait(BAR(L::bReady + s), (i / kSlots) & 1)) break;
+      const int buf = seg & 1;
+      // a segment's accumulator is free once the epilogue has read segment seg - 2
+      if (j == 0 && seg >= 2 && !warp_wait(BAR(L::bAccEmpty + buf), ((seg >> 1) & 1) ^ 1)) break;
+      if (!pre && !warp_wait(BAR(L::bReady + s), ph)) break;
       tc_fence_after();
-      const uint32_t d_x = tmem + TM::kX + (uint32_t)((i & 1) * NB);
-      const uint32_t a_t = tmem + TM::kA + s * 128;
-      const uint32_t b_s = sbase + L::kXOff + s * L::kXSlotBytes;
       if (elect_one()) {
+        const uint32_t d_acc = tmem + TM::kAcc + (uint32_t)(buf * NB);
+        const uint32_t a_t = tmem + TM::kA + (uint32_t)(s * 128);
+        const uint64_t bd = bdesc0 + (uint64_t)((s * L::kXSlotBytes) >> 4);
 #pragma unroll
         for (int cc = 0; cc < kChunksPerUnit; ++cc)
 #pragma unroll
           for (int t = 0; t < 4; ++t)
-            mma_f16_ts(d_x, a_t + cc * 32 + 8 * t, make_sdesc_sw128(b_s + cc * L::kXChunkBytes + 32 * t), kIdesc,
-                       (cc == 0 && t == 0) ? 0u : 1u);
-        if constexpr (kQ4K)
-          mma_f16_ts(tmem + TM::kY, tmem + TM::kM + s * 8, make_sdesc_sw128(sbase + L::kSOff + s * L::kXChunkBytes),
-                     kIdesc, ui.seg_first ? 0u : 1u);
-        tc_commit(BAR(L::bUDone + s));  // frees slot s; publishes X (and Y) for this unit
+            mma_f16_ts(d_acc, a_t + cc * 32 + 8 * t, bd + (uint64_t)((cc * L::kXChunkBytes + 32 * t) >> 4), kIdesc,
+                       (j == 0 && cc == 0 && t == 0) ? 0u : 1u);
+        tc_commit(BAR(L::bUDone + s));                          // slot s free
+        if (j == len - 1) tc_commit(BAR(L::bAccFull + buf));    // segment accumulator complete
       }
       __syncwarp();
+      // next unit; pre-test its slot while this unit's MMAs run
+      if (++s == kSlots) { s = 0; ph ^= 1u; }
+      if (++j == len) { j = 0; ++seg; }
+      pre = (i + 1 < nunits) && __all_sync(0xffffffffu, mbar_test_wait(BAR(L::bReady + s), ph));
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrMma);
     if (elect_one()) tc_commit(BAR(L::bFinal));  // fires once every MMA issued above has completed
     __syncwarp();
-  } else if (warp < kWarpEpilogue0) {
+  } else if (warp >= kWarpDequant0 && warp < kWarpEpilogue0) {
     // ---------------- dequant ----------------
     const int q = warp & 3;                        // TMEM lane quarter this warp may touch
-    const int g = (warp - kWarpDequant0) >> 2;     // group: chunks {g, g+2}
+    const int grp = (warp - kWarpDequant0) >> 2;   // group: units i with i % 2 == grp
     const int r = q * 32 + lane;                   // weight row within the tile
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
-    for (int i = 0; i < nunits; ++i) {
+    for (int i = grp; i < nunits; i += 2) {
       diag_unit = i;
       const int ws = i % kWStages;
       if (!warp_wait(BAR(L::bWFull + ws), (i / kWStages) & 1)) break;
-      if (!wait_slot_free(i)) break;
+      // operand slot i % kSlots is free once the MMAs of unit i - kSlots completed
+      if (i >= kSlots && !warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       tc_fence_after();
       const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
       const uint32_t a_slot = tmem + lane_off + TM::kA + (i % kSlots) * 128;
-      uint32_t sc_lo = 0, sc_hi = 0;
       if constexpr (kQ4K) {
+        // this row's block header: d, dmin and the 6-bit scales/mins of its
+        // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
+        // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7
         const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
-        sc_lo = hdr.y & 0x3F3F3F3Fu;
-        sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-      }
+        const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+        const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
+        const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+        const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+        const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
 #pragma unroll 1
-      for (int k2 = 0; k2 < 2; ++k2) {
-        const int cc = g + 2 * k2;
-        uint32_t P[32];
-        if constexpr (kQ4K) {
+        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+          // chunk cc covers sub-blocks 2cc, 2cc+1: bytes 2(cc&1), 2(cc&1)+1 of the
+          // _lo words (cc < 2) or of the _hi words (cc >= 2)
+          const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
+          const uint32_t mw = cc < 2 ? m_lo : m_hi;
+          const int sh = 16 * (cc & 1);
+          const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
+          const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
+          const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
+          const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
           const uint8_t* qs = stage + r * kQ4KBlockBytes + 16 + cc * 32;
           const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
           const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-          const __half2 S2 = six_bit_pair_to_h2(cc < 2 ? sc_lo : sc_hi, cc & 1);  // {sc[2cc], sc[2cc+1]}
-          const __half2 mlo = __low2half2(S2);
-          const __half2 alo = __hmul2(mlo, __float2half2_rn(-1024.f));
-          const __half2 shi = __high2half2(S2);
-          const __half2 mhi = __hmul2(shi, __float2half2_rn(0.0625f));
-          const __half2 ahi = __hmul2(shi, __float2half2_rn(-64.f));
-          dequant_q4k_chunk(q0, q1, mlo, alo, mhi, ahi, P);
-        } else {
-          const uint8_t* wrow = stage + r * 128;
-          const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
+          uint32_t P[32];
+          dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
+          tmem_st_x32(a_slot + cc * 32, P);
+        }
+      } else {
+        const uint8_t* wrow = stage + r * 128;
+        const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
+        const uint4 dd = *reinterpret_cast<const uint4*>(stage + kQ40ScaleOffset + r * 16);  // 8 block scales
+#pragma unroll 1
+        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+          uint32_t P[32];
           const uint4 b0 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc)) ^ sw) << 4));
           const uint4 b1 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc + 1)) ^ sw) << 4));
-          const uint32_t dd = *reinterpret_cast<const uint32_t*>(stage + kQ40ScaleOffset + r * 16 + cc * 4);
-          const __half2 d01 = u32_as_h2(dd);
+          const __half2 d01 = u32_as_h2(cc == 0 ? dd.x : cc == 1 ? dd.y : cc == 2 ? dd.z : dd.w);
           dequant_q4_0_block(b0, __low2half2(d01), P);
           dequant_q4_0_block(b1, __high2half2(d01), P + 16);
+          tmem_st_x32(a_slot + cc * 32, P);
         }
-        tmem_st_x32(a_slot + cc * 32, P);
       }
       tc_wait_st();
       tc_fence_before();
@@ -536,102 +494,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrDequant);
-  } else {
+  } else if (warp >= kWarpEpilogue0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;
     const int r = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     float acc[NB];
-#pragma unroll
-    for (int t = 0; t < NB; ++t) acc[t] = 0.f;
-
-    // Q4_K: read unit i's scales for this row while its weight stage is
-    // resident; keep d for the fold and store dmin*m (split hi + lo) as the
-    // min-term operand in TMEM slot i % kSlots.
-    auto prep = [&](int i) {
-      const int ws = i % kWStages;
-      if (!warp_wait(BAR(L::bWFull + ws), (i / kWStages) & 1)) return;
-      const uint4 hdr = *reinterpret_cast<const uint4*>(smem + L::kWOff + ws * kWStageBytes + r * kQ4KBlockBytes);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(L::bWEmpty + ws));
-      dring[(i % kDStages) * kTileRows + r] = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
-      const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
-      const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-      const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-      uint32_t mv[8];
-#pragma unroll
-      for (int jp = 0; jp < 4; ++jp) {
-        const uint32_t word = jp < 2 ? m_lo : m_hi;
-        const int sh = 16 * (jp & 1);
-        __half h0, l0, h1, l1;
-        split_hi_lo(dmin * (float)((word >> sh) & 0xFFu), h0, l0);
-        split_hi_lo(dmin * (float)((word >> (sh + 8)) & 0xFFu), h1, l1);
-        mv[jp] = h2_as_u32(__halves2half2(h0, h1));
-        mv[4 + jp] = h2_as_u32(__halves2half2(l0, l1));
-      }
-      if (!wait_slot_free(i)) return;
-      tc_fence_after();
-      tmem_st_x8(tmem + lane_off + TM::kM + (i % kSlots) * 8, mv);
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(L::bReady + i % kSlots));
-    };
-
-    // acc += scale * X[buf]; the unit's MMAs (udone) must have completed
-    auto fold_x = [&](int i, int buf, float scale) {
-      if (!warp_wait(BAR(L::bUDone + i % kSlots), (i / kSlots) & 1)) return;
-      tc_fence_after();
-      const float2 sc2 = make_float2(scale, scale);
-#pragma unroll
-      for (int h = 0; h < NB; h += 16) {
-        uint32_t x[16];
-        tmem_ld_x16(tmem + lane_off + TM::kX + (uint32_t)(buf * NB + h), x);
-        tc_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 16; t += 2) {
-          const float2 v = ffma2(sc2, make_float2(__uint_as_float(x[t]), __uint_as_float(x[t + 1])),
-                                 make_float2(acc[h + t], acc[h + t + 1]));
-          acc[h + t] = v.x;
-          acc[h + t + 1] = v.y;
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
-    };
 
     // Finish tile `tile` (this CTA's segment `seg`). One CTA per tile: write C.
-    // Otherwise ranks k > 0 leave their partial in their own shared memory
-    // ([row][NB] fp32, 16-byte chunks swizzled by row) and signal rank 0; rank 0
-    // adds them in rank order through distributed shared memory and writes C.
+    // Otherwise ranks k > 0 push their fp32 partial into rank 0's shared
+    // memory with st.async, whose bytes complete rank 0's bRedFull barrier (no
+    // fence, no separate signal: every release or remote round trip costs
+    // ~0.5 us on B200); rank 0 adds the partials in rank order and writes C.
+    // Receive layout: [rank-1][row][NB] fp32, 16-byte chunks swizzled by row.
     auto flush = [&](int tile, int seg) {
       const int n = tile * kTileRows + r;
       OutT* C = reinterpret_cast<OutT*>(p.c);
       constexpr int kChunks = NB / 4;
-      const uint32_t my_row = sbase + L::kRedOff + (uint32_t)(r * NB * 4);
       const int swz = r & (kChunks - 1);
       if (csize > 1 && crank != 0) {
-        // our buffer is free once rank 0 has read the previous segment's partial
+        // rank 0's buffer is free once it has read the previous segment
         if (seg > 0) warp_wait(BAR(L::bRedEmpty), (uint32_t)((seg - 1) & 1), true);
+        const uint32_t row = sbase + L::kRedOff + (uint32_t)((crank - 1) * L::kRedRankBytes + r * NB * 4);
+        const uint32_t dst = mapa_shared(row, 0);
+        const uint32_t dst_bar = mapa_shared(BAR(L::bRedFull), 0);
 #pragma unroll
-        for (int j = 0; j < kChunks; ++j) {
-          const uint32_t a = my_row + (uint32_t)((j ^ swz) << 4);
-          asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(acc[4 * j]), "f"(acc[4 * j + 1]),
-                       "f"(acc[4 * j + 2]), "f"(acc[4 * j + 3])
-                       : "memory");
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(BAR(L::bRedFull), 0));
+        for (int j = 0; j < kChunks; ++j)
+          st_async_f4(dst + (uint32_t)((j ^ swz) << 4), acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3],
+                      dst_bar);
         return;
       }
       if (csize > 1) {
-        warp_wait(BAR(L::bRedFull), (uint32_t)(seg & 1), true);
+        if (warp == kWarpEpilogue0 && lane == 0)
+          mbar_arrive_expect_tx(BAR(L::bRedFull), (uint32_t)((csize - 1) * L::kRedRankBytes));
+        warp_wait(BAR(L::bRedFull), (uint32_t)(seg & 1));
         for (int k = 1; k < csize; ++k) {
-          const uint32_t src = mapa_shared(my_row, (uint32_t)k);
+          const uint8_t* row = smem + L::kRedOff + (k - 1) * L::kRedRankBytes + r * NB * 4;
           float4 v[kChunks];
 #pragma unroll
-          for (int j = 0; j < kChunks; ++j) v[j] = ld_dsmem_f4(src + (uint32_t)((j ^ swz) << 4));
+          for (int j = 0; j < kChunks; ++j) v[j] = *reinterpret_cast<const float4*>(row + ((j ^ swz) << 4));
 #pragma unroll
           for (int j = 0; j < kChunks; ++j) {
             acc[4 * j] += v[j].x;
@@ -640,9 +541,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[4 * j + 3] += v[j].w;
           }
         }
-        __syncwarp();
-        if (lane == 0)
-          for (int k = 1; k < csize; ++k) mbar_arrive_remote(mapa_shared(BAR(L::bRedEmpty), (uint32_t)k));
+        if (seg + 1 < ntiles) {
+          // let the other ranks overwrite our buffer with their next partial
+          __syncwarp();
+          if (lane == 0)
+            for (int k = 1; k < csize; ++k) mbar_arrive_remote(mapa_shared(BAR(L::bRedEmpty), (uint32_t)k));
+        }
       }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
       if (ok && n < p.N) {
@@ -652,40 +556,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     };
 
-    if constexpr (kQ4K) {
-      for (int i = 0; i < nunits && i < kPrepAhead; ++i) prep(i);
-    }
-    for (int i = 0; i < nunits; ++i) {
-      diag_unit = i;
-      const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
-      // Every unit is folded, in order: a waiter on a parity barrier must not
-      // skip phases (a wait for phase n+1 posted before phase n completed
-      // would see the stale parity as complete).
-      if constexpr (kQ4K) {
-        if (i + kPrepAhead < nunits) prep(i + kPrepAhead);
-        fold_x(i, i & 1, dring[(i % kDStages) * kTileRows + r]);
-        if (ui.seg_last && ok) {
-          // Y of this segment is complete: its last MMA was committed with unit i
+    for (int seg = 0; seg < ntiles; ++seg) {
+      diag_unit = seg * len + len - 1;
+      const int buf = seg & 1;
+      if (warp_wait(BAR(L::bAccFull + buf), (uint32_t)((seg >> 1) & 1))) {
+        tc_fence_after();
 #pragma unroll
-          for (int h = 0; h < NB; h += 16) {
-            uint32_t y[16];
-            tmem_ld_x16(tmem + lane_off + TM::kY + h, y);
-            tc_wait_ld();
+        for (int h = 0; h < NB; h += 16) {
+          uint32_t x[16];
+          tmem_ld_x16(tmem + lane_off + TM::kAcc + (uint32_t)(buf * NB + h), x);
+          tc_wait_ld();
 #pragma unroll
-            for (int t = 0; t < 16; ++t) acc[h + t] -= __uint_as_float(y[t]);
-          }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(BAR(L::bYEmpty));
+          for (int t = 0; t < 16; ++t) acc[h + t] = __uint_as_float(x[t]);
         }
       } else {
-        fold_x(i, i & 1, 1.0f);
-      }
-      if (ui.seg_last) {
-        flush(ui.tile, ui.seg);
 #pragma unroll
         for (int t = 0; t < NB; ++t) acc[t] = 0.f;
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
+      flush(g + seg * p.nclusters, seg);
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrEpilogue);
   }

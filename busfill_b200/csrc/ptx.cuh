@@ -153,13 +153,15 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity)
     if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
   }
 }
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t cluster_addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(cluster_addr)
+// Asynchronous 16-byte store into another CTA's shared memory that counts its
+// bytes against that CTA's mbarrier (complete_tx): the receiver's wait on the
+// barrier phase makes the data visible, with no fence on the sender.
+__device__ __forceinline__ void st_async_f4(uint32_t cluster_addr, float a, float b, float c, float d,
+                                            uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
                : "memory");
-  return v;
 }
 // all threads of all CTAs of the cluster (converged warps)
 __device__ __forceinline__ void cluster_sync_all() {

@@ -121,17 +121,41 @@ def test_q4_0_block_chain_column_order_is_natural():
     assert [v for pair in cols for v in pair] == [float(v) for v in nib]
 
 
-def test_q4k_chunk_chain_gives_exact_sc_times_q():
-    # lo: hfma2(1024+q, sc, -1024*sc) == sc*q ; hi: hfma2(1024+16q, sc/16, -64*sc) == sc*q
-    for sc in range(64):
-        s16 = np.float16(sc)
-        for q in range(16):
-            lo = hfma(np.float16(1024 + q), s16, np.float16(-1024.0 * sc))
-            hi = hfma(np.float16(1024 + 16 * q), np.float16(sc / 16.0), np.float16(-64.0 * sc))
-            assert float(lo) == sc * q and float(hi) == sc * q
-            # the constants themselves are exact fp16 values
-            assert float(np.float16(-1024.0 * sc)) == -1024.0 * sc
-            assert float(np.float16(sc / 16.0)) == sc / 16.0
+def test_q4k_nibble_bias_is_exact():
+    # low nibble: (b & 0x0F) | 0x6400 == 1024 + q (mantissa step 1);
+    # high nibble: (b & 0xF0) | 0x5400 == 64 + q (0x5400 = 64.0, mantissa step 1/16)
+    for byte in range(256):
+        lo = np.uint16((byte & 0x0F) | 0x6400).view(np.float16)
+        hi = np.uint16((byte & 0xF0) | 0x5400).view(np.float16)
+        assert float(lo) == 1024 + (byte & 15)
+        assert float(hi) == 64 + (byte >> 4)
+        assert float(np.float16(float(lo) - 1024)) == byte & 15   # hsub2 exact
+        assert float(np.float16(float(hi) - 64)) == byte >> 4
+
+
+def q4k_operand_chain(d16, dmin16, sc, m, q):
+    """Bit-level model of the GEMM's Q4_K operand: hfma2(q, ds, -dm) with
+    ds = fp16_rn(fp32(d)*sc), dm = fp16_rn(fp32(dmin)*m) (decode_gemm.cuh)."""
+    ds = (np.float32(d16) * np.float32(sc)).astype(np.float16)
+    ndm = (-(np.float32(dmin16) * np.float32(m))).astype(np.float16)
+    return hfma(np.float16(q), ds, ndm)
+
+
+def test_q4k_operand_chain_is_within_two_roundings_of_oracle():
+    rng = np.random.default_rng(7)
+    blocks = orc.gen_q4k(64, 2048, seed=7)
+    d16, dmin16, sc, m, q = orc.split_q4k_blocks(blocks, 2048)
+    n, s = d16.shape
+    qf = q.reshape(n, s, 8, 32)
+    got = q4k_operand_chain(d16[:, :, None, None], dmin16[:, :, None, None], sc[:, :, :, None], m[:, :, :, None], qf)
+    w32 = orc.dequant_q4k_f32(blocks, 2048).reshape(n, s, 8, 32).astype(np.float64)
+    # |err| <= ulp(ds)/2 * q + ulp(dm)/2 + ulp(w)/2, each ulp <= 2^-10 * |value|
+    ds = np.abs(d16.astype(np.float64)[:, :, None, None] * sc[:, :, :, None])
+    dm = np.abs(dmin16.astype(np.float64)[:, :, None, None] * m[:, :, :, None])
+    bound = 2.0 ** -11 * (ds * qf + dm + np.abs(w32)) + 1e-7
+    assert np.all(np.abs(got.astype(np.float64) - w32) <= bound)
+    rel = np.linalg.norm(got.astype(np.float64) - w32) / np.linalg.norm(w32)
+    assert rel < 5e-4, rel
 
 
 def test_q4k_chunk_extraction_and_order():
@@ -146,8 +170,8 @@ def test_q4k_chunk_extraction_and_order():
         for t in (t0, t1):
             a, b = h2(lop3_and_or(t, 0x000F000F, 0x64006400))
             lo_cols += [float(a) - 1024, float(b) - 1024]
-            a, b = h2(lop3_and_or(t, 0x00F000F0, 0x64006400))
-            hi_cols += [(float(a) - 1024) / 16, (float(b) - 1024) / 16]
+            a, b = h2(lop3_and_or(t, 0x00F000F0, 0x54005400))
+            hi_cols += [float(a) - 64, float(b) - 64]
     assert lo_cols == [float(v & 15) for v in chunk]      # sub-block 2c, elements 0..31
     assert hi_cols == [float(v >> 4) for v in chunk]      # sub-block 2c+1
 
@@ -168,11 +192,18 @@ def test_q4k_scale_words_match_oracle_unpack():
         word_m = m_lo if j < 4 else m_hi
         assert np.array_equal((word_sc >> (8 * (j % 4))) & 0xFF, sc[:, j])
         assert np.array_equal((word_m >> (8 * (j % 4))) & 0xFF, m[:, j])
-    # six_bit_pair_to_h2: prmt(word, 0x64646464, 0x4140 / 0x4342) -> {1024+v0, 1024+v1}
-    for cpair, sel in ((0, 0x4140), (1, 0x4342)):
-        a, b = h2(prmt(sc_lo, np.uint32(0x64646464), sel))
-        assert np.array_equal(a.astype(np.float64) - 1024, sc[:, 2 * cpair].astype(np.float64))
-        assert np.array_equal(b.astype(np.float64) - 1024, sc[:, 2 * cpair + 1].astype(np.float64))
+    # the dequant warp of group grp reads bytes 2grp, 2grp+1 of the _lo words for
+    # chunk grp and of the _hi words for chunk grp + 2 (sub-blocks 2cc, 2cc+1)
+    for grp in range(2):
+        for k2 in range(2):
+            cc = grp + 2 * k2
+            word_sc = sc_hi if k2 else sc_lo
+            word_m = m_hi if k2 else m_lo
+            sh = 16 * grp
+            assert np.array_equal((word_sc >> sh) & 0xFF, sc[:, 2 * cc])
+            assert np.array_equal((word_sc >> (sh + 8)) & 0xFF, sc[:, 2 * cc + 1])
+            assert np.array_equal((word_m >> sh) & 0xFF, m[:, 2 * cc])
+            assert np.array_equal((word_m >> (sh + 8)) & 0xFF, m[:, 2 * cc + 1])
 
 
 # ---------------------------------------------------------------------------
