@@ -161,6 +161,7 @@ def run_busfill(args):
     import torch.distributed as dist
 
     import busfill_b200 as bf
+    from busfill_b200 import tp
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -176,9 +177,10 @@ def run_busfill(args):
     hbm_peak, tc_peak, peak_src = measured_peaks()
 
     M, N, K = args.m, args.n, args.k
-    if N % (world * 128) and world > 1:
-        raise SystemExit(f"N={N} must split into multiples of 128 rows over {world} ranks")
-    n_loc = N // world
+    row0, row1 = tp.shard_rows(N, world, rank)    # this rank's weight rows (whole 128-row tiles)
+    n_loc = row1 - row0
+    if n_loc == 0:
+        raise SystemExit(f"N={N} leaves rank {rank} of {world} without rows")
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + rank)
     wbytes = n_loc * K * 18 // 32
@@ -191,17 +193,18 @@ def run_busfill(args):
         weights = [(wq, ws)] + [(wq.clone(), ws.clone()) for _ in range(R - 1)]
     a = torch.randn((M, K), device=dev, generator=gen).half()
     c_loc = torch.empty((M, n_loc), dtype=torch.float16, device=dev)
-    gathered = torch.empty((world, M, n_loc), dtype=torch.float16, device=dev) if world > 1 else None
     c_full = torch.empty((M, N), dtype=torch.float16, device=dev) if world > 1 else None
 
     def gemm(w, stream):
-        if args.fmt == "q4k":
-            bf.gemm_q4k(w, a, out=c_loc, stream=stream)
+        if world == 1:
+            if args.fmt == "q4k":
+                bf.gemm_q4k(w, a, out=c_loc, stream=stream)
+            else:
+                bf.gemm_q4_0(w[0], w[1], a, out=c_loc, stream=stream)
+        elif args.fmt == "q4k":     # N-split: local rows through the C ABI, NCCL all-gather of the slices
+            tp.gemm_q4k_tp(w, a, N, out=c_full, local_out=c_loc)
         else:
-            bf.gemm_q4_0(w[0], w[1], a, out=c_loc, stream=stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered.view(world * M, n_loc), c_loc)
-            c_full.view(M, world, n_loc).copy_(gathered.permute(1, 0, 2))
+            tp.gemm_q4_0_tp(w[0], w[1], a, N, out=c_full, local_out=c_loc)
 
     def one_step(stream):
         for w in weights:
@@ -307,7 +310,7 @@ def run_busfill(args):
         out["e2e"] = e2e(torch, bf, dev, weights, a, args, max(10, steps // 10))
         out["cpu_baseline"] = cpu_baseline(args)
     elif world > 1:
-        out["e2e"] = None
+        out["e2e"] = e2e_tp(torch, bf, tp, dev, weights, a, args, N, max(10, steps // 10))
 
     if rank == 0:
         print(json.dumps(out))
@@ -470,6 +473,53 @@ def e2e(torch, bf, dev, weights, a, args, steps):
             "h2d_bytes_per_step": len(weights) * m * k * 2, "d2h_bytes_per_step": len(weights) * m * n * 2,
             "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps,
             "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* (C ABI via ctypes) -> pinned host C"}
+
+
+def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps):
+    """e2e with the weight rows split over the ranks: every call copies the
+    activations from pinned host memory, runs this rank's rows through the C
+    ABI, all-gathers the output slices (NCCL) and reads the full C back to
+    pinned host memory. Max over ranks."""
+    import torch.distributed as dist
+
+    m, k = a.shape
+    h_a = torch.empty((m, k), dtype=torch.float16).pin_memory()
+    h_a.copy_(a.cpu())
+    h_c = torch.empty((m, n_total), dtype=torch.float16).pin_memory()
+    d_a = torch.empty_like(a)
+    d_c = torch.empty((m, n_total), dtype=torch.float16, device=dev)
+    st = torch.cuda.Stream(device=dev)
+
+    def step():
+        for w in weights:
+            d_a.copy_(h_a, non_blocking=True)
+            if args.fmt == "q4k":
+                tp.gemm_q4k_tp(w, d_a, n_total, out=d_c)
+            else:
+                tp.gemm_q4_0_tp(w[0], w[1], d_a, n_total, out=d_c)
+            h_c.copy_(d_c, non_blocking=True)
+
+    with torch.cuda.stream(st):
+        for _ in range(2):
+            step()
+        st.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            step()
+        e1.record(st)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    assert bf.stream_status(st) == 0
+    calls = steps * len(weights)
+    return {"value": round(m * calls / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": len(weights) * m * k * 2, "d2h_bytes_per_step": len(weights) * m * n_total * 2,
+            "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps,
+            "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* on this rank's rows (C ABI) -> "
+                    "NCCL all-gather -> pinned host C (every rank), max over ranks"}
 
 
 # ---------------------------------------------------------------------------

@@ -169,7 +169,7 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 // ----------------------------------------------------------------------------
-// TMA (no multicast anywhere in this library)
+// TMA: plain tensor loads into this CTA's own shared memory only
 // ----------------------------------------------------------------------------
 constexpr uint64_t kPolicyEvictFirst = 0x12F0000000000000ull;
 constexpr uint64_t kPolicyEvictLast = 0x14F0000000000000ull;
