@@ -19,7 +19,7 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
     "stream_status", "stream_status_bits", "set_pdl", "probe_umma", "version",
 ]
 
@@ -60,6 +60,7 @@ _I = ctypes.c_int
 _SIGS = {
     "busfill_gemm_q4_0": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q4_0_ggml": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
@@ -177,6 +178,23 @@ def gemm_q4k(blocks, a, out=None, stream=None):
         out = torch.empty((m, n), dtype=torch.float16, device=a.device)
     _need(out, torch.float16, "out")
     _check(_lib().busfill_gemm_q4k(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)), "busfill_gemm_q4k")
+    return out
+
+
+def gemm_q4_0_ggml(blocks, a, out=None, stream=None):
+    """C[M, N] = A[M, K] @ deq(W)[N, K]^T for llama.cpp block_q4_0 rows
+    (18-byte blocks, [N, K/32*18] u8); fp16 out. K % 256 == 0."""
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = blocks.shape[0]
+    if k % 256 or blocks.shape[1] != k // 32 * 18:
+        raise ValueError(f"shape mismatch: blocks {tuple(blocks.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q4_0_ggml(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
+           "busfill_gemm_q4_0_ggml")
     return out
 
 

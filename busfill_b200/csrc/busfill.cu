@@ -272,12 +272,13 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
 
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
-  if constexpr (FMT == WFmt::Q4K) {
+  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4_0G) {
+    // 144 bytes per 256 values of a row: one block_q4_K or eight block_q4_0
     const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
                       CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
-    tws = tw;  // unused by the Q4_K kernel
+    tws = tw;  // unused by these formats
   } else {
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
                       kTileRows, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -424,6 +425,10 @@ int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, 
 
 int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
   return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
+  return gemm_impl<WFmt::Q4_0G, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int busfill_gemm_q4k_noalloc(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,

@@ -67,12 +67,15 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "ptx.cuh"
 
 namespace busfill {
 
-enum class WFmt : int { Q4_0 = 0, Q4K = 1 };
+// Q4_0: the reference's split planes; Q4K: llama.cpp block_q4_K rows;
+// Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes).
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2 };
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
 constexpr int kUnitK = 256;          // K per unit
@@ -210,6 +213,45 @@ __device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1
   }
 }
 
+// llama.cpp block_q4_0 rows, one 64-value chunk cc (blocks 2cc and 2cc+1 of
+// the unit's eight 18-byte blocks). A unit is 144 bytes of the row; the chunk
+// is its bytes [36cc, 36cc+36), i.e. words cc..cc+8 of the three 16-byte
+// loads w[0..11] that cover bytes [16*floor(36cc/16), +48). Block 2cc starts
+// on a 4-byte boundary (d in the low half of its first word, nibbles 2 bytes
+// further on), block 2cc+1 two bytes later (d in the high half of word 4,
+// nibbles word-aligned from word 5). Element e < 16 of a block is the low
+// nibble of its byte e, element e >= 16 the high nibble of byte e - 16.
+// Writes fp16_rn((q-8)*d): out[0..15] block 2cc, out[16..31] block 2cc+1.
+template <int CC>
+__device__ __forceinline__ void dequant_q4_0g_chunk(const uint32_t* w, uint32_t* out) {
+  constexpr int o = CC;  // first word of the chunk within w
+  const __half2 b1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
+  const __half2 b72 = __halves2half2(__ushort_as_half(0x5480), __ushort_as_half(0x5480));    // 72
+  uint32_t q[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = prmt(w[o + i], w[o + i + 1], 0x5432u);  // bytes 2.. of the first block
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[4 + i] = w[o + 5 + i];
+  const uint32_t d0 = w[o] & 0xFFFFu, d1 = w[o + 4] >> 16;
+  const __half2 dd[2] = {u32_as_h2(d0 | (d0 << 16)), u32_as_h2(d1 | (d1 << 16))};
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t t0 = prmt(q[4 * b + i], q[4 * b + i], 0x0100u);  // byte0 = byte 4i, byte2 = byte 4i+1
+      const uint32_t t1 = prmt(q[4 * b + i], q[4 * b + i], 0x0302u);  // bytes 4i+2, 4i+3
+      const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}
+      const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
+      const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}
+      const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
+      out[16 * b + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l01), b1032), dd[b]));
+      out[16 * b + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l23), b1032), dd[b]));
+      out[16 * b + 8 + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h01), b72), dd[b]));
+      out[16 * b + 8 + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h23), b72), dd[b]));
+    }
+  }
+}
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>
@@ -245,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = DecodeSmem<NB>;
   using TM = DecodeTmem<NB>;
   constexpr bool kQ4K = (FMT == WFmt::Q4K);
+  constexpr bool kRows144 = (FMT != WFmt::Q4_0);  // 144-byte row units (block_q4_K, 8 x block_q4_0)
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
   constexpr int kWStages = L::kWStages;
 
@@ -285,62 +328,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     return ok;
   };
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kWStages; ++s) {
-      mbar_init(BAR(L::bWFull + s), 1);
-      mbar_init(BAR(L::bWEmpty + s), 4);   // the 4 dequant warps of the unit's group
-    }
-    for (int s = 0; s < kSlots; ++s) {
-      mbar_init(BAR(L::bReady + s), 5);    // the unit's 4 dequant warps + the activation producer (+ TMA bytes)
-      mbar_init(BAR(L::bUDone + s), 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(BAR(L::bAccFull + b), 1);
-      mbar_init(BAR(L::bAccEmpty + b), 4); // the 4 epilogue warps
-    }
-    mbar_init(BAR(L::bRedFull), 1);    // rank 0's expect_tx; the other ranks' st.async bytes complete it
-    mbar_init(BAR(L::bRedEmpty), 4);   // rank 0's 4 epilogue warps
-    mbar_init(BAR(L::bFinal), 1);
-    fence_mbar_init();
-    tma_prefetch_desc(&tmap_w);
-    if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
-    tma_prefetch_desc(&tmap_a);
-  }
-  // weight TMA for unit i into ring stage i % kWStages (the stage must be free)
-  auto issue_w = [&](int i) {
+  // arrivals each barrier expects per phase
+  auto bar_count = [&](int b) -> uint32_t {
+    if (b >= L::bWEmpty && b < L::bWEmpty + kWStages) return 4;  // the 4 dequant warps of the unit's group
+    if (b >= L::bReady && b < L::bReady + kSlots) return 5;       // 4 dequant warps + the activation producer (+ TMA bytes)
+    if (b >= L::bAccEmpty && b < L::bAccEmpty + 2) return 4;      // the 4 epilogue warps
+    if (b == L::bRedEmpty) return 4;                              // rank 0's 4 epilogue warps
+    return 1;  // TMA expect_tx arrivals, MMA commits, rank 0's expect_tx on bRedFull
+  };
+  // weight TMA for unit i into ring stage i % kWStages (the stage must be free); one thread
+  auto issue_w_thread = [&](int i) {
     const int s = i % kWStages;
     const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
     const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
-    if (elect_one()) {
-      mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
-      if constexpr (kQ4K) {
-        tma_load_2d(dst, &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
-      } else {
-        tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
-        tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, ui.sb * 8, ui.tile * kTileRows, BAR(L::bWFull + s),
-                    kPolicyEvictFirst);
-      }
+    mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
+    if constexpr (kRows144) {
+      tma_load_2d(dst, &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+    } else {
+      tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+      tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, ui.sb * 8, ui.tile * kTileRows, BAR(L::bWFull + s),
+                  kPolicyEvictFirst);
     }
-    __syncwarp();
   };
-  // The first ring's worth of weights needs nothing but the barriers thread 0
-  // just initialised: start streaming before the CTA- and cluster-wide set-up.
+  // activations of unit i into slot i % kSlots (the slot must be free); one
+  // thread. The copy's bytes and this arrival count towards the slot's ready
+  // phase, which the unit's dequant warps complete.
+  auto issue_x_thread = [&](int i) {
+    const int s = i % kSlots;
+    const int sb = sb0 + i % len;
+    mbar_arrive_expect_tx(BAR(L::bReady + s), L::kXSlotBytes);
+#pragma unroll
+    for (int cc = 0; cc < kChunksPerUnit; ++cc)
+      tma_load_2d(sbase + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes, &tmap_a, sb * kUnitK + cc * kChunkK,
+                  0, BAR(L::bReady + s), kPolicyEvictLast);
+  };
+  // Set-up is on the critical path of every launch: the CTAs that start last
+  // (on the SMs the previous kernel frees last) finish last. So the barriers
+  // are initialised by all lanes of warp 0 at once, and the first ring of
+  // weight boxes and the first slots of activations are issued one per lane
+  // before the CTA-wide sync. Weights do not depend on earlier kernels and
+  // never wait for griddepcontrol.wait; activations do.
   const int w_early = nunits < kWStages ? nunits : kWStages;
+  const int x_early = nunits < kSlots ? nunits : kSlots;
   if (warp == kWarpWProducer) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
+      tma_prefetch_desc(&tmap_a);
+    }
+    for (int b = lane; b < L::kNumBars; b += 32) mbar_init(BAR(b), bar_count(b));
+    fence_mbar_init();
     __syncwarp();
-    for (int i = 0; i < w_early; ++i) issue_w(i);
-  }
-  if (warp == kWarpXProducer) {
+    named_bar_arrive(1, 64);  // barriers ready: release the activation producer
+    if (lane < w_early) issue_w_thread(lane);
+    __syncwarp();
+  } else if (warp == kWarpXProducer) {
     tmem_alloc(sbase + L::kMiscOff, kTmemCols);
     tmem_relinquish();
+    named_bar_sync(1, 64);
+    pdl_wait_prerequisites();  // activations may be the previous kernel's output
+    if (lane < x_early) issue_x_thread(lane);
+    __syncwarp();
   }
-  __syncwarp();
   tc_fence_before();
   __syncthreads();
-  // the other CTAs of the cluster arrive on our barriers: they must be initialised first
-  if (csize > 1) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem = misc[0];
+  // The other CTAs of the cluster touch our barriers and shared memory only
+  // at the end of a tile: arrive now, and wait (for every CTA of the cluster
+  // to have initialised its barriers) only before the first such access.
+  if (csize > 1) cluster_arrive();
+  bool cl_waited = false;    // this thread has waited on the set-up phase
+  bool cl_arrived = false;   // this thread has arrived on the teardown phase
   // Let the next kernel on the stream launch now: its CTAs take SMs as ours
   // retire and begin streaming their weights before our tail completes.
   if (threadIdx.x == 0) pdl_launch_dependents();
@@ -350,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued = w_early;
     for (int i = w_early; i < nunits; ++i) {
       if (!warp_wait(BAR(L::bWEmpty + i % kWStages), ((i / kWStages) & 1) ^ 1)) break;
-      issue_w(i);
+      if (elect_one()) issue_w_thread(i);
+      __syncwarp();
       issued = i + 1;
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrWeightProducer);
@@ -363,20 +423,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
   } else if (warp == kWarpXProducer) {
     // ---------------- activation producer ----------------
-    pdl_wait_prerequisites();  // activations may be the previous kernel's output
-    int issued = 0;
-    for (int i = 0; i < nunits; ++i) {
-      const int s = i % kSlots;
-      // slot s is free once the MMAs of unit i - kSlots have completed
-      if (i >= kSlots && !warp_wait(BAR(L::bUDone + s), ((i / kSlots) & 1) ^ 1)) break;
-      const int sb = sb0 + i % len;
-      if (elect_one()) {
-        mbar_arrive_expect_tx(BAR(L::bReady + s), L::kXSlotBytes);
-#pragma unroll
-        for (int cc = 0; cc < kChunksPerUnit; ++cc)
-          tma_load_2d(sbase + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes, &tmap_a,
-                      sb * kUnitK + cc * kChunkK, 0, BAR(L::bReady + s), kPolicyEvictLast);
-      }
+    int issued = x_early;
+    for (int i = x_early; i < nunits; ++i) {
+      // slot i % kSlots is free once the MMAs of unit i - kSlots have completed
+      if (!warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
+      if (elect_one()) issue_x_thread(i);
       __syncwarp();
       issued = i + 1;
     }
@@ -470,6 +521,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
           tmem_st_x32(a_slot + cc * 32, P);
         }
+      } else if constexpr (FMT == WFmt::Q4_0G) {
+        const uint8_t* urow = stage + r * kQ4KBlockBytes;
+        uint32_t P[32];
+        auto chunk = [&](auto cc_tag) {
+          constexpr int cc = decltype(cc_tag)::value;
+          constexpr int v0 = (36 * cc) / 16;  // first 16-byte load covering the chunk
+          uint32_t w[12];
+#pragma unroll
+          for (int v = 0; v < 3; ++v) {
+            const uint4 x = *reinterpret_cast<const uint4*>(urow + 16 * (v0 + v));
+            w[4 * v] = x.x; w[4 * v + 1] = x.y; w[4 * v + 2] = x.z; w[4 * v + 3] = x.w;
+          }
+          dequant_q4_0g_chunk<(36 * cc % 16) / 4>(w, P);
+          tmem_st_x32(a_slot + cc * 32, P);
+        };
+        chunk(std::integral_constant<int, 0>{});
+        chunk(std::integral_constant<int, 1>{});
+        chunk(std::integral_constant<int, 2>{});
+        chunk(std::integral_constant<int, 3>{});
       } else {
         const uint8_t* wrow = stage + r * 128;
         const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
@@ -507,11 +577,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     // fence, no separate signal: every release or remote round trip costs
     // ~0.5 us on B200); rank 0 adds the partials in rank order and writes C.
     // Receive layout: [rank-1][row][NB] fp32, 16-byte chunks swizzled by row.
+    // After the last tile each CTA arrives on the cluster's teardown barrier
+    // as soon as it is done with distributed shared memory (ranks k > 0 once
+    // their partials are pushed, rank 0 once it has read them), so rank 0
+    // finds the barrier complete when it waits after its C store.
     auto flush = [&](int tile, int seg) {
       const int n = tile * kTileRows + r;
       OutT* C = reinterpret_cast<OutT*>(p.c);
       constexpr int kChunks = NB / 4;
       const int swz = r & (kChunks - 1);
+      if (csize > 1 && !cl_waited) {
+        __syncwarp();
+        cluster_wait();  // every CTA of the cluster has initialised its barriers
+        cl_waited = true;
+      }
       if (csize > 1 && crank != 0) {
         // rank 0's buffer is free once it has read the previous segment
         if (seg > 0) warp_wait(BAR(L::bRedEmpty), (uint32_t)((seg - 1) & 1), true);
@@ -522,6 +601,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < kChunks; ++j)
           st_async_f4(dst + (uint32_t)((j ^ swz) << 4), acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3],
                       dst_bar);
+        if (seg == ntiles - 1) {
+          __syncwarp();
+          cluster_arrive();
+          cl_arrived = true;
+        }
         return;
       }
       if (csize > 1) {
@@ -541,11 +625,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc[4 * j + 3] += v[j].w;
           }
         }
+        __syncwarp();
         if (seg + 1 < ntiles) {
           // let the other ranks overwrite our buffer with their next partial
-          __syncwarp();
           if (lane == 0)
             for (int k = 1; k < csize; ++k) mbar_arrive_remote(mapa_shared(BAR(L::bRedEmpty), (uint32_t)k));
+        } else {
+          cluster_arrive();
+          cl_arrived = true;
         }
       }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
@@ -582,11 +669,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   // ---------------- teardown ----------------
+  // Every thread of the cluster arrives once and waits once on each of the two
+  // cluster barrier phases: set-up (barriers initialised) and teardown (done
+  // with distributed shared memory); the epilogue warps took their turns above.
   __syncwarp();
+  if (csize > 1) {
+    if (!cl_waited) cluster_wait();
+    if (!cl_arrived) cluster_arrive();
+  }
   __syncthreads();
-  // no CTA may leave while another CTA of its cluster can still read its
-  // shared memory or arrive on its barriers
-  if (csize > 1) cluster_sync_all();
   if (warp == kWarpXProducer) {
     bool done = true;
     if (lane == 0) done = mbar_wait(BAR(L::bFinal), 0);
@@ -595,6 +686,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+  // no CTA may leave while another CTA of its cluster can still read its
+  // shared memory or arrive on its barriers
+  if (csize > 1) cluster_wait();
 }
 
 }  // namespace busfill

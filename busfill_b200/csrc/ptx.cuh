@@ -167,6 +167,20 @@ __device__ __forceinline__ void st_async_f4(uint32_t cluster_addr, float a, floa
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// The two halves of cluster_sync_all, for a split barrier: every thread of the
+// cluster arrives once and later waits once per phase (converged warps); the
+// wait returns when every thread of the cluster has arrived.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+// CTA named barriers (ids 1..15; id 0 is __syncthreads): `count` threads, a
+// multiple of 32, take part; arrive does not wait.
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(uint32_t id, uint32_t count) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 // ----------------------------------------------------------------------------
 // TMA: plain tensor loads into this CTA's own shared memory only

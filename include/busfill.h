@@ -68,6 +68,18 @@ BUSFILL_API int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const u
  * (kernels/q4k_batched.py:7-8). */
 BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
 
+/* Q4_0 as llama.cpp stores it: block_q4_0 rows, K/32 blocks of 18 bytes per
+ * weight row (fp16 d, then 16 bytes whose low nibbles are elements 0-15 and
+ * high nibbles elements 16-31); value = (q - 8) * d, the same rule as
+ * busfill_gemm_q4_0.  a [M, K] fp16, c [M, N] fp16.  Requires K % 256 == 0;
+ * blocks and a 16-byte aligned.  No reference counterpart: it is the
+ * ggml-native ingest of the Q4_0 weights the reference's kernels take as
+ * split planes (kernels/busfill_v1a.cu:41-46; the layout is named at
+ * kernels/busfill_v0.cu:18-20), so llama.cpp buffers drop in without a
+ * repack. */
+BUSFILL_API int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                                       void* stream);
+
 /* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
  * in the reference.
  *

@@ -162,6 +162,41 @@ def test_gemm_q4_0_parity(m, n, k):
     assert_gates(c, cref, exact)
 
 
+@pytest.mark.parametrize("m,n,k", SHAPES)
+def test_gemm_q4_0_ggml_parity(m, n, k):
+    """llama.cpp block_q4_0 rows: the same weights as the split planes, so the
+    fp16 operands are identical and so is the whole accumulation order: the
+    output must equal the split-plane GEMM's bit for bit, and pass the gates."""
+    wq, ws = orc.gen_q4_0(n, k, seed=m * 3 + n + k)
+    blocks = orc.q4_0_planes_to_ggml_blocks(wq, ws)
+    a = orc.gen_activations(m, k, seed=m + 11 * k)
+    c = bf.gemm_q4_0_ggml(cu(blocks), cu(a))
+    c_planes = bf.gemm_q4_0(cu(wq), cu(ws), cu(a))
+    check_status()
+    assert torch.equal(c.view(torch.int16), c_planes.view(torch.int16))
+    w16 = orc.dequant_q4_0_ggml(blocks, k)
+    cref = orc.gemm_ref(a, orc.dequant_q4_0_planes_f32(wq, ws))
+    assert_gates(c, cref, a.astype(np.float64) @ w16.astype(np.float64).T)
+
+
+def test_gemm_q4_0_ggml_gguf_golden(golden_dir):
+    """GEMM over the gguf-py block_q4_0 fixture (16 rows x 256), tiled to 128 rows."""
+    g = np.load(os.path.join(golden_dir, "q4_0_gguf.npz"))
+    k = int(g["k"])
+    blocks = np.tile(g["blocks"], (8, 1))
+    w32 = np.tile(g["w32"], (8, 1))
+    a = orc.gen_activations(9, k, seed=99)
+    c = bf.gemm_q4_0_ggml(cu(blocks), cu(a))
+    check_status()
+    # The fixture's scales are arbitrary fp16 values (weights up to ~126), so
+    # outputs reach ~1e3 and the absolute gate does not apply; the result must
+    # still be the fp16 rounding of an fp32 sum of the exact fp16 products.
+    exact = a.astype(np.float64) @ w32.astype(np.float16).astype(np.float64).T
+    got = c.float().cpu().numpy().astype(np.float64)
+    assert np.all(np.isfinite(got))
+    assert np.all(np.abs(got - exact) <= 2.0 ** -10 * np.abs(exact) + 1e-2)
+
+
 # (cluster size, M, N, K): forced K splits, including schedules where every
 # cluster takes several tiles in turn (the reduction buffer is reused)
 KSPLIT_CASES = [
