@@ -98,6 +98,22 @@ bool make_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Activations [rows, K] fp16 row-major seen as 3-D (64 values, rows, K/64
+// chunks) so that one box brings `chunks` consecutive 64-value chunks of
+// `box_rows` rows, landing chunk-major with the 128-byte swizzle.
+bool make_tmap_act3d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K, uint32_t box_rows,
+                     uint32_t chunks) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {64, rows, K / 64};
+  const cuuint64_t strides[2] = {K * 2, 128};
+  const cuuint32_t box[3] = {64, box_rows, chunks};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ---------------------------------------------------------------------------
 // per-(device, stream) device words: [0] error bits, [1] first failure record.
 // Zeroed at allocation; busfill_stream_status clears them after a failure.
@@ -294,8 +310,7 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     const DecodeSchedule sch = nb == 16 ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count)
                                         : choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count);
     const uint16_t* a_chunk = a + (size_t)m0 * K;
-    if (!make_tmap_2d(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, a_chunk, (uint64_t)K, (uint64_t)mc, (uint64_t)K * 2,
-                      kChunkK, (uint32_t)nb, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (!make_tmap_act3d(&ta, a_chunk, (uint64_t)mc, (uint64_t)K, (uint32_t)nb, kChunksPerUnit))
       return BUSFILL_ERR_CUDA;
     DecodeParams p;
     p.c = reinterpret_cast<OutT*>(c) + (size_t)m0 * N;

@@ -26,12 +26,13 @@
 //
 // Warp roles (16 warps, one CTA per SM):
 //   0      weight TMA producer: one 2D box of 128 rows x one unit (18 KB) per
-//          stage into a 4- or 6-stage ring; the first ring's worth is issued
-//          before the CTA and cluster set-up. Weights do not depend on earlier
+//          stage into a 6- or 8-stage ring; the first stages are issued before
+//          the CTA and cluster set-up. Weights do not depend on earlier
 //          kernels, so none of this waits for griddepcontrol.wait.
-//   1      activation TMA producer: four 64-value x NB-row boxes per unit
-//          (128-byte swizzle) into the unit's slot; the copy completes on the
-//          same barrier as the slot's TMEM operands, so the MMA warp waits,
+//   1      activation TMA producer: one 3-D box per unit (four 64-value x
+//          NB-row chunks, 128-byte swizzle) into a 4- or 6-stage ring of its
+//          own, several units ahead of the MMA; the copy completes on the same
+//          barrier as the unit's TMEM operands, so the MMA warp waits,
 //          pre-tests and commits one barrier per unit; TMEM allocator.
 //   3      MMA issuer (converged warp, one elected thread issues).
 //   4-11   dequant: thread (warp%4, lane) owns weight row 32*(warp%4)+lane and
@@ -41,15 +42,7 @@
 //          accumulator and finishes the tile (cluster reduction, C store).
 //   2      idle.
 //
-// Numerics (fp32 accumulation of fp16 products in both formats).
-//   Q4_0: operand fp16_rn((q-8)*d), bit-identical to the reference dequant
-//   (kernels/busfill_v0.cu:74-81): the lop3 magic bias 0x6400 gives the exact
-//   fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
-//   Q4_K: operand q*ds - dm in one hfma2, with ds = fp16_rn(d*sc) and dm =
-//   fp16_rn(dmin*m) per 32-value sub-block and q exact (low nibbles via the
-//   bias 0x6400 = 1024 + q, high nibbles via 0x5400, whose mantissa step is
-//   1/16, = 64 + q). Two fp16 roundings per weight (~3e-4 relative rms); the
-//   bit-exact fp16 dequant is busfill_dequant_q4k.
+// Numerics: formats.cuh (per format, the fp16 operand each weight becomes).
 //
 // Work split: a tile of 128 weight rows is split along K over the c CTAs of
 // a thread-block cluster (rank k takes units [k*S/c, (k+1)*S/c) of every
@@ -69,22 +62,12 @@
 #include <cstdint>
 #include <type_traits>
 
+#include "formats.cuh"
 #include "ptx.cuh"
 
 namespace busfill {
 
-// Q4_0: the reference's split planes; Q4K: llama.cpp block_q4_K rows;
-// Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes).
-enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2 };
-
-constexpr int kTileRows = 128;       // weight rows per tile = MMA M
-constexpr int kUnitK = 256;          // K per unit
-constexpr int kChunkK = 64;          // K per activation box / 32 TMEM operand columns
-constexpr int kChunksPerUnit = kUnitK / kChunkK;
-constexpr int kQ4KBlockBytes = 144;
-constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
-constexpr int kQ40ScaleOffset = 16384;
-constexpr int kSlots = 3;            // unit slots (TMEM operands + activations) between the producers and the MMA
+constexpr int kSlots = 3;            // unit operand slots in TMEM between the dequant warps and the MMA
 constexpr int kThreads = 512;
 constexpr int kWarpWProducer = 0;
 constexpr int kWarpXProducer = 1;
@@ -134,7 +117,14 @@ constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
 // (a group that skipped the other group's phase of a stage could see that
 // stale phase as complete: mbarrier waits only tell parities apart).
 template <int NB>
-constexpr int w_stages() { return NB == 32 ? 6 : 8; }
+constexpr int w_stages() { return 6; }
+
+// Activation ring depth (one unit per stage), separate from the TMEM operand
+// slots so that a unit's activations are requested several units ahead: a
+// box waits behind the weight boxes in its SM's TMA queue (~1.2 us from issue
+// to landing under load on B200), longer than the three-slot operand cycle.
+template <int NB>
+constexpr int x_stages() { return NB == 32 ? 4 : 6; }
 
 template <int NB>
 struct DecodeSmem {
@@ -143,8 +133,10 @@ struct DecodeSmem {
   static constexpr int kWOff = 0;
   static constexpr int kWStages = w_stages<NB>();
   static_assert(kWStages % 2 == 0, "each weight stage must belong to one dequant group");
+  static constexpr int kXStages = x_stages<NB>();
+  static_assert(kXStages >= kSlots, "an activation stage per operand slot at least");
   static constexpr int kXOff = kWOff + kWStages * kWStageBytes;
-  static constexpr int kRedOff = kXOff + kSlots * kXSlotBytes;        // rank 0: [rank-1][128][NB] fp32 partials
+  static constexpr int kRedOff = kXOff + kXStages * kXSlotBytes;      // rank 0: [rank-1][128][NB] fp32 partials
   static constexpr int kRedRankBytes = kTileRows * NB * 4;
   static constexpr int kBarOff = kRedOff + (max_cluster<NB>() - 1) * kRedRankBytes;
   // barrier slots
@@ -157,107 +149,14 @@ struct DecodeSmem {
   static constexpr int bAccEmpty = bAccFull + 2;           // segment accumulator b read by the epilogue
   static constexpr int bRedFull = bAccEmpty + 2;           // rank 0: the other ranks' partials landed (tx bytes)
   static constexpr int bRedEmpty = bRedFull + 1;           // rank k > 0: rank 0 has read this rank's partial
-  static constexpr int bFinal = bRedEmpty + 1;
+  static constexpr int bXFree = bRedEmpty + 1;            // activation stage x free: the MMAs of its unit completed (commit)
+  static constexpr int bFinal = bXFree + kXStages;
   static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;  // slack to align the base to 1024 B
   static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
 };
-
-// ---------------------------------------------------------------------------
-// dequant helpers (one weight row per thread)
-// ---------------------------------------------------------------------------
-
-// Q4_0, one 32-value block: 16 bytes -> 16 columns of fp16 pairs (k = 2c, 2c+1)
-// holding fp16_rn((q-8)*d). Byte j holds elements 2j (low nibble) and 2j+1.
-__device__ __forceinline__ void dequant_q4_0_block(const uint4 b, const __half2 d2, uint32_t* out) {
-  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032, 1032
-  const uint32_t w[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = w[i];
-    const uint32_t hi = w[i] >> 4;
-#pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      // byte0 <- low nibble of byte x, byte2 <- high nibble of byte x
-      const uint32_t t = prmt(lo, hi, (uint32_t)(((4 + x) << 8) | x));
-      const uint32_t v = lop3_and_or(t, 0x000F000Fu, 0x64006400u);      // {1024+lo, 1024+hi}
-      out[4 * i + x] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v), bias), d2));
-    }
-  }
-}
-
-// Q4_K, one 64-value chunk of a super-block: 32 bytes; byte l holds element l
-// of sub-block 2c (low nibble) and of sub-block 2c+1 (high nibble). Writes
-// q*ds - dm in one hfma2 per pair: out[0..15] = sub-block 2c (ds_lo, ndm_lo),
-// out[16..31] = sub-block 2c+1 (ds_hi, ndm_hi); ndm = -dm.
-__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, const __half2 ds_lo,
-                                                  const __half2 ndm_lo, const __half2 ds_hi, const __half2 ndm_hi,
-                                                  uint32_t* out) {
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t t0 = prmt(w[i], w[i], 0x0100u);  // byte0 = b0, byte2 = b1
-    const uint32_t t1 = prmt(w[i], w[i], 0x0302u);  // byte0 = b2, byte2 = b3
-    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}: mantissa step 1
-    const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
-    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}: mantissa step 1/16
-    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
-    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
-    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
-    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
-    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
-  }
-}
-
-// llama.cpp block_q4_0 rows, one 64-value chunk cc (blocks 2cc and 2cc+1 of
-// the unit's eight 18-byte blocks). A unit is 144 bytes of the row; the chunk
-// is its bytes [36cc, 36cc+36), i.e. words cc..cc+8 of the three 16-byte
-// loads w[0..11] that cover bytes [16*floor(36cc/16), +48). Block 2cc starts
-// on a 4-byte boundary (d in the low half of its first word, nibbles 2 bytes
-// further on), block 2cc+1 two bytes later (d in the high half of word 4,
-// nibbles word-aligned from word 5). Element e < 16 of a block is the low
-// nibble of its byte e, element e >= 16 the high nibble of byte e - 16.
-// Writes fp16_rn((q-8)*d): out[0..15] block 2cc, out[16..31] block 2cc+1.
-template <int CC>
-__device__ __forceinline__ void dequant_q4_0g_chunk(const uint32_t* w, uint32_t* out) {
-  constexpr int o = CC;  // first word of the chunk within w
-  const __half2 b1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
-  const __half2 b72 = __halves2half2(__ushort_as_half(0x5480), __ushort_as_half(0x5480));    // 72
-  uint32_t q[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) q[i] = prmt(w[o + i], w[o + i + 1], 0x5432u);  // bytes 2.. of the first block
-#pragma unroll
-  for (int i = 0; i < 4; ++i) q[4 + i] = w[o + 5 + i];
-  const uint32_t d0 = w[o] & 0xFFFFu, d1 = w[o + 4] >> 16;
-  const __half2 dd[2] = {u32_as_h2(d0 | (d0 << 16)), u32_as_h2(d1 | (d1 << 16))};
-#pragma unroll
-  for (int b = 0; b < 2; ++b) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t t0 = prmt(q[4 * b + i], q[4 * b + i], 0x0100u);  // byte0 = byte 4i, byte2 = byte 4i+1
-      const uint32_t t1 = prmt(q[4 * b + i], q[4 * b + i], 0x0302u);  // bytes 4i+2, 4i+3
-      const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}
-      const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
-      const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}
-      const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
-      out[16 * b + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l01), b1032), dd[b]));
-      out[16 * b + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l23), b1032), dd[b]));
-      out[16 * b + 8 + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h01), b72), dd[b]));
-      out[16 * b + 8 + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h23), b72), dd[b]));
-    }
-  }
-}
-
-template <typename OutT>
-__device__ __forceinline__ OutT to_out(float v);
-template <>
-__device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
-template <>
-__device__ __forceinline__ float to_out<float>(float v) { return v; }
 
 // Per-unit schedule facts every role derives the same way: unit i of this CTA
 // is unit sb0 + i % len of its cluster's (i / len)-th tile.
@@ -286,7 +185,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(NB == 16 || NB == 32, "batch tile");
   using L = DecodeSmem<NB>;
   using TM = DecodeTmem<NB>;
-  constexpr bool kQ4K = (FMT == WFmt::Q4K);
   constexpr bool kRows144 = (FMT != WFmt::Q4_0);  // 144-byte row units (block_q4_K, 8 x block_q4_0)
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
   constexpr int kWStages = L::kWStages;
@@ -350,17 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                   kPolicyEvictFirst);
     }
   };
-  // activations of unit i into slot i % kSlots (the slot must be free); one
-  // thread. The copy's bytes and this arrival count towards the slot's ready
-  // phase, which the unit's dequant warps complete.
+  // activations of unit i into stage i % kXStages (the stage must be free);
+  // one thread. The copy's bytes and this arrival count towards the slot's ready
+  // phase, which the unit's dequant warps complete. One 3-D box brings the
+  // unit's four 64-value chunks (dims: 64 values, rows, chunk), landing as
+  // [chunk][row][128 B] swizzled, the MMA's B layout: an SM's TMA unit takes
+  // about as long per box for 4 KB as for 32 KB (measured on B200), so one
+  // box per unit instead of four shortens the activations' path to the MMA.
   auto issue_x_thread = [&](int i) {
     const int s = i % kSlots;
     const int sb = sb0 + i % len;
     mbar_arrive_expect_tx(BAR(L::bReady + s), L::kXSlotBytes);
-#pragma unroll
-    for (int cc = 0; cc < kChunksPerUnit; ++cc)
-      tma_load_2d(sbase + L::kXOff + s * L::kXSlotBytes + cc * L::kXChunkBytes, &tmap_a, sb * kUnitK + cc * kChunkK,
-                  0, BAR(L::bReady + s), kPolicyEvictLast);
+    tma_load_3d(sbase + L::kXOff + (i % L::kXStages) * L::kXSlotBytes, &tmap_a, 0, 0, sb * kChunksPerUnit,
+                BAR(L::bReady + s), kPolicyEvictLast);
   };
   // Set-up is on the critical path of every launch: the CTAs that start last
   // (on the SMs the previous kernel frees last) finish last. So the barriers
@@ -368,7 +268,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // weight boxes and the first slots of activations are issued one per lane
   // before the CTA-wide sync. Weights do not depend on earlier kernels and
   // never wait for griddepcontrol.wait; activations do.
-  const int w_early = nunits < kWStages ? nunits : kWStages;
+  // Only the first kWEarly weight stages go out at once; stage i < kWStages
+  // follows when stage i - kWEarly has landed. Every SM asking for its whole
+  // ring at launch makes each SM's first stage land only at the end of that
+  // burst (~2-3 us on B200), which delays the first MMA; the ring still fills
+  // well ahead of the dequant.
+  constexpr int kWEarly = 2;
+  const int w_early = nunits < kWEarly ? nunits : kWEarly;
   const int x_early = nunits < kSlots ? nunits : kSlots;
   if (warp == kWarpWProducer) {
     if (lane == 0) {
@@ -408,6 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- weight producer ----------------
     int issued = w_early;
     for (int i = w_early; i < nunits; ++i) {
+      if (i < kWStages && !warp_wait(BAR(L::bWFull + (i - kWEarly)), 0)) break;
       if (!warp_wait(BAR(L::bWEmpty + i % kWStages), ((i / kWStages) & 1) ^ 1)) break;
       if (elect_one()) issue_w_thread(i);
       __syncwarp();
@@ -425,8 +332,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- activation producer ----------------
     int issued = x_early;
     for (int i = x_early; i < nunits; ++i) {
-      // slot i % kSlots is free once the MMAs of unit i - kSlots have completed
-      if (!warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
+      // activation stage i % kXStages is free once the MMAs of unit i - kXStages completed
+      if (i >= L::kXStages && !warp_wait(BAR(L::bXFree + i % L::kXStages), ((i / L::kXStages) & 1) ^ 1)) break;
+      // the arrival must count towards unit i's phase of its slot barrier: unit
+      // i - kSlots's phase must have completed (it cannot complete without
+      // this producer, so nothing later can alias it)
+      if (!warp_wait(BAR(L::bReady + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       if (elect_one()) issue_x_thread(i);
       __syncwarp();
       issued = i + 1;
@@ -458,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (elect_one()) {
         const uint32_t d_acc = tmem + TM::kAcc + (uint32_t)(buf * NB);
         const uint32_t a_t = tmem + TM::kA + (uint32_t)(s * 128);
-        const uint64_t bd = bdesc0 + (uint64_t)((s * L::kXSlotBytes) >> 4);
+        const uint64_t bd = bdesc0 + (uint64_t)(((i % L::kXStages) * L::kXSlotBytes) >> 4);
 #pragma unroll
         for (int cc = 0; cc < kChunksPerUnit; ++cc)
 #pragma unroll
@@ -466,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_f16_ts(d_acc, a_t + cc * 32 + 8 * t, bd + (uint64_t)((cc * L::kXChunkBytes + 32 * t) >> 4), kIdesc,
                        (j == 0 && cc == 0 && t == 0) ? 0u : 1u);
         tc_commit(BAR(L::bUDone + s));                          // slot s free
+        tc_commit(BAR(L::bXFree + i % L::kXStages));            // activation stage free
         if (j == len - 1) tc_commit(BAR(L::bAccFull + buf));    // segment accumulator complete
       }
       __syncwarp();
@@ -491,70 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (i >= kSlots && !warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       tc_fence_after();
       const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
-      const uint32_t a_slot = tmem + lane_off + TM::kA + (i % kSlots) * 128;
-      if constexpr (kQ4K) {
-        // this row's block header: d, dmin and the 6-bit scales/mins of its
-        // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
-        // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7
-        const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-        const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
-        const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
-        const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-        const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-#pragma unroll 1
-        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
-          // chunk cc covers sub-blocks 2cc, 2cc+1: bytes 2(cc&1), 2(cc&1)+1 of the
-          // _lo words (cc < 2) or of the _hi words (cc >= 2)
-          const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
-          const uint32_t mw = cc < 2 ? m_lo : m_hi;
-          const int sh = 16 * (cc & 1);
-          const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
-          const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
-          const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
-          const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
-          const uint8_t* qs = stage + r * kQ4KBlockBytes + 16 + cc * 32;
-          const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-          uint32_t P[32];
-          dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
-          tmem_st_x32(a_slot + cc * 32, P);
-        }
-      } else if constexpr (FMT == WFmt::Q4_0G) {
-        const uint8_t* urow = stage + r * kQ4KBlockBytes;
-        uint32_t P[32];
-        auto chunk = [&](auto cc_tag) {
-          constexpr int cc = decltype(cc_tag)::value;
-          constexpr int v0 = (36 * cc) / 16;  // first 16-byte load covering the chunk
-          uint32_t w[12];
-#pragma unroll
-          for (int v = 0; v < 3; ++v) {
-            const uint4 x = *reinterpret_cast<const uint4*>(urow + 16 * (v0 + v));
-            w[4 * v] = x.x; w[4 * v + 1] = x.y; w[4 * v + 2] = x.z; w[4 * v + 3] = x.w;
-          }
-          dequant_q4_0g_chunk<(36 * cc % 16) / 4>(w, P);
-          tmem_st_x32(a_slot + cc * 32, P);
-        };
-        chunk(std::integral_constant<int, 0>{});
-        chunk(std::integral_constant<int, 1>{});
-        chunk(std::integral_constant<int, 2>{});
-        chunk(std::integral_constant<int, 3>{});
-      } else {
-        const uint8_t* wrow = stage + r * 128;
-        const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
-        const uint4 dd = *reinterpret_cast<const uint4*>(stage + kQ40ScaleOffset + r * 16);  // 8 block scales
-#pragma unroll 1
-        for (int cc = 0; cc < kChunksPerUnit; ++cc) {
-          uint32_t P[32];
-          const uint4 b0 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc)) ^ sw) << 4));
-          const uint4 b1 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc + 1)) ^ sw) << 4));
-          const __half2 d01 = u32_as_h2(cc == 0 ? dd.x : cc == 1 ? dd.y : cc == 2 ? dd.z : dd.w);
-          dequant_q4_0_block(b0, __low2half2(d01), P);
-          dequant_q4_0_block(b1, __high2half2(d01), P + 16);
-          tmem_st_x32(a_slot + cc * 32, P);
-        }
-      }
+      dequant_unit_row<FMT>(stage, r, tmem + lane_off + TM::kA + (i % kSlots) * 128);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();

@@ -1,0 +1,204 @@
+// Weight formats of the quantized GEMMs and the per-row dequant of one unit
+// (128 weight rows x 256 K) into a tcgen05 A operand in tensor memory.
+//
+// Numerics (fp32 accumulation of fp16 products in every format):
+//   Q4_0: operand fp16_rn((q-8)*d), bit-identical to the reference dequant
+//   (kernels/busfill_v0.cu:74-81): the lop3 magic bias 0x6400 gives the exact
+//   fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
+//   Q4_0G (llama.cpp block_q4_0 rows): the same rule; high nibbles go
+//   through the bias 0x5400 (64 + q) and hsub2 by 72.
+//   Q4_K: operand q*ds - dm in one hfma2, with ds = fp16_rn(d*sc) and dm =
+//   fp16_rn(dmin*m) per 32-value sub-block and q exact (low nibbles via the
+//   bias 0x6400 = 1024 + q, high nibbles via 0x5400, whose mantissa step is
+//   1/16, = 64 + q). Two fp16 roundings per weight (~3e-4 relative rms); the
+//   bit-exact fp16 dequant is busfill_dequant_q4k.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+#include <type_traits>
+
+#include "ptx.cuh"
+
+namespace busfill {
+
+// Q4_0: the reference's split planes; Q4K: llama.cpp block_q4_K rows;
+// Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes).
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2 };
+
+constexpr int kTileRows = 128;       // weight rows per tile = MMA M
+constexpr int kUnitK = 256;          // K per unit
+constexpr int kChunkK = 64;          // K per activation box / 32 TMEM operand columns
+constexpr int kChunksPerUnit = kUnitK / kChunkK;
+constexpr int kQ4KBlockBytes = 144;
+constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
+constexpr int kQ40ScaleOffset = 16384;
+// ---------------------------------------------------------------------------
+// dequant helpers (one weight row per thread)
+// ---------------------------------------------------------------------------
+
+// Q4_0, one 32-value block: 16 bytes -> 16 columns of fp16 pairs (k = 2c, 2c+1)
+// holding fp16_rn((q-8)*d). Byte j holds elements 2j (low nibble) and 2j+1.
+__device__ __forceinline__ void dequant_q4_0_block(const uint4 b, const __half2 d2, uint32_t* out) {
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032, 1032
+  const uint32_t w[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = w[i];
+    const uint32_t hi = w[i] >> 4;
+#pragma unroll
+    for (int x = 0; x < 4; ++x) {
+      // byte0 <- low nibble of byte x, byte2 <- high nibble of byte x
+      const uint32_t t = prmt(lo, hi, (uint32_t)(((4 + x) << 8) | x));
+      const uint32_t v = lop3_and_or(t, 0x000F000Fu, 0x64006400u);      // {1024+lo, 1024+hi}
+      out[4 * i + x] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v), bias), d2));
+    }
+  }
+}
+
+// Q4_K, one 64-value chunk of a super-block: 32 bytes; byte l holds element l
+// of sub-block 2c (low nibble) and of sub-block 2c+1 (high nibble). Writes
+// q*ds - dm in one hfma2 per pair: out[0..15] = sub-block 2c (ds_lo, ndm_lo),
+// out[16..31] = sub-block 2c+1 (ds_hi, ndm_hi); ndm = -dm.
+__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, const __half2 ds_lo,
+                                                  const __half2 ndm_lo, const __half2 ds_hi, const __half2 ndm_hi,
+                                                  uint32_t* out) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t t0 = prmt(w[i], w[i], 0x0100u);  // byte0 = b0, byte2 = b1
+    const uint32_t t1 = prmt(w[i], w[i], 0x0302u);  // byte0 = b2, byte2 = b3
+    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}: mantissa step 1
+    const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
+    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}: mantissa step 1/16
+    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
+    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
+    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
+    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
+    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
+  }
+}
+
+// llama.cpp block_q4_0 rows, one 64-value chunk cc (blocks 2cc and 2cc+1 of
+// the unit's eight 18-byte blocks). A unit is 144 bytes of the row; the chunk
+// is its bytes [36cc, 36cc+36), i.e. words cc..cc+8 of the three 16-byte
+// loads w[0..11] that cover bytes [16*floor(36cc/16), +48). Block 2cc starts
+// on a 4-byte boundary (d in the low half of its first word, nibbles 2 bytes
+// further on), block 2cc+1 two bytes later (d in the high half of word 4,
+// nibbles word-aligned from word 5). Element e < 16 of a block is the low
+// nibble of its byte e, element e >= 16 the high nibble of byte e - 16.
+// Writes fp16_rn((q-8)*d): out[0..15] block 2cc, out[16..31] block 2cc+1.
+template <int CC>
+__device__ __forceinline__ void dequant_q4_0g_chunk(const uint32_t* w, uint32_t* out) {
+  constexpr int o = CC;  // first word of the chunk within w
+  const __half2 b1032 = __halves2half2(__ushort_as_half(0x6408), __ushort_as_half(0x6408));  // 1032
+  const __half2 b72 = __halves2half2(__ushort_as_half(0x5480), __ushort_as_half(0x5480));    // 72
+  uint32_t q[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[i] = prmt(w[o + i], w[o + i + 1], 0x5432u);  // bytes 2.. of the first block
+#pragma unroll
+  for (int i = 0; i < 4; ++i) q[4 + i] = w[o + 5 + i];
+  const uint32_t d0 = w[o] & 0xFFFFu, d1 = w[o + 4] >> 16;
+  const __half2 dd[2] = {u32_as_h2(d0 | (d0 << 16)), u32_as_h2(d1 | (d1 << 16))};
+#pragma unroll
+  for (int b = 0; b < 2; ++b) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t t0 = prmt(q[4 * b + i], q[4 * b + i], 0x0100u);  // byte0 = byte 4i, byte2 = byte 4i+1
+      const uint32_t t1 = prmt(q[4 * b + i], q[4 * b + i], 0x0302u);  // bytes 4i+2, 4i+3
+      const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u);  // {1024 + q}
+      const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
+      const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}
+      const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
+      out[16 * b + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l01), b1032), dd[b]));
+      out[16 * b + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(l23), b1032), dd[b]));
+      out[16 * b + 8 + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h01), b72), dd[b]));
+      out[16 * b + 8 + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(h23), b72), dd[b]));
+    }
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ OutT to_out(float v);
+template <>
+__device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float to_out<float>(float v) { return v; }
+
+// Dequantize this thread's weight row r (0..127) of one unit held in a
+// weight stage (the TMA box of the unit: Q4_K / Q4_0G 128 x 144 B rows;
+// Q4_0 128 x 128 B of nibbles with the 128-byte swizzle, then 128 x 8 fp16
+// scales at kQ40ScaleOffset) and store it as the unit's 128 TMEM operand
+// columns from `a_slot` (this warp's lane quarter already in the address):
+// column 32*cc + c holds k = 64*cc + 2c, 2c+1 as an fp16 pair. The caller
+// waits for the stores (tcgen05.wait::st) before publishing the slot.
+template <WFmt FMT>
+__device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, int r, uint32_t a_slot) {
+  if constexpr (FMT == WFmt::Q4K) {
+    // this row's block header: d, dmin and the 6-bit scales/mins of its
+    // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
+    // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7
+    const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
+    const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+#pragma unroll 1
+    for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+      // chunk cc covers sub-blocks 2cc, 2cc+1: bytes 2(cc&1), 2(cc&1)+1 of the
+      // _lo words (cc < 2) or of the _hi words (cc >= 2)
+      const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
+      const uint32_t mw = cc < 2 ? m_lo : m_hi;
+      const int sh = 16 * (cc & 1);
+      const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
+      const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
+      const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
+      const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
+      const uint8_t* qs = stage + r * kQ4KBlockBytes + 16 + cc * 32;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
+      uint32_t P[32];
+      dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
+      tmem_st_x32(a_slot + cc * 32, P);
+    }
+  } else if constexpr (FMT == WFmt::Q4_0G) {
+    const uint8_t* urow = stage + r * kQ4KBlockBytes;
+    uint32_t P[32];
+    auto chunk = [&](auto cc_tag) {
+      constexpr int cc = decltype(cc_tag)::value;
+      constexpr int v0 = (36 * cc) / 16;  // first 16-byte load covering the chunk
+      uint32_t w[12];
+#pragma unroll
+      for (int v = 0; v < 3; ++v) {
+        const uint4 x = *reinterpret_cast<const uint4*>(urow + 16 * (v0 + v));
+        w[4 * v] = x.x; w[4 * v + 1] = x.y; w[4 * v + 2] = x.z; w[4 * v + 3] = x.w;
+      }
+      dequant_q4_0g_chunk<(36 * cc % 16) / 4>(w, P);
+      tmem_st_x32(a_slot + cc * 32, P);
+    };
+    chunk(std::integral_constant<int, 0>{});
+    chunk(std::integral_constant<int, 1>{});
+    chunk(std::integral_constant<int, 2>{});
+    chunk(std::integral_constant<int, 3>{});
+  } else {
+    const uint8_t* wrow = stage + r * 128;
+    const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
+    const uint4 dd = *reinterpret_cast<const uint4*>(stage + kQ40ScaleOffset + r * 16);  // 8 block scales
+#pragma unroll 1
+    for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+      uint32_t P[32];
+      const uint4 b0 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc)) ^ sw) << 4));
+      const uint4 b1 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc + 1)) ^ sw) << 4));
+      const __half2 d01 = u32_as_h2(cc == 0 ? dd.x : cc == 1 ? dd.y : cc == 2 ? dd.z : dd.w);
+      dequant_q4_0_block(b0, __low2half2(d01), P);
+      dequant_q4_0_block(b1, __high2half2(d01), P + 16);
+      tmem_st_x32(a_slot + cc * 32, P);
+    }
+  }
+}
+
+}  // namespace busfill

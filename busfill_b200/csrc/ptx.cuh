@@ -201,6 +201,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* desc, int3
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* desc, int32_t x, int32_t y, int32_t z,
+                                            uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // ----------------------------------------------------------------------------
 // tcgen05
 // ----------------------------------------------------------------------------
