@@ -20,7 +20,7 @@ import re
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
-    "stream_status", "stream_status_bits", "set_pdl", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -114,6 +114,12 @@ def set_ksplit(csize: int) -> None:
     """Force the number of CTAs (cluster size, 1..8) that split each 128-row
     tile along K; 0 restores the library's own choice."""
     _check(_lib().busfill_set_option(2, int(csize)), "busfill_set_option")
+
+
+def set_prefill_min_m(m: int) -> None:
+    """GEMMs with at least `m` batch rows take the large-batch (prefill)
+    kernel; 0 restores the default threshold."""
+    _check(_lib().busfill_set_option(3, int(m)), "busfill_set_option")
 
 
 # ---------------------------------------------------------------------------

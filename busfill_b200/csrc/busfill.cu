@@ -15,6 +15,7 @@
 
 #include "busfill.h"
 #include "decode_gemm.cuh"
+#include "prefill_gemm.cuh"
 #include "dequant.cuh"
 
 using namespace busfill;
@@ -34,6 +35,10 @@ constexpr int kVersion = 100;  // 0.1.0
 std::atomic<unsigned> g_last_detail{0};
 std::atomic<int> g_use_pdl{1};
 std::atomic<int> g_force_ksplit{0};  // 0 = automatic
+// Batches of at least this many rows take the prefill kernel (one pass over
+// the weights for all rows); smaller ones the decode kernel (32 rows a launch).
+constexpr int kDefaultPrefillMinM = 128;
+std::atomic<int> g_prefill_min_m{kDefaultPrefillMinM};
 
 // ---------------------------------------------------------------------------
 // device properties (cached)
@@ -329,6 +334,68 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
   return BUSFILL_OK;
 }
 
+// ---------------------------------------------------------------------------
+// prefill GEMM launch
+// ---------------------------------------------------------------------------
+template <WFmt FMT, typename OutT>
+int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
+                int M, int N, int K, unsigned* error, cudaStream_t s) {
+  const int S = K / kUnitK;
+  CUtensorMap tw, tws, ta;
+  std::memset(&tws, 0, sizeof(tws));
+  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4_0G) {
+    const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes,
+                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    tws = tw;
+  } else {
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return BUSFILL_ERR_CUDA;
+    if (!make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)K / 32, (uint64_t)N, (uint64_t)K / 16, 8,
+                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+  }
+  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, prefill::kBatchTile, kChunksPerUnit)) return BUSFILL_ERR_CUDA;
+
+  const void* kern = reinterpret_cast<const void*>(prefill_gemm_kernel<FMT, OutT>);
+  {
+    static std::once_flag once[64];
+    static cudaError_t err[64];
+    std::call_once(once[dev & 63], [&] {
+      err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::kAlloc);
+    });
+    if (err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
+  }
+  prefill::Params p;
+  p.c = c;
+  p.error = error;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.pairs = (N + prefill::kPairRows - 1) / prefill::kPairRows;
+  p.btiles = (M + prefill::kBatchTile - 1) / prefill::kBatchTile;
+  p.units = S;
+  const long long items = (long long)p.pairs * p.btiles;
+  const int grid = (int)std::min<long long>(items, di.sm_count);
+  void* args[] = {&tw, &tws, &ta, &p};
+  if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::kAlloc, s, args, g_use_pdl.load() != 0) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_LAUNCH;
+  }
+  return BUSFILL_OK;
+}
+
+// Decode (M < prefill threshold) or prefill kernel for one GEMM.
+template <WFmt FMT, typename OutT>
+int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
+             int N, int K, unsigned* error, cudaStream_t s) {
+  if (M >= g_prefill_min_m.load()) return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
+  return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
+}
+
 template <WFmt FMT, typename OutT>
 int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M, int N, int K,
               cudaStream_t s) {
@@ -344,7 +411,7 @@ int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, 
     st = get_error_words(dev, s, &err);
   }
   if (st != BUSFILL_OK) return st;
-  return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, err, s);
+  return run_gemm<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, err, s);
 }
 
 int grid_for(long long work, int sm_count) {
@@ -391,7 +458,7 @@ int gemm_q4k_static(const uint8_t* w, const uint16_t* a, uint16_t* c, int M, int
     cudaGetLastError();
     return BUSFILL_ERR_CUDA;
   }
-  return run_decode<WFmt::Q4K, __half>(di, dev, w, nullptr, a, c, M, N, K, reinterpret_cast<unsigned*>(scratch), s);
+  return run_gemm<WFmt::Q4K, __half>(di, dev, w, nullptr, a, c, M, N, K, reinterpret_cast<unsigned*>(scratch), s);
 }
 
 }  // namespace
@@ -428,6 +495,11 @@ int busfill_set_option(int option, int value) {
   if (option == BUSFILL_OPT_KSPLIT) {
     if (value < 0 || value > 8) return BUSFILL_ERR_INVALID_ARG;
     g_force_ksplit.store(value);
+    return BUSFILL_OK;
+  }
+  if (option == BUSFILL_OPT_PREFILL_MIN_M) {
+    if (value < 0) return BUSFILL_ERR_INVALID_ARG;
+    g_prefill_min_m.store(value == 0 ? kDefaultPrefillMinM : value);
     return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;

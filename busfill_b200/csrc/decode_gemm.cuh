@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (i >= kSlots && !warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       tc_fence_after();
       const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
-      dequant_unit_row<FMT>(stage, r, tmem + lane_off + TM::kA + (i % kSlots) * 128);
+      dequant_unit_row<FMT>(stage, stage + kQ40ScaleOffset, r, tmem + lane_off + TM::kA + (i % kSlots) * 128);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();

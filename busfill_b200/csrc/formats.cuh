@@ -127,15 +127,18 @@ __device__ __forceinline__ __half to_out<__half>(float v) { return __float2half_
 template <>
 __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
-// Dequantize this thread's weight row r (0..127) of one unit held in a
-// weight stage (the TMA box of the unit: Q4_K / Q4_0G 128 x 144 B rows;
-// Q4_0 128 x 128 B of nibbles with the 128-byte swizzle, then 128 x 8 fp16
-// scales at kQ40ScaleOffset) and store it as the unit's 128 TMEM operand
-// columns from `a_slot` (this warp's lane quarter already in the address):
-// column 32*cc + c holds k = 64*cc + 2c, 2c+1 as an fp16 pair. The caller
-// waits for the stores (tcgen05.wait::st) before publishing the slot.
-template <WFmt FMT>
-__device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, int r, uint32_t a_slot) {
+// Dequantize chunks [C0, C1) of this thread's weight row r of one unit held
+// in a weight stage (the TMA box of the unit: Q4_K / Q4_0G rows of 144 B;
+// Q4_0 rows of 128 B of nibbles with the 128-byte swizzle, and 8 fp16 scales
+// per row at `q40_scales` + 16 r) and store them as TMEM operand columns from
+// `a_slot` (this warp's lane quarter already in the address): chunk cc goes
+// to columns 32 (cc - C0) .. +31, column c of a chunk holding k = 64 cc + 2c,
+// 2c+1 as an fp16 pair. The caller waits for the stores (tcgen05.wait::st)
+// before publishing the slot.
+template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
+__device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* q40_scales, int r,
+                                                 uint32_t a_slot) {
+  static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
   if constexpr (FMT == WFmt::Q4K) {
     // this row's block header: d, dmin and the 6-bit scales/mins of its
     // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
@@ -148,7 +151,7 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, int r, ui
     const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
     const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
 #pragma unroll 1
-    for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+    for (int cc = C0; cc < C1; ++cc) {
       // chunk cc covers sub-blocks 2cc, 2cc+1: bytes 2(cc&1), 2(cc&1)+1 of the
       // _lo words (cc < 2) or of the _hi words (cc >= 2)
       const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
@@ -163,7 +166,7 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, int r, ui
       const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
       uint32_t P[32];
       dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
-      tmem_st_x32(a_slot + cc * 32, P);
+      tmem_st_x32(a_slot + (cc - C0) * 32, P);
     }
   } else if constexpr (FMT == WFmt::Q4_0G) {
     const uint8_t* urow = stage + r * kQ4KBlockBytes;
@@ -178,25 +181,25 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, int r, ui
         w[4 * v] = x.x; w[4 * v + 1] = x.y; w[4 * v + 2] = x.z; w[4 * v + 3] = x.w;
       }
       dequant_q4_0g_chunk<(36 * cc % 16) / 4>(w, P);
-      tmem_st_x32(a_slot + cc * 32, P);
+      tmem_st_x32(a_slot + (cc - C0) * 32, P);
     };
-    chunk(std::integral_constant<int, 0>{});
-    chunk(std::integral_constant<int, 1>{});
-    chunk(std::integral_constant<int, 2>{});
-    chunk(std::integral_constant<int, 3>{});
+    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
+    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
+    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
+    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
   } else {
     const uint8_t* wrow = stage + r * 128;
     const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
-    const uint4 dd = *reinterpret_cast<const uint4*>(stage + kQ40ScaleOffset + r * 16);  // 8 block scales
+    const uint4 dd = *reinterpret_cast<const uint4*>(q40_scales + r * 16);  // 8 block scales
 #pragma unroll 1
-    for (int cc = 0; cc < kChunksPerUnit; ++cc) {
+    for (int cc = C0; cc < C1; ++cc) {
       uint32_t P[32];
       const uint4 b0 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc)) ^ sw) << 4));
       const uint4 b1 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc + 1)) ^ sw) << 4));
       const __half2 d01 = u32_as_h2(cc == 0 ? dd.x : cc == 1 ? dd.y : cc == 2 ? dd.z : dd.w);
       dequant_q4_0_block(b0, __low2half2(d01), P);
       dequant_q4_0_block(b1, __high2half2(d01), P + 16);
-      tmem_st_x32(a_slot + cc * 32, P);
+      tmem_st_x32(a_slot + (cc - C0) * 32, P);
     }
   }
 }

@@ -1,0 +1,355 @@
+// Dequant-fused 4-bit-weight GEMM for large batches (prefill, M >= ~128) on
+// sm_100a: C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 in, fp32 accumulate.
+//
+// The same contraction as the decode kernel (decode_gemm.cuh), in the regime
+// where it turns compute-bound: at M = 2048 the work is 2 M N K flops against
+// one pass of 4.5-bit weights, so the tensor pipe, not HBM, sets the time.
+// The reference has no such path (its kernel computes batch rows < 32 only,
+// kernels/busfill_v1a.cu:41-104); the shapes are BASELINE config 4.
+//
+// Shape of the computation. A work item is two 128-row weight tiles (256
+// weight rows) x 128 batch rows, looped over K in units of 256. The weights
+// of a unit are dequantized into tensor memory (the MMA's A operand, one
+// 128-lane tile per weight tile) and each tile's accumulator [128 weight rows
+// x 128 batch rows] fp32 lives in TMEM next to them:
+//   columns   0..127  accumulator of weight tile 0
+//   columns 128..255  accumulator of weight tile 1
+//   columns 256..511  four half-unit operand slots (t, h) of 64 columns:
+//                     tile t, K half h (chunks 2h, 2h+1) of the current unit.
+// The MMAs of a unit run (t0,h0) (t1,h0) (t0,h1) (t1,h1), 8 MMAs of
+// 128x128x16 each, so a half slot is refilled while the three other MMA
+// blocks run. Activations come as one 3-D TMA box per unit (4 chunks x 128
+// rows x 64 values, 64 KB) and weights as one box per unit for both tiles
+// (256 rows, 36 KB): an SM's TMA unit takes a roughly fixed time per box
+// (~0.5 us with every SM loading, measured on B200), so few large boxes.
+//
+// Measured on B200: a 128x128x16 TS MMA (A in TMEM) takes ~74 cycles back to
+// back, 92% of the dense fp16 rate; a unit (32 MMAs) ~2400 cycles.
+//
+// Warp roles (16 warps, one CTA per SM, persistent over work items):
+//   0      weight TMA producer (2-stage ring of 36 KB)
+//   1      activation TMA producer (2-stage ring of 64 KB); TMEM allocator
+//   3      MMA issuer (converged warp, one elected thread issues)
+//   4-7    dequant of weight tile 0, 8-11 of weight tile 1: thread (warp%4,
+//          lane) owns tile row 32*(warp%4)+lane, both K halves of each unit
+//   12-15  epilogue: reads both accumulators once per item, writes C
+//   2      idle
+//
+// Work order: item = pair * B + batch_tile, so the CTAs running at the same
+// time share weight tiles (one HBM read, the rest from L2) and stream the
+// activations, which stay L2-resident (evict-last hint).
+//
+// Every wait is bounded (ptx.cuh: kWaitTimeoutNs).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "formats.cuh"
+#include "ptx.cuh"
+
+namespace busfill {
+
+namespace prefill {
+
+constexpr int kThreads = 512;
+constexpr int kBatchTile = 128;                 // batch rows per item = MMA N
+constexpr int kPairRows = 2 * kTileRows;        // weight rows per item
+constexpr int kWStages = 2;
+constexpr int kXStages = 2;
+constexpr int kWStage = 2 * kWStageBytes;       // both tiles' unit (Q4_0: 32 KB nibbles, then 4 KB scales)
+constexpr int kQ40Scales = 2 * kQ40ScaleOffset; // Q4_0: scales of the 256 rows after the nibbles
+constexpr int kXChunk = kBatchTile * 128;       // 64 values x 128 rows, 16 KB
+constexpr int kXStage = kChunksPerUnit * kXChunk;
+constexpr int kAccCols = kBatchTile;            // per weight tile
+constexpr int kSlotCols = 64;                   // half a unit
+constexpr int kSlot0 = 2 * kAccCols;
+constexpr int kTmemCols = 512;
+static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
+
+// shared memory map
+constexpr int kWOff = 0;
+constexpr int kXOff = kWOff + kWStages * kWStage;
+constexpr int kBarOff = kXOff + kXStages * kXStage;
+constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
+constexpr int bXFull = bWEmpty + kWStages, bXEmpty = bXFull + kXStages;
+constexpr int bReady = bXEmpty + kXStages;      // half slot s = 2t + h filled (4 dequant warps of tile t)
+constexpr int bSDone = bReady + 4;              // half slot s read by its MMAs (commit)
+constexpr int bAccFull = bSDone + 4, bAccEmpty = bAccFull + 1, bFinal = bAccEmpty + 1;
+constexpr int kNumBars = bFinal + 1;
+constexpr int kMiscOff = kBarOff + kNumBars * 8;
+constexpr int kBytes = kMiscOff + 64;
+constexpr int kAlloc = kBytes + 1024;
+static_assert(kXOff % 1024 == 0 && kXStage % 1024 == 0, "swizzled operands need 1 KB alignment");
+static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
+
+struct Params {
+  void* c;            // [M, N] row-major, OutT
+  unsigned* error;    // device error word (+1: first failure record)
+  int M, N, K;
+  int pairs;          // P = ceil(N / 256)
+  int btiles;         // B = ceil(M / 128)
+  int units;          // S = K / 256
+};
+
+}  // namespace prefill
+
+template <WFmt FMT, typename OutT>
+__global__ void __launch_bounds__(prefill::kThreads, 1)
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
+                        const __grid_constant__ CUtensorMap tmap_a, const prefill::Params p) {
+  using namespace prefill;
+  constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, kBatchTile);
+  constexpr bool kRows144 = (FMT != WFmt::Q4_0);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_s = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + (((raw_s + 1023u) & ~1023u) - raw_s);
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + kBarOff;
+  auto BAR = [&](int slot) { return bar0 + 8u * (uint32_t)slot; };
+  uint32_t* misc = reinterpret_cast<uint32_t*>(smem + kMiscOff);  // [0] tmem base
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.units;
+  const int items = p.pairs * p.btiles;
+  const int my_items = (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int nunits = my_items * S;
+  auto item_of = [&](int j) { return (int)blockIdx.x + j * (int)gridDim.x; };
+
+  bool ok = true;
+  int diag_unit = -1;
+  auto warp_wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    if (!ok) return false;
+    ok = __all_sync(0xffffffffu, mbar_wait(bar, parity));
+    if (!ok && lane == 0) {
+      const unsigned rec = 0x80000000u | ((unsigned)warp << 24) | ((unsigned)(diag_unit & 0xFFF) << 12) |
+                           (((bar - bar0) / 8u) << 1) | parity;
+      atomicCAS(p.error + 1, 0u, rec);
+    }
+    return ok;
+  };
+  auto bar_count = [&](int b) -> uint32_t {
+    if (b >= bWEmpty && b < bWEmpty + kWStages) return 8;  // both tiles' dequant warps
+    if (b >= bReady && b < bReady + 4) return 4;           // the tile's dequant warps
+    if (b == bAccEmpty) return 4;                          // the epilogue warps
+    return 1;                                              // TMA expect_tx arrivals, MMA commits
+  };
+
+  // weight TMA of unit u (item j = u / S, unit k = u % S) into stage u % kWStages
+  auto issue_w = [&](int u) {
+    const int it = item_of(u / S), k = u % S;
+    const int pair = it / p.btiles;
+    const int s = u % kWStages;
+    const uint32_t dst = sbase + kWOff + s * kWStage;
+    mbar_arrive_expect_tx(BAR(bWFull + s), kWStage);
+    if constexpr (kRows144) {
+      tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+    } else {
+      tma_load_2d(dst, &tmap_w, k * 128, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+      tma_load_2d(dst + kQ40Scales, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+    }
+  };
+  auto issue_x = [&](int u) {
+    const int it = item_of(u / S), k = u % S;
+    const int bt = it % p.btiles;
+    const int s = u % kXStages;
+    mbar_arrive_expect_tx(BAR(bXFull + s), kXStage);
+    tma_load_3d(sbase + kXOff + s * kXStage, &tmap_a, 0, bt * kBatchTile, k * kChunksPerUnit, BAR(bXFull + s),
+                kPolicyEvictLast);
+  };
+
+  // set-up: barriers by warp 0's lanes, the first weight stages before the
+  // CTA-wide sync (weights never depend on an earlier kernel)
+  const int w_early = nunits < kWStages ? nunits : kWStages;
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_w);
+      if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
+      tma_prefetch_desc(&tmap_a);
+    }
+    for (int b = lane; b < kNumBars; b += 32) mbar_init(BAR(b), bar_count(b));
+    fence_mbar_init();
+    __syncwarp();
+    if (lane < w_early) issue_w(lane);
+    __syncwarp();
+  } else if (warp == 1) {
+    tmem_alloc(sbase + kMiscOff, prefill::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = misc[0];
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- weight producer ----------------
+    int issued = w_early;
+    for (int u = w_early; u < nunits; ++u) {
+      diag_unit = u;
+      if (!warp_wait(BAR(bWEmpty + u % kWStages), ((u / kWStages) & 1) ^ 1)) break;
+      if (elect_one()) issue_w(u);
+      __syncwarp();
+      issued = u + 1;
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrWeightProducer);
+    ok = true;
+    for (int u = issued > kWStages ? issued - kWStages : 0; u < issued; ++u)
+      if (!warp_wait(BAR(bWFull + u % kWStages), (u / kWStages) & 1)) {
+        if (lane == 0) atomicOr(p.error, kErrTeardown);
+        break;
+      }
+  } else if (warp == 1) {
+    // ---------------- activation producer ----------------
+    pdl_wait_prerequisites();  // activations may be the previous kernel's output
+    int issued = 0;
+    for (int u = 0; u < nunits; ++u) {
+      diag_unit = u;
+      if (u >= kXStages && !warp_wait(BAR(bXEmpty + u % kXStages), ((u / kXStages) & 1) ^ 1)) break;
+      if (elect_one()) issue_x(u);
+      __syncwarp();
+      issued = u + 1;
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrActProducer);
+    ok = true;
+    for (int u = issued > kXStages ? issued - kXStages : 0; u < issued; ++u)
+      if (!warp_wait(BAR(bXFull + u % kXStages), (u / kXStages) & 1)) {
+        if (lane == 0) atomicOr(p.error, kErrTeardown);
+        break;
+      }
+  } else if (warp == 3) {
+    // ---------------- MMA issuer ----------------
+    const uint64_t bdesc0 = make_sdesc_sw128(sbase + kXOff);
+    for (int u = 0; u < nunits; ++u) {
+      diag_unit = u;
+      const int j = u / S, k = u % S;
+      // the accumulators are free once the epilogue has read item j - 1
+      if (k == 0 && j >= 1 && !warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1))) break;
+      if (!warp_wait(BAR(bXFull + u % kXStages), (u / kXStages) & 1)) break;
+      const uint64_t bx = bdesc0 + (uint64_t)(((u % kXStages) * kXStage) >> 4);
+      bool good = true;
+#pragma unroll 1
+      for (int h = 0; h < 2 && good; ++h) {
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) {
+          const int sl = 2 * t + h;
+          if (!warp_wait(BAR(bReady + sl), (uint32_t)(u & 1))) { good = false; break; }
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t d_acc = tmem + (uint32_t)(t * kAccCols);
+            const uint32_t a_t = tmem + (uint32_t)(kSlot0 + sl * kSlotCols);
+#pragma unroll
+            for (int cl = 0; cl < 2; ++cl)
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks,
+                           bx + (uint64_t)((((2 * h + cl) * kXChunk) + 32 * ks) >> 4), kIdesc,
+                           (k == 0 && h == 0 && cl == 0 && ks == 0) ? 0u : 1u);
+            tc_commit(BAR(bSDone + sl));  // half slot free once these MMAs complete
+          }
+          __syncwarp();
+        }
+      }
+      if (!good) break;
+      if (elect_one()) {
+        tc_commit(BAR(bXEmpty + u % kXStages));        // activation stage free
+        if (k == S - 1) tc_commit(BAR(bAccFull));      // item's accumulators complete
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrMma);
+    if (elect_one()) tc_commit(BAR(bFinal));
+    __syncwarp();
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------- dequant (tile t = group) ----------------
+    const int q = warp & 3;
+    const int t = (warp - 4) >> 2;
+    const int r = q * 32 + lane;
+    const int row = t * kTileRows + r;       // row within the 256-row weight stage
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    for (int u = 0; u < nunits; ++u) {
+      diag_unit = u;
+      const int ws = u % kWStages;
+      if (!warp_wait(BAR(bWFull + ws), (u / kWStages) & 1)) break;
+      const uint8_t* stage = smem + kWOff + ws * kWStage;
+      bool good = true;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        const int sl = 2 * t + h;
+        // half slot sl is free once the MMAs of the previous unit read it
+        if (u >= 1 && !warp_wait(BAR(bSDone + sl), (uint32_t)((u - 1) & 1))) { good = false; break; }
+        tc_fence_after();
+        const uint32_t a_col = tmem + lane_off + (uint32_t)(kSlot0 + sl * kSlotCols);
+        if (h == 0)
+          dequant_unit_row<FMT, 0, 2>(stage, stage + kQ40Scales, row, a_col);
+        else
+          dequant_unit_row<FMT, 2, 4>(stage, stage + kQ40Scales, row, a_col);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(BAR(bReady + sl));
+      }
+      if (!good) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(bWEmpty + ws));
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrDequant);
+  } else if (warp >= 12) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    OutT* C = reinterpret_cast<OutT*>(p.c);
+    bool waited_pdl = false;
+    for (int j = 0; j < my_items; ++j) {
+      diag_unit = j * S + S - 1;
+      const int it = item_of(j);
+      const int pair = it / p.btiles, bt = it % p.btiles;
+      const bool have = warp_wait(BAR(bAccFull), (uint32_t)(j & 1));
+      tc_fence_after();
+      if (!waited_pdl) {
+        pdl_wait_prerequisites();  // C may still be read by the previous kernel
+        waited_pdl = true;
+      }
+#pragma unroll 1
+      for (int t = 0; t < 2; ++t) {
+        const int n = pair * kPairRows + t * kTileRows + r;
+#pragma unroll 1
+        for (int cb = 0; cb < kBatchTile; cb += 32) {
+          uint32_t x[32];
+          tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb), x);
+          tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb + 16), x + 16);
+          tc_wait_ld();
+          if (have && n < p.N) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int b = bt * kBatchTile + cb + i;
+              if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(__uint_as_float(x[i]));
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(BAR(bAccEmpty));
+    }
+    if (!ok && lane == 0) atomicOr(p.error, kErrEpilogue);
+  }
+
+  // ---------------- teardown ----------------
+  __syncwarp();
+  __syncthreads();
+  if (warp == 1) {
+    bool done = true;
+    if (lane == 0) done = mbar_wait(BAR(bFinal), 0);
+    done = __shfl_sync(0xffffffffu, done ? 1 : 0, 0) != 0;
+    if (!done && lane == 0) atomicOr(p.error, kErrTeardown);
+    tc_fence_after();
+    tmem_dealloc(tmem, prefill::kTmemCols);
+  }
+}
+
+}  // namespace busfill

@@ -169,9 +169,14 @@ BUSFILL_API int busfill_version(void);
  *   BUSFILL_OPT_KSPLIT: 0 (default) lets the library choose how many CTAs (a
  *     thread-block cluster of 1..8) split the K range of each 128-row tile;
  *     1..8 forces that split where K/256 allows it (a tuning and test knob).
+ *   BUSFILL_OPT_PREFILL_MIN_M: GEMMs with M >= value rows run the large-batch
+ *     (prefill) kernel, one pass over the weights for all rows, instead of
+ *     the decode kernel's launches of 32 rows; 0 restores the default (128).
+ *     A tuning and test knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
+#define BUSFILL_OPT_PREFILL_MIN_M 3
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the

@@ -1,0 +1,126 @@
+"""GPU parity of the large-batch (prefill) kernel, through the C ABI.
+
+Batches of at least the prefill threshold (default 128 rows) run one pass over
+the weights for all rows; the decode kernel covers smaller batches. These
+tests run the prefill kernel at its own shapes, force it onto small and
+ragged shapes (BUSFILL_OPT_PREFILL_MIN_M), and check the BASELINE config-4
+shapes at full size on sampled rows and columns against the oracle.
+Gates as in test_gpu_parity: max abs err <= 0.6 and rel-L2 <= 1e-3 against
+an fp32 matmul of the dequantized weights, plus a tighter fp64 check.
+"""
+import numpy as np
+import pytest
+
+from oracle import q4_oracle as orc
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+import busfill_b200 as bf  # noqa: E402
+
+DEV = "cuda:0"
+TIGHT_REL_L2 = 5e-4
+
+
+def cu(x):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(DEV)
+
+
+def check(c_dev, a, w_ref, w_exact):
+    c = c_dev.float().cpu().numpy()
+    cref = orc.gemm_ref(a, w_ref)
+    max_abs, rel, finite = orc.gemm_errors(c, cref)
+    assert finite and max_abs <= orc.GATE_MAX_ABS and rel <= orc.GATE_REL_L2, (max_abs, rel)
+    exact = a.astype(np.float64) @ w_exact.astype(np.float64).T
+    _, rel_t, _ = orc.gemm_errors(c, exact)
+    assert rel_t <= TIGHT_REL_L2, rel_t
+
+
+@pytest.fixture
+def prefill_always():
+    bf.set_prefill_min_m(1)
+    try:
+        yield
+    finally:
+        bf.set_prefill_min_m(0)
+
+
+PREFILL_SHAPES = [
+    (128, 512, 512), (130, 384, 768), (256, 1280, 1024), (300, 640, 2048), (257, 200, 256), (512, 2304, 1536),
+]
+
+
+@pytest.mark.parametrize("m,n,k", PREFILL_SHAPES)
+def test_prefill_q4k(m, n, k):
+    blocks = orc.gen_q4k(n, k, seed=m + 3 * n + k)
+    a = orc.gen_activations(m, k, seed=m * 7 + k)
+    c = bf.gemm_q4k(cu(blocks), cu(a))
+    assert bf.stream_status() == 0
+    w32 = orc.dequant_q4k_f32(blocks, k)
+    check(c, a, w32, w32)
+
+
+@pytest.mark.parametrize("m,n,k", PREFILL_SHAPES)
+def test_prefill_q4_0_planes_and_ggml(m, n, k):
+    """Both Q4_0 layouts give the same fp16 operands, so the same bits."""
+    wq, ws = orc.gen_q4_0(n, k, seed=m + 5 * n + k)
+    blocks = orc.q4_0_planes_to_ggml_blocks(wq, ws)
+    a = orc.gen_activations(m, k, seed=m * 11 + k)
+    c = bf.gemm_q4_0(cu(wq), cu(ws), cu(a))
+    cg = bf.gemm_q4_0_ggml(cu(blocks), cu(a))
+    assert bf.stream_status() == 0
+    assert torch.equal(c.view(torch.int16), cg.view(torch.int16))
+    check(c, a, orc.dequant_q4_0_planes_f32(wq, ws), orc.dequant_q4_0_planes(wq, ws))
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 128, 256), (17, 200, 512), (33, 1024, 2048), (64, 256, 5120)])
+def test_prefill_forced_on_small_batches(prefill_always, m, n, k):
+    blocks = orc.gen_q4k(n, k, seed=m + n)
+    wq, ws = orc.gen_q4_0(n, k, seed=m + 2 * n)
+    a = orc.gen_activations(m, k, seed=m + k)
+    c = bf.gemm_q4k(cu(blocks), cu(a))
+    c0 = bf.gemm_q4_0(cu(wq), cu(ws), cu(a))
+    assert bf.stream_status() == 0
+    w32 = orc.dequant_q4k_f32(blocks, k)
+    check(c, a, w32, w32)
+    check(c0, a, orc.dequant_q4_0_planes_f32(wq, ws), orc.dequant_q4_0_planes(wq, ws))
+
+
+def test_prefill_matches_decode_kernel(prefill_always):
+    """Same GEMM through both kernels: they accumulate in different orders, so
+    compare within a few fp16 ulps of the output."""
+    m, n, k = 96, 640, 3072
+    blocks = orc.gen_q4k(n, k, seed=5)
+    a = cu(orc.gen_activations(m, k, seed=6))
+    cp = bf.gemm_q4k(cu(blocks), a).float()
+    bf.set_prefill_min_m(10 ** 6)
+    cd = bf.gemm_q4k(cu(blocks), a).float()
+    assert bf.stream_status() == 0
+    assert torch.allclose(cp, cd, rtol=2e-3, atol=2e-3)
+
+
+def test_prefill_fp32_reference_surface(prefill_always):
+    """busfill_q4 (fp32 output, the reference's argument order) on the prefill path."""
+    m, n, k = 40, 256, 512
+    wq, ws = orc.gen_q4_0(n, k, seed=41)
+    a = orc.gen_activations(m, k, seed=42)
+    c = torch.empty((m, n), dtype=torch.float32, device=DEV)
+    bf.busfill_q4(cu(a), cu(wq), cu(ws), c, m, k, n)
+    assert bf.stream_status() == 0
+    check(c, a, orc.dequant_q4_0_planes_f32(wq, ws), orc.dequant_q4_0_planes(wq, ws))
+
+
+@pytest.mark.parametrize("m,n,k", [(2048, 5120, 17408), (2048, 17408, 5120), (512, 5120, 17408)])
+def test_prefill_config4_sampled(m, n, k):
+    """BASELINE config 4 at full size: the whole output is computed, and a
+    sample of 64 rows x 512 columns is checked against the oracle."""
+    blocks = orc.gen_q4k(n, k, seed=m + n + k)
+    a = orc.gen_activations(m, k, seed=m + k)
+    c = bf.gemm_q4k(cu(blocks), cu(a))
+    assert bf.stream_status() == 0
+    rng = np.random.default_rng(m + n)
+    rows = np.sort(rng.choice(m, 64, replace=False))
+    cols = np.sort(rng.choice(n, 512, replace=False))
+    w32 = orc.dequant_q4k_f32(blocks[cols], k)
+    check(c[rows][:, cols], a[rows], w32, w32)
+    assert torch.isfinite(c.float()).all()
