@@ -307,6 +307,7 @@ def run_busfill(args):
         out["isolated_no_pdl"] = isolated_no_pdl(bf, capture, time_graph, min(steps, 50), R, M)
         out["sweep"] = sweep(torch, bf, dev, l2, hbm_peak, args)
         out["cublas_fp16"] = cublas_comparator(torch, bf, dev, l2, weights, a, args)
+        out["config4_prefill"] = config4(torch, bf, dev, args, hbm_peak, tc_peak, peak_src)
         out["e2e"] = e2e(torch, bf, dev, weights, a, args, max(10, steps // 10))
         out["cpu_baseline"] = cpu_baseline(args)
     elif world > 1:
@@ -398,6 +399,53 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         del g, ws
         torch.cuda.empty_cache()
     return rows
+
+
+def config4(torch, bf, dev, args, hbm_peak, tc_peak, peak_src):
+    """Q4_K down-proj (K=17408, N=5120) and up-proj
+    (K=5120, N=17408) at M in {1, 128, 512, 2048}, through the default
+    dispatch (prefill kernel for large batches, decode kernel otherwise),
+    against the tensor roofline (2 M N K flops) and the HBM roofline
+    (algorithmic bytes), with cuBLAS fp16 on the dequantized weights beside it.
+    Each GEMM is timed alone (CUDA events around 5 back-to-back calls after 2
+    warm-up calls; the weights, 50 MB, are re-read every call)."""
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 4)
+    rows = []
+    st = torch.cuda.Stream(device=dev)
+
+    def timed(fn, it=5):
+        with torch.cuda.stream(st):
+            for _ in range(2):
+                fn()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(it):
+                fn()
+            e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / it
+
+    for k, n in ((17408, 5120), (5120, 17408)):
+        w = make_q4k_weights(torch, n, k, gen, dev)
+        w16 = bf.dequant_q4k(w, k, stream=st)
+        for m in (1, 128, 512, 2048):
+            a = torch.randn((m, k), device=dev, generator=gen).half()
+            c = torch.empty((m, n), dtype=torch.float16, device=dev)
+            us = timed(lambda: bf.gemm_q4k(w, a, out=c, stream=st))
+            assert bf.stream_status(st) == 0
+            us_cb = timed(lambda: torch.matmul(a, w16.t(), out=c))
+            fl = 2.0 * m * n * k
+            tf = fl / (us * 1e-6) / 1e12
+            gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
+            rows.append({"M": m, "N": n, "K": k, "kernel": "prefill" if bf.uses_prefill(m, n) else "decode",
+                         "us": round(us, 2), "tflops": round(tf, 1), "tensor_frac": round(tf / tc_peak, 4),
+                         "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 4),
+                         "cublas_fp16_us": round(us_cb, 2)})
+        del w, w16
+        torch.cuda.empty_cache()
+    return {"rows": rows, "tensor_peak_tflops": tc_peak, "hbm_peak_gbs": hbm_peak, "peak_source": peak_src,
+            "note": "tensor_frac against the measured dense bf16 cuBLAS peak (burst); fp16 runs at the same rate"}
 
 
 def cublas_comparator(torch, bf, dev, l2, weights, a, args):

@@ -20,7 +20,7 @@ import re
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
-    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "uses_prefill", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -73,6 +73,7 @@ _SIGS = {
     "busfill_version": [],
     "busfill_set_option": [_I, _I],
     "busfill_probe_umma": [_P, _P, _P, _I, _P],
+    "busfill_gemm_kernel_for": [_I, _I],
 }
 
 
@@ -114,6 +115,11 @@ def set_ksplit(csize: int) -> None:
     """Force the number of CTAs (cluster size, 1..8) that split each 128-row
     tile along K; 0 restores the library's own choice."""
     _check(_lib().busfill_set_option(2, int(csize)), "busfill_set_option")
+
+
+def uses_prefill(m: int, n: int) -> bool:
+    """True if a GEMM of m batch rows and n output columns runs the prefill kernel."""
+    return _lib().busfill_gemm_kernel_for(int(m), int(n)) == 1
 
 
 def set_prefill_min_m(m: int) -> None:

@@ -35,10 +35,23 @@ constexpr int kVersion = 100;  // 0.1.0
 std::atomic<unsigned> g_last_detail{0};
 std::atomic<int> g_use_pdl{1};
 std::atomic<int> g_force_ksplit{0};  // 0 = automatic
-// Batches of at least this many rows take the prefill kernel (one pass over
-// the weights for all rows); smaller ones the decode kernel (32 rows a launch).
-constexpr int kDefaultPrefillMinM = 128;
-std::atomic<int> g_prefill_min_m{kDefaultPrefillMinM};
+// Batch size from which GEMMs take the prefill kernel (one pass over the
+// weights for all rows) instead of the decode kernel (32 rows a launch).
+// 0 = automatic: M >= 128 and at least kPrefillMinItems work items (256
+// weight rows x 128 batch rows each), since the prefill kernel runs one item
+// per SM at a time; with fewer items the decode kernel's K split over
+// clusters uses the GPU better (measured on B200: M = 128, N = 5120,
+// K = 17408 takes 157 us as 20 prefill items, 93 us as four decode launches).
+constexpr int kPrefillMinItems = 64;
+std::atomic<int> g_prefill_min_m{0};
+
+bool use_prefill(int M, int N) {
+  const int forced = g_prefill_min_m.load();
+  if (forced > 0) return M >= forced;
+  const long long items = (long long)((N + prefill::kPairRows - 1) / prefill::kPairRows) *
+                          ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
+  return M >= 128 && items >= kPrefillMinItems;
+}
 
 // ---------------------------------------------------------------------------
 // device properties (cached)
@@ -357,7 +370,7 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
                       prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   }
-  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, prefill::kBatchTile, kChunksPerUnit)) return BUSFILL_ERR_CUDA;
+  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, prefill::kBatchTile, 2)) return BUSFILL_ERR_CUDA;
 
   const void* kern = reinterpret_cast<const void*>(prefill_gemm_kernel<FMT, OutT>);
   {
@@ -392,7 +405,7 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
 template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
              int N, int K, unsigned* error, cudaStream_t s) {
-  if (M >= g_prefill_min_m.load()) return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
+  if (use_prefill(M, N)) return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
   return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
 }
 
@@ -472,6 +485,8 @@ int busfill_version(void) { return kVersion; }
 
 unsigned busfill_last_failure_detail(void) { return g_last_detail.load(); }
 
+int busfill_gemm_kernel_for(int M, int N) { return use_prefill(M, N) ? 1 : 0; }
+
 const char* busfill_status_string(int status) {
   switch (status) {
     case BUSFILL_OK: return "ok";
@@ -499,7 +514,7 @@ int busfill_set_option(int option, int value) {
   }
   if (option == BUSFILL_OPT_PREFILL_MIN_M) {
     if (value < 0) return BUSFILL_ERR_INVALID_ARG;
-    g_prefill_min_m.store(value == 0 ? kDefaultPrefillMinM : value);
+    g_prefill_min_m.store(value);
     return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;

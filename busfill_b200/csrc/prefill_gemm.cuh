@@ -18,17 +18,19 @@
 //                     tile t, K half h (chunks 2h, 2h+1) of the current unit.
 // The MMAs of a unit run (t0,h0) (t1,h0) (t0,h1) (t1,h1), 8 MMAs of
 // 128x128x16 each, so a half slot is refilled while the three other MMA
-// blocks run. Activations come as one 3-D TMA box per unit (4 chunks x 128
-// rows x 64 values, 64 KB) and weights as one box per unit for both tiles
+// blocks run. Activations come as one 3-D TMA box per K half (2 chunks x 128
+// rows x 64 values, 32 KB) and weights as one box per unit for both tiles
 // (256 rows, 36 KB): an SM's TMA unit takes a roughly fixed time per box
-// (~0.5 us with every SM loading, measured on B200), so few large boxes.
+// (~0.5 us with every SM loading, measured on B200), so few large boxes. The
+// weight ring is three units deep: a weight box lands ~1.7 us after issue
+// under load, longer than a unit's MMAs (~1.3 us).
 //
 // Measured on B200: a 128x128x16 TS MMA (A in TMEM) takes ~74 cycles back to
 // back, 92% of the dense fp16 rate; a unit (32 MMAs) ~2400 cycles.
 //
 // Warp roles (16 warps, one CTA per SM, persistent over work items):
-//   0      weight TMA producer (2-stage ring of 36 KB)
-//   1      activation TMA producer (2-stage ring of 64 KB); TMEM allocator
+//   0      weight TMA producer (3-stage ring of 36 KB)
+//   1      activation TMA producer (3-stage ring of 32 KB); TMEM allocator
 //   3      MMA issuer (converged warp, one elected thread issues)
 //   4-7    dequant of weight tile 0, 8-11 of weight tile 1: thread (warp%4,
 //          lane) owns tile row 32*(warp%4)+lane, both K halves of each unit
@@ -56,12 +58,12 @@ namespace prefill {
 constexpr int kThreads = 512;
 constexpr int kBatchTile = 128;                 // batch rows per item = MMA N
 constexpr int kPairRows = 2 * kTileRows;        // weight rows per item
-constexpr int kWStages = 2;
-constexpr int kXStages = 2;
+constexpr int kWStages = 3;
+constexpr int kXStages = 3;                     // half units (2 chunks each)
 constexpr int kWStage = 2 * kWStageBytes;       // both tiles' unit (Q4_0: 32 KB nibbles, then 4 KB scales)
 constexpr int kQ40Scales = 2 * kQ40ScaleOffset; // Q4_0: scales of the 256 rows after the nibbles
 constexpr int kXChunk = kBatchTile * 128;       // 64 values x 128 rows, 16 KB
-constexpr int kXStage = kChunksPerUnit * kXChunk;
+constexpr int kXStage = 2 * kXChunk;            // one K half of a unit, 32 KB
 constexpr int kAccCols = kBatchTile;            // per weight tile
 constexpr int kSlotCols = 64;                   // half a unit
 constexpr int kSlot0 = 2 * kAccCols;
@@ -152,13 +154,15 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
       tma_load_2d(dst + kQ40Scales, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
     }
   };
-  auto issue_x = [&](int u) {
+  // activations of half unit v = 2u + h (chunks 2h, 2h+1 of unit u) into stage v % kXStages
+  auto issue_x = [&](int v) {
+    const int u = v >> 1, h = v & 1;
     const int it = item_of(u / S), k = u % S;
     const int bt = it % p.btiles;
-    const int s = u % kXStages;
+    const int s = v % kXStages;
     mbar_arrive_expect_tx(BAR(bXFull + s), kXStage);
-    tma_load_3d(sbase + kXOff + s * kXStage, &tmap_a, 0, bt * kBatchTile, k * kChunksPerUnit, BAR(bXFull + s),
-                kPolicyEvictLast);
+    tma_load_3d(sbase + kXOff + s * kXStage, &tmap_a, 0, bt * kBatchTile, k * kChunksPerUnit + 2 * h,
+                BAR(bXFull + s), kPolicyEvictLast);
   };
 
   // set-up: barriers by warp 0's lanes, the first weight stages before the
@@ -206,17 +210,17 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     // ---------------- activation producer ----------------
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
     int issued = 0;
-    for (int u = 0; u < nunits; ++u) {
-      diag_unit = u;
-      if (u >= kXStages && !warp_wait(BAR(bXEmpty + u % kXStages), ((u / kXStages) & 1) ^ 1)) break;
-      if (elect_one()) issue_x(u);
+    for (int v = 0; v < 2 * nunits; ++v) {
+      diag_unit = v >> 1;
+      if (v >= kXStages && !warp_wait(BAR(bXEmpty + v % kXStages), ((v / kXStages) & 1) ^ 1)) break;
+      if (elect_one()) issue_x(v);
       __syncwarp();
-      issued = u + 1;
+      issued = v + 1;
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrActProducer);
     ok = true;
-    for (int u = issued > kXStages ? issued - kXStages : 0; u < issued; ++u)
-      if (!warp_wait(BAR(bXFull + u % kXStages), (u / kXStages) & 1)) {
+    for (int v = issued > kXStages ? issued - kXStages : 0; v < issued; ++v)
+      if (!warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1)) {
         if (lane == 0) atomicOr(p.error, kErrTeardown);
         break;
       }
@@ -228,11 +232,12 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
       const int j = u / S, k = u % S;
       // the accumulators are free once the epilogue has read item j - 1
       if (k == 0 && j >= 1 && !warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1))) break;
-      if (!warp_wait(BAR(bXFull + u % kXStages), (u / kXStages) & 1)) break;
-      const uint64_t bx = bdesc0 + (uint64_t)(((u % kXStages) * kXStage) >> 4);
       bool good = true;
 #pragma unroll 1
       for (int h = 0; h < 2 && good; ++h) {
+        const int v = 2 * u + h;
+        if (!warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1)) { good = false; break; }
+        const uint64_t bx = bdesc0 + (uint64_t)(((v % kXStages) * kXStage) >> 4);
 #pragma unroll 1
         for (int t = 0; t < 2; ++t) {
           const int sl = 2 * t + h;
@@ -245,19 +250,17 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
             for (int cl = 0; cl < 2; ++cl)
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
-                mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks,
-                           bx + (uint64_t)((((2 * h + cl) * kXChunk) + 32 * ks) >> 4), kIdesc,
+                mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks, bx + (uint64_t)(((cl * kXChunk) + 32 * ks) >> 4), kIdesc,
                            (k == 0 && h == 0 && cl == 0 && ks == 0) ? 0u : 1u);
             tc_commit(BAR(bSDone + sl));  // half slot free once these MMAs complete
           }
           __syncwarp();
         }
+        if (good && elect_one()) tc_commit(BAR(bXEmpty + v % kXStages));  // activation stage free
+        __syncwarp();
       }
       if (!good) break;
-      if (elect_one()) {
-        tc_commit(BAR(bXEmpty + u % kXStages));        // activation stage free
-        if (k == S - 1) tc_commit(BAR(bAccFull));      // item's accumulators complete
-      }
+      if (elect_one() && k == S - 1) tc_commit(BAR(bAccFull));  // item's accumulators complete
       __syncwarp();
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrMma);

@@ -171,13 +171,19 @@ BUSFILL_API int busfill_version(void);
  *     1..8 forces that split where K/256 allows it (a tuning and test knob).
  *   BUSFILL_OPT_PREFILL_MIN_M: GEMMs with M >= value rows run the large-batch
  *     (prefill) kernel, one pass over the weights for all rows, instead of
- *     the decode kernel's launches of 32 rows; 0 restores the default (128).
- *     A tuning and test knob; results agree within the accuracy gate.
+ *     the decode kernel's launches of 32 rows; 0 (default) chooses by shape
+ *     (M >= 128 and at least 64 work items of 256 weight rows x 128 batch
+ *     rows). A tuning and test knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
 #define BUSFILL_OPT_PREFILL_MIN_M 3
 BUSFILL_API int busfill_set_option(int option, int value);
+
+/* Which kernel a GEMM of M batch rows and N output columns runs with the
+ * current options: 0 = decode kernel (launches of 32 rows), 1 = prefill
+ * kernel (one pass over the weights). Diagnostic; no reference counterpart. */
+BUSFILL_API int busfill_gemm_kernel_for(int M, int N);
 
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the
  * spirit of kernels/frag_probe.cu:1-48: d[128, nb] = a[128, 64] * b[nb, 64]^T

@@ -247,3 +247,21 @@ def test_ksplit_option_values():
     assert lib.busfill_set_option(2, 9) == -1
     assert lib.busfill_set_option(2, -1) == -1
     assert lib.busfill_set_option(2, 0) == 0
+
+
+def test_kernel_choice_by_shape():
+    """Default dispatch: prefill kernel for M >= 128 with >= 64 work items
+    (256 weight rows x 128 batch rows each), decode kernel otherwise; the
+    option forces a plain M threshold and 0 restores the default."""
+    bf.load_library()
+    assert not bf.uses_prefill(32, 5120)
+    assert not bf.uses_prefill(127, 17408)
+    assert not bf.uses_prefill(128, 5120)        # 20 items: the decode kernel's K split does better
+    assert bf.uses_prefill(128, 17408)           # 68 items
+    assert bf.uses_prefill(512, 5120) and bf.uses_prefill(2048, 5120)
+    bf.set_prefill_min_m(1)
+    try:
+        assert bf.uses_prefill(1, 128)
+    finally:
+        bf.set_prefill_min_m(0)
+    assert not bf.uses_prefill(1, 128)

@@ -1,10 +1,11 @@
 """GPU parity of the large-batch (prefill) kernel, through the C ABI.
 
-Batches of at least the prefill threshold (default 128 rows) run one pass over
-the weights for all rows; the decode kernel covers smaller batches. These
-tests run the prefill kernel at its own shapes, force it onto small and
-ragged shapes (BUSFILL_OPT_PREFILL_MIN_M), and check the BASELINE config-4
-shapes at full size on sampled rows and columns against the oracle.
+Large batches (by default M >= 128 with at least 64 work items of 256 weight
+rows x 128 batch rows) run one pass over the weights for all rows; the decode
+kernel covers the rest. These tests force the prefill kernel
+(BUSFILL_OPT_PREFILL_MIN_M) onto small, ragged and multi-item shapes, and run
+the BASELINE config-4 shapes at full size through the default dispatch,
+checked on sampled rows and columns against the oracle.
 Gates as in test_gpu_parity: max abs err <= 0.6 and rel-L2 <= 1e-3 against
 an fp32 matmul of the dequantized weights, plus a tighter fp64 check.
 """
@@ -51,7 +52,7 @@ PREFILL_SHAPES = [
 
 
 @pytest.mark.parametrize("m,n,k", PREFILL_SHAPES)
-def test_prefill_q4k(m, n, k):
+def test_prefill_q4k(prefill_always, m, n, k):
     blocks = orc.gen_q4k(n, k, seed=m + 3 * n + k)
     a = orc.gen_activations(m, k, seed=m * 7 + k)
     c = bf.gemm_q4k(cu(blocks), cu(a))
@@ -61,7 +62,7 @@ def test_prefill_q4k(m, n, k):
 
 
 @pytest.mark.parametrize("m,n,k", PREFILL_SHAPES)
-def test_prefill_q4_0_planes_and_ggml(m, n, k):
+def test_prefill_q4_0_planes_and_ggml(prefill_always, m, n, k):
     """Both Q4_0 layouts give the same fp16 operands, so the same bits."""
     wq, ws = orc.gen_q4_0(n, k, seed=m + 5 * n + k)
     blocks = orc.q4_0_planes_to_ggml_blocks(wq, ws)
