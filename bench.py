@@ -271,8 +271,8 @@ def run_busfill(args):
     achieved = b_launch / (us_per_gemm * 1e-6) / 1e9
     workload = f"{args.fmt}_gemm_m{M}_k{K}_n{N}"
     out = {
-        "metric": "Q4_K GEMM tokens/s (M / avg GEMM time) at K=N=5120" if args.fmt == "q4k"
-        else "Q4_0 GEMM tokens/s (M / avg GEMM time)",
+        "metric": f"{'Q4_K' if args.fmt == 'q4k' else 'Q4_0'} GEMM tokens/s (M / avg GEMM time) at "
+                  + (f"K=N={K}" if K == N else f"K={K}, N={N}"),
         "value": round(tok_s, 1),
         "unit": "tokens/s",
         "n_gpus": world,
