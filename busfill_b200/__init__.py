@@ -19,7 +19,7 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
     "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "uses_prefill", "probe_umma", "version",
 ]
 
@@ -61,6 +61,7 @@ _SIGS = {
     "busfill_gemm_q4_0": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4_0_ggml": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q4k_swiglu": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
@@ -207,6 +208,23 @@ def gemm_q4_0_ggml(blocks, a, out=None, stream=None):
     _need(out, torch.float16, "out")
     _check(_lib().busfill_gemm_q4_0_ggml(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
            "busfill_gemm_q4_0_ggml")
+    return out
+
+
+def gemm_q4k_swiglu(w_gate, w_up, a, out=None, stream=None):
+    """h[M, N] = silu(A @ deq(Wg)^T) * (A @ deq(Wu)^T) for two llama.cpp
+    block_q4_K weights [N, K/256*144] (ffn_gate, ffn_up); fp16 out."""
+    torch = _torch()
+    _need(w_gate, torch.uint8, "w_gate"); _need(w_up, torch.uint8, "w_up"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = w_gate.shape[0]
+    if k % 256 or w_gate.shape[1] != k // 256 * 144 or tuple(w_up.shape) != tuple(w_gate.shape):
+        raise ValueError(f"shape mismatch: w_gate {tuple(w_gate.shape)}, w_up {tuple(w_up.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q4k_swiglu(_ptr(w_gate), _ptr(w_up), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
+           "busfill_gemm_q4k_swiglu")
     return out
 
 

@@ -11,6 +11,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <type_traits>
 #include <utility>
 
 #include "busfill.h"
@@ -45,10 +46,11 @@ std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
 
-bool use_prefill(int M, int N) {
+bool use_prefill(int M, int N, bool swiglu = false) {
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
-  const long long items = (long long)((N + prefill::kPairRows - 1) / prefill::kPairRows) *
+  const int pair_rows = swiglu ? kTileRows : prefill::kPairRows;  // SwiGLU items: gate tile j + up tile j
+  const long long items = (long long)((N + pair_rows - 1) / pair_rows) *
                           ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
   return M >= 128 && items >= kPrefillMinItems;
 }
@@ -186,18 +188,18 @@ cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStr
 // ---------------------------------------------------------------------------
 // decode GEMM launch
 // ---------------------------------------------------------------------------
-template <WFmt FMT, int NB, typename OutT>
+template <WFmt FMT, int NB, typename OutT, bool SW = false>
 const void* decode_kernel_ptr() {
-  return reinterpret_cast<const void*>(decode_gemm_kernel<FMT, NB, OutT>);
+  return reinterpret_cast<const void*>(decode_gemm_kernel<FMT, NB, OutT, SW>);
 }
 
 // Raise the kernel's dynamic shared memory limit, once per device.
-template <WFmt FMT, int NB, typename OutT>
+template <WFmt FMT, int NB, typename OutT, bool SW = false>
 bool decode_smem_attr(int dev) {
   static std::once_flag once[64];
   static cudaError_t err[64];
   std::call_once(once[dev & 63], [&] {
-    err[dev & 63] = cudaFuncSetAttribute(decode_kernel_ptr<FMT, NB, OutT>(),
+    err[dev & 63] = cudaFuncSetAttribute(decode_kernel_ptr<FMT, NB, OutT, SW>(),
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<NB>::kAlloc);
   });
   return err[dev & 63] == cudaSuccess;
@@ -242,9 +244,10 @@ struct DecodeSchedule {
 // Pick the K split c (1..max_cluster) with the shortest estimated weight-streaming time:
 // each active CTA moves at most kSmGBs (one SM's TMA rate on 144-byte weight
 // rows, measured on B200) and all of them together at most kHbmGBs; a cluster
-// takes ceil(T / G) tiles of ceil(S / c) units each. Ties go to the smaller c.
+// takes ceil(T / G) tiles of `segs` x ceil(S / c) units each (segs = 2 for
+// SwiGLU gate/up pairs). Ties go to the smaller c.
 template <WFmt FMT, int NB, typename OutT>
-DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count) {
+DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count, int segs) {
   constexpr double kSmGBs = 57.0;
   constexpr double kHbmGBs = 6500.0;
   DecodeSchedule best;
@@ -257,7 +260,7 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count) {
     const int ncl = std::min(T, cap);
     if (ncl < 1) continue;
     const long long rounds = (T + ncl - 1) / ncl;
-    const long long units = rounds * ((S + c - 1) / c);
+    const long long units = rounds * segs * ((S + c - 1) / c);
     const double rate = std::min(kSmGBs, kHbmGBs / (double)(ncl * c));
     const double ns = (double)units * kWStageBytes / rate;
     if (ns < best_ns * 0.999) {
@@ -269,14 +272,14 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count) {
   return best;
 }
 
-template <WFmt FMT, int NB, typename OutT>
+template <WFmt FMT, int NB, typename OutT, bool SW = false>
 int launch_decode_nb(const DeviceInfo& di, const CUtensorMap& tw, const CUtensorMap& tws, const CUtensorMap& ta,
                      const DecodeParams& p, cudaStream_t s) {
-  const void* kern = decode_kernel_ptr<FMT, NB, OutT>();
+  const void* kern = decode_kernel_ptr<FMT, NB, OutT, SW>();
   constexpr int smem = DecodeSmem<NB>::kAlloc;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!decode_smem_attr<FMT, NB, OutT>(dev)) return BUSFILL_ERR_LAUNCH;
+  if (!decode_smem_attr<FMT, NB, OutT, SW>(dev)) return BUSFILL_ERR_LAUNCH;
   const int grid = p.nclusters * p.csize;
   void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tws), const_cast<CUtensorMap*>(&ta),
                   const_cast<DecodeParams*>(&p)};
@@ -298,11 +301,14 @@ int check_gemm_args(const uint8_t* w, const uint16_t* ws, const uint16_t* a, con
 
 // Launches the decode kernel once per 32 rows of A; `error` points at the two
 // device words the kernels report failures to.
+// With `w_up` (144-byte formats only) the GEMM is the SwiGLU pair:
+// C = silu(A deq(w)^T) * (A deq(w_up)^T).
 template <WFmt FMT, typename OutT>
 int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-               int M, int N, int K, unsigned* error, cudaStream_t s) {
+               int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
   const int S = K / kUnitK;
   const int T = (N + kTileRows - 1) / kTileRows;
+  const int swiglu = w_up ? 1 : 0;
 
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
@@ -312,8 +318,12 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
                       CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
-    tws = tw;  // unused by these formats
+    tws = tw;  // the up projection's map with SwiGLU, else unused
+    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, kQ4KBlockBytes,
+                                kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
   } else {
+    if (swiglu) return BUSFILL_ERR_INVALID_ARG;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
                       kTileRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return BUSFILL_ERR_CUDA;
@@ -325,8 +335,8 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
   for (int m0 = 0; m0 < M; m0 += 32) {
     const int mc = std::min(32, M - m0);
     const int nb = mc <= 16 ? 16 : 32;
-    const DecodeSchedule sch = nb == 16 ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count)
-                                        : choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count);
+    const DecodeSchedule sch = nb == 16 ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count, 1 + swiglu)
+                                        : choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count, 1 + swiglu);
     const uint16_t* a_chunk = a + (size_t)m0 * K;
     if (!make_tmap_act3d(&ta, a_chunk, (uint64_t)mc, (uint64_t)K, (uint32_t)nb, kChunksPerUnit))
       return BUSFILL_ERR_CUDA;
@@ -340,8 +350,15 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     p.units_per_tile = S;
     p.csize = sch.csize;
     p.nclusters = sch.nclusters;
-    const int st = nb == 16 ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
-                            : launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
+    int st = BUSFILL_OK;
+    if constexpr (FMT != WFmt::Q4_0 && std::is_same<OutT, __half>::value) {
+      if (swiglu)
+        st = nb == 16 ? launch_decode_nb<FMT, 16, OutT, true>(di, tw, tws, ta, p, s)
+                      : launch_decode_nb<FMT, 32, OutT, true>(di, tw, tws, ta, p, s);
+    }
+    if (!swiglu)
+      st = nb == 16 ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
+                    : launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
     if (st != BUSFILL_OK) return st;
   }
   return BUSFILL_OK;
@@ -352,17 +369,24 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
 // ---------------------------------------------------------------------------
 template <WFmt FMT, typename OutT>
 int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-                int M, int N, int K, unsigned* error, cudaStream_t s) {
+                int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
   const int S = K / kUnitK;
+  const int swiglu = w_up ? 1 : 0;
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
   if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4_0G) {
+    // one 256-row box per unit, or with SwiGLU one 128-row box from each matrix
     const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
-    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes,
-                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+    const uint32_t box_rows = swiglu ? kTileRows : prefill::kPairRows;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
     tws = tw;
+    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, kQ4KBlockBytes,
+                                box_rows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
   } else {
+    if (swiglu) return BUSFILL_ERR_INVALID_ARG;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
                       prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return BUSFILL_ERR_CUDA;
@@ -387,7 +411,8 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   p.M = M;
   p.N = N;
   p.K = K;
-  p.pairs = (N + prefill::kPairRows - 1) / prefill::kPairRows;
+  p.pairs = swiglu ? (N + kTileRows - 1) / kTileRows : (N + prefill::kPairRows - 1) / prefill::kPairRows;
+  p.swiglu = swiglu;
   p.btiles = (M + prefill::kBatchTile - 1) / prefill::kBatchTile;
   p.units = S;
   const long long items = (long long)p.pairs * p.btiles;
@@ -404,16 +429,19 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
 // Decode (M < prefill threshold) or prefill kernel for one GEMM.
 template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
-             int N, int K, unsigned* error, cudaStream_t s) {
-  if (use_prefill(M, N)) return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
-  return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s);
+             int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
+  if (use_prefill(M, N, w_up != nullptr))
+    return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
+  return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
 }
 
 template <WFmt FMT, typename OutT>
 int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M, int N, int K,
-              cudaStream_t s) {
+              cudaStream_t s, const uint8_t* w_up = nullptr, bool swiglu = false) {
   int st = check_gemm_args<FMT>(w, ws, a, c, M, N, K);
   if (st != BUSFILL_OK) return st;
+  if (swiglu && !w_up) return BUSFILL_ERR_INVALID_ARG;
+  if (w_up && !aligned16(w_up)) return BUSFILL_ERR_ALIGNMENT;
   DeviceInfo di;
   int dev = 0;
   st = current_device(&di, &dev);
@@ -424,7 +452,7 @@ int gemm_impl(const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, 
     st = get_error_words(dev, s, &err);
   }
   if (st != BUSFILL_OK) return st;
-  return run_gemm<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, err, s);
+  return run_gemm<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, err, s, w_up);
 }
 
 int grid_for(long long work, int sm_count) {
@@ -527,6 +555,12 @@ int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, 
 
 int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
   return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, uint16_t* h, int M, int N,
+                            int K, void* stream) {
+  return gemm_impl<WFmt::Q4K, __half>(w_gate, nullptr, a, h, M, N, K, reinterpret_cast<cudaStream_t>(stream), w_up,
+                                      true);
 }
 
 int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {

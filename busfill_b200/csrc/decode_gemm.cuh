@@ -159,16 +159,20 @@ struct DecodeSmem {
 };
 
 // Per-unit schedule facts every role derives the same way: unit i of this CTA
-// is unit sb0 + i % len of its cluster's (i / len)-th tile.
+// is unit sb0 + i % len of its cluster's (i / len)-th segment. A segment is a
+// tile; with SwiGLU (sw = 1) segments 2j and 2j+1 are the gate and the up tile
+// of the cluster's j-th tile index.
 struct UnitInfo {
   int tile, sb, seg;
+  bool up;                    // SwiGLU: the up projection's tile
   bool seg_first, seg_last;   // first / last unit of this CTA's part of the tile
 };
-__device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, int nclusters) {
+__device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, int nclusters, int sw) {
   UnitInfo r;
   r.seg = i / len;
   const int j = i - r.seg * len;
-  r.tile = g + r.seg * nclusters;
+  r.tile = g + (r.seg >> sw) * nclusters;
+  r.up = sw && (r.seg & 1);
   r.sb = sb0 + j;
   r.seg_first = (j == 0);
   r.seg_last = (j == len - 1);
@@ -178,7 +182,10 @@ __device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, in
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
-template <WFmt FMT, int NB, typename OutT>
+// SW: SwiGLU pair (144-byte formats): tmap_w is the gate, tmap_ws the up
+// projection, C = silu(A Wg^T) * (A Wu^T); every tile index of the cluster
+// becomes two segments (gate, up).
+template <WFmt FMT, int NB, typename OutT, bool SW = false>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                        const __grid_constant__ CUtensorMap tmap_a, const DecodeParams p) {
@@ -186,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = DecodeSmem<NB>;
   using TM = DecodeTmem<NB>;
   constexpr bool kRows144 = (FMT != WFmt::Q4_0);  // 144-byte row units (block_q4_K, 8 x block_q4_0)
+  static_assert(!SW || kRows144, "SwiGLU pairs take 144-byte row formats");
+  constexpr int kSw = SW ? 1 : 0;
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
   constexpr int kWStages = L::kWStages;
 
@@ -206,7 +215,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int g = (int)(blockIdx.x / (unsigned)csize);
   const int sb0 = ksplit_begin(crank, S, csize);
   const int len = ksplit_begin(crank + 1, S, csize) - sb0;
-  const int ntiles = (p.tiles - g + p.nclusters - 1) / p.nclusters;
+  // segments of this CTA: its cluster's tile indices, two segments each with SwiGLU
+  const int ntiles = ((p.tiles - g + p.nclusters - 1) / p.nclusters) << kSw;
   const int nunits = ntiles * len;
 
   // Every role waits with the whole warp; a wait that times out in any lane
@@ -237,11 +247,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   // weight TMA for unit i into ring stage i % kWStages (the stage must be free); one thread
   auto issue_w_thread = [&](int i) {
     const int s = i % kWStages;
-    const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters);
+    const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters, kSw);
     const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
     mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
     if constexpr (kRows144) {
-      tma_load_2d(dst, &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
+      tma_load_2d(dst, ui.up ? &tmap_ws : &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s),
+                  kPolicyEvictFirst);
     } else {
       tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
       tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, ui.sb * 8, ui.tile * kTileRows, BAR(L::bWFull + s),
@@ -419,6 +430,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     float acc[NB];
+    float gate[SW ? NB : 1];  // SwiGLU: the reduced gate tile, held until its up tile
 
     // Finish tile `tile` (this CTA's segment `seg`). One CTA per tile: write C.
     // Otherwise ranks k > 0 push their fp32 partial into rank 0's shared
@@ -484,6 +496,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           cl_arrived = true;
         }
       }
+      if constexpr (SW) {
+        if ((seg & 1) == 0) {
+#pragma unroll
+          for (int t = 0; t < NB; ++t) gate[t] = acc[t];
+          return;
+        }
+#pragma unroll
+        for (int t = 0; t < NB; ++t) acc[t] = silu(gate[t]) * acc[t];
+      }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
       if (ok && n < p.N) {
 #pragma unroll
@@ -512,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
-      flush(g + seg * p.nclusters, seg);
+      flush(g + (seg >> kSw) * p.nclusters, seg);
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrEpilogue);
   }

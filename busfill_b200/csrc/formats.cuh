@@ -120,6 +120,10 @@ __device__ __forceinline__ void dequant_q4_0g_chunk(const uint32_t* w, uint32_t*
   }
 }
 
+// silu(x) = x * sigmoid(x), in fp32 (one exp through the CUDA intrinsic); the
+// SwiGLU epilogues write fp16_rn(silu(gate) * up) of the fp32 accumulators
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>

@@ -90,9 +90,10 @@ struct Params {
   void* c;            // [M, N] row-major, OutT
   unsigned* error;    // device error word (+1: first failure record)
   int M, N, K;
-  int pairs;          // P = ceil(N / 256)
+  int pairs;          // P = ceil(N / 256); SwiGLU: ceil(N / 128) (gate tile j, up tile j)
   int btiles;         // B = ceil(M / 128)
   int units;          // S = K / 256
+  int swiglu;         // 1: C = silu(A Wg^T) * (A Wu^T); tmap_w gate, tmap_ws up (128-row boxes)
 };
 
 }  // namespace prefill
@@ -148,7 +149,13 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     const uint32_t dst = sbase + kWOff + s * kWStage;
     mbar_arrive_expect_tx(BAR(bWFull + s), kWStage);
     if constexpr (kRows144) {
-      tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+      if (p.swiglu) {
+        tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kTileRows, BAR(bWFull + s), kPolicyEvictLast);
+        tma_load_2d(dst + kWStageBytes, &tmap_ws, k * kQ4KBlockBytes, pair * kTileRows, BAR(bWFull + s),
+                    kPolicyEvictLast);
+      } else {
+        tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+      }
     } else {
       tma_load_2d(dst, &tmap_w, k * 128, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
       tma_load_2d(dst + kQ40Scales, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
@@ -317,20 +324,40 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         pdl_wait_prerequisites();  // C may still be read by the previous kernel
         waited_pdl = true;
       }
+      if (p.swiglu) {
+        // accumulator 0 holds the gate tile, 1 the up tile of the same rows
+        const int n = pair * kTileRows + r;
 #pragma unroll 1
-      for (int t = 0; t < 2; ++t) {
-        const int n = pair * kPairRows + t * kTileRows + r;
-#pragma unroll 1
-        for (int cb = 0; cb < kBatchTile; cb += 32) {
-          uint32_t x[32];
-          tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb), x);
-          tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb + 16), x + 16);
+        for (int cb = 0; cb < kBatchTile; cb += 16) {
+          uint32_t xg[16], xu[16];
+          tmem_ld_x16(tmem + lane_off + (uint32_t)cb, xg);
+          tmem_ld_x16(tmem + lane_off + (uint32_t)(kAccCols + cb), xu);
           tc_wait_ld();
           if (have && n < p.N) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
+            for (int i = 0; i < 16; ++i) {
               const int b = bt * kBatchTile + cb + i;
-              if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(__uint_as_float(x[i]));
+              if (b < p.M)
+                C[(size_t)b * p.N + n] = to_out<OutT>(silu(__uint_as_float(xg[i])) * __uint_as_float(xu[i]));
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int t = 0; t < 2; ++t) {
+          const int n = pair * kPairRows + t * kTileRows + r;
+#pragma unroll 1
+          for (int cb = 0; cb < kBatchTile; cb += 32) {
+            uint32_t x[32];
+            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb), x);
+            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb + 16), x + 16);
+            tc_wait_ld();
+            if (have && n < p.N) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int b = bt * kBatchTile + cb + i;
+                if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(__uint_as_float(x[i]));
+              }
             }
           }
         }

@@ -68,6 +68,19 @@ BUSFILL_API int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const u
  * (kernels/q4k_batched.py:7-8). */
 BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
 
+/* Fused SwiGLU pair of a gated feed-forward layer:
+ *   h[M, N] = silu(A deq(w_gate)^T) * (A deq(w_up)^T),  silu(x) = x / (1 + e^-x),
+ * with both products accumulated in fp32 and h rounded once to fp16.
+ * w_gate and w_up are llama.cpp block_q4_K rows [N, K/256 x 144 B] (the
+ * ffn_gate and ffn_up tensors), a [M, K] fp16, h [M, N] fp16. Requires
+ * K % 256 == 0; all pointers 16-byte aligned. The gate and up tiles of the
+ * same 128 rows are computed by the same CTAs, so neither product goes to
+ * memory. No reference counterpart: the epilogue BASELINE config 3's layer
+ * set puts after the up projection (kernels/q4k_batched.py:7-8 names the
+ * Q4_K GEMM it belongs to). */
+BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, uint16_t* h,
+                                        int M, int N, int K, void* stream);
+
 /* Q4_0 as llama.cpp stores it: block_q4_0 rows, K/32 blocks of 18 bytes per
  * weight row (fp16 d, then 16 bytes whose low nibbles are elements 0-15 and
  * high nibbles elements 16-31); value = (q - 8) * d, the same rule as

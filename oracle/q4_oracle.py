@@ -279,6 +279,16 @@ GATE_MAX_ABS = 0.6      # kernels/q4k_batched.py:102
 GATE_REL_L2 = 1e-3
 
 
+def swiglu_ref(a16: np.ndarray, w_gate: np.ndarray, w_up: np.ndarray) -> np.ndarray:
+    """silu(A Wg^T) * (A Wu^T) in float64 on the given (dequantized) weights:
+    the fused gate/up epilogue of a gated feed-forward layer, silu(x) =
+    x / (1 + exp(-x))."""
+    a = np.asarray(a16, dtype=np.float16).astype(np.float64)
+    g = a @ np.asarray(w_gate, dtype=np.float64).T
+    u = a @ np.asarray(w_up, dtype=np.float64).T
+    return g / (1.0 + np.exp(-g)) * u
+
+
 def gemm_errors(c, cref):
     """(max_abs_err, rel_l2, all_finite) of a GEMM output against the reference."""
     c = np.asarray(c, dtype=np.float64)
