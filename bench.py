@@ -50,7 +50,8 @@ def parse_args():
     ap.add_argument("--n", type=int, default=5120)
     ap.add_argument("--k", type=int, default=5120)
     ap.add_argument("--seed", type=int, default=1234)
-    ap.add_argument("--no-extras", action="store_true", help="skip sweep / cuBLAS / e2e / CPU legs")
+    ap.add_argument("--no-extras", action="store_true", help="skip sweep / cuBLAS / e2e / CPU / layer-set legs")
+    ap.add_argument("--layers", type=int, default=64, help="layers in the BASELINE config-3 layer-set sweep")
     return ap.parse_args()
 
 
@@ -65,6 +66,11 @@ def measured_peaks():
         return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def metric_name(fmt, K, N):
+    return (f"{'Q4_K' if fmt == 'q4k' else 'Q4_0'} GEMM tokens/s (M / avg GEMM time) at "
+            + (f"K=N={K}" if K == N else f"K={K}, N={N}"))
 
 
 def alg_bytes(m, n, k):
@@ -271,8 +277,7 @@ def run_busfill(args):
     achieved = b_launch / (us_per_gemm * 1e-6) / 1e9
     workload = f"{args.fmt}_gemm_m{M}_k{K}_n{N}"
     out = {
-        "metric": f"{'Q4_K' if args.fmt == 'q4k' else 'Q4_0'} GEMM tokens/s (M / avg GEMM time) at "
-                  + (f"K=N={K}" if K == N else f"K={K}, N={N}"),
+        "metric": metric_name(args.fmt, K, N),
         "value": round(tok_s, 1),
         "unit": "tokens/s",
         "n_gpus": world,
@@ -303,6 +308,8 @@ def run_busfill(args):
         "clocks": sampler.summary(),
     }
 
+    if not args.no_extras:
+        out["layerset"] = layerset(torch, bf, tp, dev, world, rank, args, hbm_peak)
     if world == 1 and not args.no_extras:
         out["isolated_no_pdl"] = isolated_no_pdl(bf, capture, time_graph, min(steps, 50), R, M)
         out["sweep"] = sweep(torch, bf, dev, l2, hbm_peak, args)
@@ -399,6 +406,93 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         del g, ws
         torch.cuda.empty_cache()
     return rows
+
+
+def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
+    """a 27B-class dense decoder layer set in Q4_K at M = 32,
+    `args.layers` distinct layers streamed back to back: fused QKV 5120 ->
+    10240, O 8192 -> 5120, gate/up 5120 -> 2 x 17408 as one fused SwiGLU GEMM,
+    down 17408 -> 5120. Attention itself is outside the path: a fixed [32,
+    8192] tensor stands in for its output. Over `world` GPUs every weight is
+    column-split (tp.shard_rows) and each output all-gathered (NCCL), so every
+    rank holds the full activations for the next GEMM. Timed as a CUDA graph of
+    one sweep over all layers, CUDA events, max over ranks."""
+    import torch.distributed as dist
+    L = args.layers
+    shapes = {"qkv": (10240, 5120), "o": (5120, 8192), "gate": (17408, 5120), "up": (17408, 5120),
+              "down": (5120, 17408)}
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 1000 + rank)
+    layers = []
+    local_bytes = 0
+    for _ in range(L):
+        lw = {}
+        for name, (n, k) in shapes.items():
+            r0, r1 = tp.shard_rows(n, world, rank)
+            lw[name] = make_q4k_weights(torch, r1 - r0, k, gen, dev)
+            local_bytes += (r1 - r0) * k * 18 // 32
+        layers.append(lw)
+    total_bytes = sum(n * k * 18 // 32 for n, k in shapes.values()) * L
+    x = (torch.randn((m, 5120), device=dev, generator=gen) / 64).half()
+    attn = (torch.randn((m, 8192), device=dev, generator=gen) / 64).half()
+    full = {name: torch.empty((m, n), dtype=torch.float16, device=dev) for name, (n, _) in shapes.items()}
+    loc = {name: torch.empty((m, tp.shard_rows(n, world, rank)[1] - tp.shard_rows(n, world, rank)[0]),
+                             dtype=torch.float16, device=dev) for name, (n, _) in shapes.items()}
+    st = torch.cuda.Stream(device=dev)
+
+    def gemm(name, w, a):
+        n = shapes[name][0]
+        if world == 1:
+            return bf.gemm_q4k(w, a, out=full[name], stream=st)
+        return tp.gemm_q4k_tp(w, a, n, out=full[name], local_out=loc[name])
+
+    def swiglu(lw, a):
+        n = shapes["gate"][0]
+        if world == 1:
+            return bf.gemm_q4k_swiglu(lw["gate"], lw["up"], a, out=full["gate"], stream=st)
+        bf.gemm_q4k_swiglu(lw["gate"], lw["up"], a, out=loc["gate"], stream=torch.cuda.current_stream())
+        return tp.gather_columns(loc["gate"], n, out=full["gate"])
+
+    def sweep():
+        h = x
+        for lw in layers:
+            gemm("qkv", lw["qkv"], h)             # its output would feed attention (outside the path)
+            o = gemm("o", lw["o"], attn)
+            g = swiglu(lw, o)
+            h = gemm("down", lw["down"], g)
+
+    with torch.cuda.stream(st):
+        sweep()
+        st.synchronize()
+        assert bf.stream_status(st) == 0
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            sweep()
+        g.replay()
+        st.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(sweeps):
+            g.replay()
+        e1.record(st)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / sweeps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del g
+    del layers
+    torch.cuda.empty_cache()
+    return {"layers": L, "M": m, "ms_per_sweep": round(ms, 4), "tokens_per_s": round(m / (ms * 1e-3), 1),
+            "weight_bytes_total": total_bytes, "weight_bytes_per_gpu": local_bytes,
+            "GB_s_total": round(total_bytes / (ms * 1e-3) / 1e9, 1),
+            "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / hbm_peak, 4),
+            "n_gpus": world, "parallelism": f"tp{world} column split + NCCL all-gather per GEMM" if world > 1
+            else "single GPU", "kernels": "busfill_gemm_q4k x3 + busfill_gemm_q4k_swiglu per layer",
+            "timing": f"CUDA graph of one {L}-layer sweep, {sweeps} replays, CUDA events, max over ranks"}
 
 
 def config4(torch, bf, dev, args, hbm_peak, tc_peak, peak_src):
@@ -637,8 +731,7 @@ def run_reference(args):
         el = time.perf_counter() - t0
     t_full = el / args.steps * (n / rows)      # extrapolate the slice to all N rows
     value = m / t_full
-    out = {"metric": "Q4_K GEMM tokens/s (M / avg GEMM time) at K=N=5120" if args.fmt == "q4k"
-           else "Q4_0 GEMM tokens/s (M / avg GEMM time)",
+    out = {"metric": metric_name(args.fmt, k, n),
            "value": round(value, 2), "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
            "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(el / args.steps * 1e3, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
