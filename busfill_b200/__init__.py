@@ -75,6 +75,13 @@ _SIGS = {
     "busfill_set_option": [_I, _I],
     "busfill_probe_umma": [_P, _P, _P, _I, _P],
     "busfill_gemm_kernel_for": [_I, _I],
+    "busfill_gemm_q4k_gather": [_P, _P, _I, _I, _I, _P, _P],
+    "busfill_gemm_q4k_swiglu_gather": [_P, _P, _P, _I, _I, _I, _P, _P],
+    "busfill_ipc_alloc": [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)],
+    "busfill_ipc_free": [_P],
+    "busfill_ipc_get_handle": [_P, _P],
+    "busfill_ipc_open": [_P, ctypes.POINTER(ctypes.c_void_p)],
+    "busfill_ipc_close": [_P],
 }
 
 

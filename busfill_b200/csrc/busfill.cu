@@ -305,7 +305,8 @@ int check_gemm_args(const uint8_t* w, const uint16_t* ws, const uint16_t* a, con
 // C = silu(A deq(w)^T) * (A deq(w_up)^T).
 template <WFmt FMT, typename OutT>
 int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-               int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
+               int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr,
+               const busfill_gather* gather = nullptr) {
   const int S = K / kUnitK;
   const int T = (N + kTileRows - 1) / kTileRows;
   const int swiglu = w_up ? 1 : 0;
@@ -341,6 +342,25 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     if (!make_tmap_act3d(&ta, a_chunk, (uint64_t)mc, (uint64_t)K, (uint32_t)nb, kChunksPerUnit))
       return BUSFILL_ERR_CUDA;
     DecodeParams p;
+    p.gather = GatherArgs{};
+    if (gather) {
+      // rows m0.. of every rank's full output; the first launch waits for the
+      // activations' flags, the last one raises this call's flags
+      p.gather.npeers = gather->npeers;
+      p.gather.col_off = gather->col_off;
+      p.gather.ldc = gather->ldc;
+      for (int q = 0; q < gather->npeers; ++q) {
+        p.gather.out[q] = reinterpret_cast<OutT*>(gather->out[q]) + (size_t)m0 * gather->ldc;
+        p.gather.flag[q] = gather->flag[q];
+      }
+      p.gather.counters = gather->counters;
+      p.gather.signal = (m0 + 32 >= M) ? 1 : 0;
+      if (m0 == 0 && gather->wait && gather->nwait > 0) {
+        p.gather.wait = gather->wait;
+        p.gather.wait_gen = gather->wait_gen;
+        p.gather.nwait = gather->nwait;
+      }
+    }
     p.c = reinterpret_cast<OutT*>(c) + (size_t)m0 * N;
     p.error = error;
     p.M = mc;
@@ -433,6 +453,31 @@ int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws
   if (use_prefill(M, N, w_up != nullptr))
     return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
   return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
+}
+
+// The gathered GEMM: its arguments checked, always the decode kernel.
+template <WFmt FMT>
+int gemm_gather_impl(const uint8_t* w, const uint8_t* w_up, bool swiglu, const uint16_t* a, int M, int N, int K,
+                     const busfill_gather* g, cudaStream_t s) {
+  if (!g || !g->counters || (swiglu && !w_up)) return BUSFILL_ERR_INVALID_ARG;
+  if (g->npeers < 1 || g->npeers > kMaxPeers || g->col_off < 0 || g->ldc < g->col_off + N) return BUSFILL_ERR_SHAPE;
+  if (g->nwait < 0 || g->nwait > 32 || (g->nwait > 0 && (!g->wait || !g->wait_gen))) return BUSFILL_ERR_INVALID_ARG;
+  for (int q = 0; q < g->npeers; ++q)
+    if (!g->out[q] || !g->flag[q]) return BUSFILL_ERR_INVALID_ARG;
+  int st = check_gemm_args<FMT>(w, nullptr, a, g->out[0], M, N, K);
+  if (st != BUSFILL_OK) return st;
+  if (w_up && !aligned16(w_up)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev = 0;
+  st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  unsigned* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = get_error_words(dev, s, &err);
+  }
+  if (st != BUSFILL_OK) return st;
+  return run_decode<FMT, __half>(di, dev, w, nullptr, a, g->out[0], M, N, K, err, s, swiglu ? w_up : nullptr, g);
 }
 
 template <WFmt FMT, typename OutT>
@@ -561,6 +606,66 @@ int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const ui
                             int K, void* stream) {
   return gemm_impl<WFmt::Q4K, __half>(w_gate, nullptr, a, h, M, N, K, reinterpret_cast<cudaStream_t>(stream), w_up,
                                       true);
+}
+
+int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int N, int K, const busfill_gather* g,
+                            void* stream) {
+  return gemm_gather_impl<WFmt::Q4K>(blocks, nullptr, false, a, M, N, K, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, int M, int N, int K,
+                                   const busfill_gather* g, void* stream) {
+  return gemm_gather_impl<WFmt::Q4K>(w_gate, w_up, true, a, M, N, K, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_ipc_alloc(size_t bytes, void** dev_ptr) {
+  if (!dev_ptr || bytes == 0) return BUSFILL_ERR_INVALID_ARG;
+  if (cudaMalloc(dev_ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_ALLOC;
+  }
+  if (cudaMemset(*dev_ptr, 0, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  return BUSFILL_OK;
+}
+
+int busfill_ipc_free(void* dev_ptr) {
+  if (!dev_ptr) return BUSFILL_ERR_INVALID_ARG;
+  return cudaFree(dev_ptr) == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_CUDA;
+}
+
+int busfill_ipc_get_handle(const void* dev_ptr, void* handle64) {
+  if (!dev_ptr || !handle64) return BUSFILL_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  std::memcpy(handle64, &h, sizeof(h));
+  return BUSFILL_OK;
+}
+
+int busfill_ipc_open(const void* handle64, void** dev_ptr) {
+  if (!handle64 || !dev_ptr) return BUSFILL_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  if (cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  return BUSFILL_OK;
+}
+
+int busfill_ipc_close(void* dev_ptr) {
+  if (!dev_ptr) return BUSFILL_ERR_INVALID_ARG;
+  if (cudaIpcCloseMemHandle(dev_ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  return BUSFILL_OK;
 }
 
 int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {

@@ -85,6 +85,25 @@ constexpr unsigned kErrDequant = 8u;
 constexpr unsigned kErrEpilogue = 16u;
 constexpr unsigned kErrTeardown = 32u;
 
+// Column split over a process group, with the all-gather in the epilogue:
+// every rank writes its slice of the output straight into each rank's full
+// output (peer memory over NVLink), and when the whole grid's slice has
+// landed the last CTA sets this rank's flag word in every rank's memory. A
+// later GEMM that reads the gathered output waits on those words first.
+constexpr int kMaxPeers = 8;
+struct GatherArgs {
+  int npeers;                 // ranks receiving the output (this one included); 0 = local C only
+  int col_off;                // first column of this rank's slice in the full rows
+  int ldc;                    // row length of the full outputs
+  int signal;                 // this launch raises the flags (the last launch of a call)
+  void* out[kMaxPeers];       // each rank's full output [rows, ldc], at this launch's first row
+  unsigned* flag[kMaxPeers];  // per rank: the word this rank sets in that rank's memory
+  unsigned* counters;         // this rank's [CTA count (zero between calls), signal generation]
+  const unsigned* wait;       // nwait local words to wait on (acquire) before reading A; may be null
+  unsigned* wait_gen;         // waits done so far on them: wait for *wait_gen + 1, then advance it
+  int nwait;
+};
+
 struct DecodeParams {
   void* c;              // [M, N] row-major, OutT
   unsigned* error;      // device error word (+1: first failure record)
@@ -93,6 +112,7 @@ struct DecodeParams {
   int units_per_tile;   // S = K / 256
   int csize;            // CTAs per cluster: the K split of every tile (1..8)
   int nclusters;        // G; cluster g takes tiles g, g + G, ...; G <= T
+  GatherArgs gather;
 };
 
 // Units [first, last) of every tile that cluster rank `rank` of `csize` takes.
@@ -304,6 +324,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
     named_bar_sync(1, 64);
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
+    if (p.gather.nwait > 0) {
+      // activations gathered by an earlier GEMM on every rank: wait for each
+      // rank's flag, then let this thread's TMA copies see what it acquired
+      const unsigned target = *p.gather.wait_gen + 1u;  // advanced by the previous call's last CTA
+      bool got = true;
+      if (lane < p.gather.nwait) got = wait_flag_sys(p.gather.wait + lane, target);
+      if (!__all_sync(0xffffffffu, got) && lane == 0) {
+        atomicOr(p.error, kErrActProducer);
+        atomicCAS(p.error + 1, 0u, 0x80000000u | ((unsigned)warp << 24) | 0xFFFu << 12);
+      }
+      fence_proxy_async_global();
+    }
     if (lane < x_early) issue_x_thread(lane);
     __syncwarp();
   }
@@ -506,7 +538,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < NB; ++t) acc[t] = silu(gate[t]) * acc[t];
       }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
-      if (ok && n < p.N) {
+      if (p.gather.npeers > 0) {
+        // this rank's slice into every rank's full output (peer stores over NVLink)
+        if (ok && n < p.N) {
+          for (int q = 0; q < p.gather.npeers; ++q) {
+            OutT* Cq = reinterpret_cast<OutT*>(p.gather.out[q]) + p.gather.col_off + n;
+#pragma unroll
+            for (int t = 0; t < NB; ++t)
+              if (t < p.M) Cq[(size_t)t * p.gather.ldc] = to_out<OutT>(acc[t]);
+          }
+        }
+        __threadfence_system();  // visible to every rank before the flags go up
+      } else if (ok && n < p.N) {
 #pragma unroll
         for (int t = 0; t < NB; ++t)
           if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
@@ -559,6 +602,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   // no CTA may leave while another CTA of its cluster can still read its
   // shared memory or arrive on its barriers
   if (csize > 1) cluster_wait();
+  // gathered output: the last CTA to finish raises this rank's flag in every
+  // rank's memory (each CTA fenced its peer stores at system scope first) to
+  // the call site's next generation, and advances this consumer's wait count
+  if ((p.gather.signal || p.gather.nwait > 0) && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned prev = atomicAdd(p.gather.counters, 1u);
+    if (prev == gridDim.x - 1) {
+      p.gather.counters[0] = 0u;  // ready for the next launch
+      if (p.gather.nwait > 0) *p.gather.wait_gen += 1u;
+      if (p.gather.signal) {
+        const unsigned gen = p.gather.counters[1] + 1u;
+        p.gather.counters[1] = gen;
+        __threadfence_system();
+        for (int q = 0; q < p.gather.npeers; ++q) st_release_sys(p.gather.flag[q], gen);
+      }
+    }
+  }
 }
 
 }  // namespace busfill

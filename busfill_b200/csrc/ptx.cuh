@@ -173,6 +173,36 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// ----------------------------------------------------------------------------
+// flags between GPUs (peer memory mapped over NVLink)
+// ----------------------------------------------------------------------------
+// store that releases this thread's prior writes at system scope
+__device__ __forceinline__ void st_release_sys(unsigned* addr, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+// Wait (bounded, kWaitTimeoutNs) until *addr has reached `epoch` (wrap-safe);
+// acquires at system scope. Returns false on timeout.
+__device__ __forceinline__ bool wait_flag_sys(const unsigned* addr, unsigned epoch) {
+  if ((int)(ld_acquire_sys(addr) - epoch) >= 0) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if ((int)(ld_acquire_sys(addr) - epoch) >= 0) return true;
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+}
+// order this thread's generic-proxy view of global memory before its later
+// async-proxy (TMA) reads of it
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // CTA named barriers (ids 1..15; id 0 is __syncthreads): `count` threads, a
 // multiple of 32, take part; arrive does not wait.
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {

@@ -14,6 +14,7 @@ the largest shard for the gather.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Callable, Optional
 
 TILE_ROWS = 128
@@ -117,3 +118,147 @@ def _empty_slice(a):
     import torch
 
     return torch.empty((a.shape[0], 0), dtype=torch.float16, device=a.device)
+
+
+# ---------------------------------------------------------------------------
+# Column split with the all-gather fused into the GEMM epilogue
+# ---------------------------------------------------------------------------
+class Gather(ctypes.Structure):
+    """ctypes mirror of busfill_gather (include/busfill.h)."""
+    _fields_ = [("npeers", ctypes.c_int), ("col_off", ctypes.c_int), ("ldc", ctypes.c_int),
+                ("out", ctypes.c_void_p * 8), ("flag", ctypes.c_void_p * 8), ("counters", ctypes.c_void_p),
+                ("wait", ctypes.c_void_p), ("wait_gen", ctypes.c_void_p), ("nwait", ctypes.c_int)]
+
+
+class _DevArray:
+    """A raw device pointer seen as a torch tensor (CUDA array interface)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (int(ptr), False),
+                                         "version": 3, "strides": None}
+
+
+class GatherSpace:
+    """Output buffers, flags and counters of a sequence of gathered GEMM call
+    sites, in one device allocation per rank that every rank maps (CUDA IPC).
+
+    Site i owns, in every rank's allocation, a full output [rows_i, cols_i]
+    fp16, one flag word per source rank (rank r writes word r) and two counter
+    words; plus, for its own wait on an earlier site's flags, one wait-count
+    word. A site's output is written by every rank's GEMM for that site and
+    read by later sites; a separate buffer per call site keeps a rank from
+    overwriting data another rank has not read yet.
+    """
+
+    _ALIGN = 256
+
+    def __init__(self, sites, group=None):
+        import torch
+        import torch.distributed as dist
+
+        from . import _check, _lib
+
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("at most 8 ranks")
+        self.sites = [(int(r), int(c)) for r, c in sites]
+        off = 0
+        self._off = []
+        for rows, cols in self.sites:
+            o_out = off
+            off = _align(off + rows * cols * 2, self._ALIGN)
+            o_flag = off
+            off = _align(off + 4 * self.world, self._ALIGN)
+            o_cnt = off
+            off = _align(off + 16, self._ALIGN)
+            self._off.append((o_out, o_flag, o_cnt))
+        self.bytes = max(off, self._ALIGN)
+        lib = _lib()
+        base = ctypes.c_void_p()
+        _check(lib.busfill_ipc_alloc(self.bytes, ctypes.byref(base)), "busfill_ipc_alloc")
+        self._base = base.value
+        handle = ctypes.create_string_buffer(64)
+        _check(lib.busfill_ipc_get_handle(self._base, handle), "busfill_ipc_get_handle")
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.bases = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                self.bases.append(self._base)
+                continue
+            p = ctypes.c_void_p()
+            hb = ctypes.create_string_buffer(h, 64)
+            _check(lib.busfill_ipc_open(hb, ctypes.byref(p)), "busfill_ipc_open")
+            self.bases.append(p.value)
+        self._structs = {}
+        self._torch = torch
+
+    def output(self, site):
+        """This rank's full output of `site` as a torch fp16 tensor [rows, cols]."""
+        rows, cols = self.sites[site]
+        return self._torch.as_tensor(_DevArray(self._base + self._off[site][0], (rows, cols), "<f2"),
+                                     device=self._torch.device("cuda", self._torch.cuda.current_device()))
+
+    def args(self, site, wait_site=None):
+        """The busfill_gather struct of `site` on this rank (cached)."""
+        key = (site, wait_site)
+        g = self._structs.get(key)
+        if g is not None:
+            return g
+        rows, cols = self.sites[site]
+        start, stop = shard_rows(cols, self.world, self.rank)
+        o_out, o_flag, o_cnt = self._off[site]
+        g = Gather()
+        g.npeers = self.world
+        g.col_off = start
+        g.ldc = cols
+        for q in range(self.world):
+            g.out[q] = self.bases[q] + o_out
+            g.flag[q] = self.bases[q] + o_flag + 4 * self.rank
+        g.counters = self._base + o_cnt
+        if wait_site is not None:
+            g.wait = self._base + self._off[wait_site][1]
+            g.wait_gen = self._base + o_cnt + 8      # this site's count of waits on wait_site's flags
+            g.nwait = self.world
+        self._structs[key] = g
+        return g
+
+    def close(self):
+        from . import _lib
+        lib = _lib()
+        for q, b in enumerate(self.bases):
+            if q != self.rank and b:
+                lib.busfill_ipc_close(b)
+        if self._base:
+            lib.busfill_ipc_free(self._base)
+        self.bases, self._base = [], 0
+
+
+def _align(x, a):
+    return (x + a - 1) // a * a
+
+
+def gemm_q4k_gather(blocks_local, a, space, site, wait_site=None, stream=None):
+    """C = A @ deq(W)^T with W's rows split over the group and the all-gather
+    done by the GEMM epilogue (busfill_gemm_q4k_gather); returns this rank's
+    full output of `site`. `wait_site`: the site whose gathered output `a` is."""
+    from . import _check, _lib, _ptr, _stream
+    m, k = a.shape
+    n = blocks_local.shape[0]
+    g = space.args(site, wait_site)
+    _check(_lib().busfill_gemm_q4k_gather(_ptr(blocks_local), _ptr(a), m, n, k, ctypes.byref(g), _stream(stream)),
+           "busfill_gemm_q4k_gather")
+    return space.output(site)
+
+
+def gemm_q4k_swiglu_gather(w_gate_local, w_up_local, a, space, site, wait_site=None, stream=None):
+    """busfill_gemm_q4k_swiglu on this rank's gate/up rows with the gathered output."""
+    from . import _check, _lib, _ptr, _stream
+    m, k = a.shape
+    n = w_gate_local.shape[0]
+    g = space.args(site, wait_site)
+    _check(_lib().busfill_gemm_q4k_swiglu_gather(_ptr(w_gate_local), _ptr(w_up_local), _ptr(a), m, n, k,
+                                                 ctypes.byref(g), _stream(stream)),
+           "busfill_gemm_q4k_swiglu_gather")
+    return space.output(site)

@@ -81,6 +81,58 @@ BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint1
 BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, uint16_t* h,
                                         int M, int N, int K, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Column-split GEMMs with the all-gather fused into the epilogue
+ *
+ * Over a group of `npeers` GPUs (one process each, same node), rank r holds
+ * rows [col_off, col_off + N) of a weight whose full output has `ldc`
+ * columns. Each rank's GEMM writes its [M, N] slice straight into every
+ * rank's full output buffer (out[q] is rank q's [M, ldc] buffer, mapped into
+ * this process, e.g. with busfill_ipc_open), over NVLink, and once the whole
+ * slice has landed it sets flag[q] (a word in rank q's memory that only this
+ * rank writes) to the call site's next generation. A later GEMM whose
+ * activations are that gathered output passes the nwait local words it must
+ * wait on (`wait`, one per source rank) and `wait_gen`, a local word counting
+ * how often this consumer has waited on them; its kernel waits (acquire,
+ * bounded by 1 s, else BUSFILL_ERR_DEVICE_TIMEOUT) until every word reaches
+ * *wait_gen + 1, then advances *wait_gen. Generations live in device memory,
+ * so the calls can be captured in a CUDA graph and replayed. No NCCL call, no
+ * host round trip. `counters` is two zeroed device words of this rank per
+ * call site (a CTA count the kernel leaves at zero, and the generation).
+ * Every rank must make the same calls in the same order. The reference is
+ * single-GPU (no counterpart); this is BASELINE's N-split with its
+ * all-gather moved into the GEMM.
+ * ------------------------------------------------------------------------- */
+#define BUSFILL_MAX_PEERS 8
+typedef struct busfill_gather {
+  int npeers;                        /* ranks receiving the output (this one included), 1..8 */
+  int col_off;                       /* first column of this rank's slice */
+  int ldc;                           /* columns of the full outputs */
+  uint16_t* out[BUSFILL_MAX_PEERS];  /* each rank's full output [M, ldc] fp16 (device pointers) */
+  uint32_t* flag[BUSFILL_MAX_PEERS]; /* per rank q: the word this rank sets in rank q's memory */
+  uint32_t* counters;                /* this rank's 2 zeroed words for this call site */
+  const uint32_t* wait;              /* optional: nwait local flag words to wait on before reading a */
+  uint32_t* wait_gen;                /* with wait: local word, waits done so far on those flags */
+  int nwait;
+} busfill_gather;
+
+/* busfill_gemm_q4k on this rank's weight rows [N, K/256 x 144 B], output
+ * gathered per `g` (g->out[rank] is this rank's own full output). */
+BUSFILL_API int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int N, int K,
+                                        const busfill_gather* g, void* stream);
+/* busfill_gemm_q4k_swiglu on this rank's gate/up rows, output gathered per `g`. */
+BUSFILL_API int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, int M,
+                                               int N, int K, const busfill_gather* g, void* stream);
+
+/* CUDA IPC for the peer buffers above: a 64-byte handle of a device
+ * allocation (cudaIpcGetMemHandle), its mapping in another process of the
+ * same node (cudaIpcOpenMemHandle, peer access enabled lazily), and unmapping. */
+BUSFILL_API int busfill_ipc_alloc(size_t bytes, void** dev_ptr); /* cudaMalloc + zero fill, shareable */
+BUSFILL_API int busfill_ipc_free(void* dev_ptr);
+BUSFILL_API int busfill_ipc_get_handle(const void* dev_ptr, void* handle64);
+BUSFILL_API int busfill_ipc_open(const void* handle64, void** dev_ptr);
+BUSFILL_API int busfill_ipc_close(void* dev_ptr);
+
 /* Q4_0 as llama.cpp stores it: block_q4_0 rows, K/32 blocks of 18 bytes per
  * weight row (fp16 d, then 16 bytes whose low nibbles are elements 0-15 and
  * high nibbles elements 16-31); value = (q - 8) * d, the same rule as
