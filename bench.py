@@ -198,23 +198,28 @@ def run_busfill(args):
         wq, ws = make_q4_0_weights(torch, n_loc, K, gen, dev)
         weights = [(wq, ws)] + [(wq.clone(), ws.clone()) for _ in range(R - 1)]
     a = torch.randn((M, K), device=dev, generator=gen).half()
+    a_full = a
     c_loc = torch.empty((M, n_loc), dtype=torch.float16, device=dev)
     c_full = torch.empty((M, N), dtype=torch.float16, device=dev) if world > 1 else None
+    # Q4_K over several GPUs: the all-gather runs in the GEMM epilogue (peer
+    # stores into every rank's output, one call site per weight copy);
+    # Q4_0: NCCL all-gather after the GEMM
+    space = tp.GatherSpace([(M, N)] * R) if (world > 1 and args.fmt == "q4k") else None
 
-    def gemm(w, stream):
+    def gemm(w, stream, i=0):
         if world == 1:
             if args.fmt == "q4k":
                 bf.gemm_q4k(w, a, out=c_loc, stream=stream)
             else:
                 bf.gemm_q4_0(w[0], w[1], a, out=c_loc, stream=stream)
-        elif args.fmt == "q4k":     # N-split: local rows through the C ABI, NCCL all-gather of the slices
-            tp.gemm_q4k_tp(w, a, N, out=c_full, local_out=c_loc)
+        elif space is not None:
+            tp.gemm_q4k_gather(w, a_full, space, i, stream=stream)
         else:
             tp.gemm_q4_0_tp(w[0], w[1], a, N, out=c_full, local_out=c_loc)
 
     def one_step(stream):
-        for w in weights:
-            gemm(w, stream)
+        for i, w in enumerate(weights):
+            gemm(w, stream, i)
 
     stream = torch.cuda.Stream(device=dev)
     stream.wait_stream(torch.cuda.current_stream())
@@ -292,7 +297,9 @@ def run_busfill(args):
         "data": "synthetic (seeded torch RNG, BASELINE config distributions)",
         "config": {
             "workload": workload, "format": args.fmt, "M": M, "N": N, "K": K,
-            "parallelism": f"tp{world} (N-split + NCCL all-gather)" if world > 1 else "single GPU",
+            "parallelism": (f"tp{world} (N-split, all-gather fused into the GEMM epilogue: NVLink peer stores)"
+                            if space is not None else f"tp{world} (N-split + NCCL all-gather)") if world > 1
+                           else "single GPU",
             "weight_copies": R, "weight_set_bytes": R * wbytes,
             "l2": f"inputs larger than L2: {R} rotating weight copies, {R * wbytes / 1e6:.0f} MB > 2x L2 "
                   f"({l2 / 1e6:.0f} MB)",
@@ -318,12 +325,15 @@ def run_busfill(args):
         out["e2e"] = e2e(torch, bf, dev, weights, a, args, max(10, steps // 10))
         out["cpu_baseline"] = cpu_baseline(args)
     elif world > 1:
-        out["e2e"] = e2e_tp(torch, bf, tp, dev, weights, a, args, N, max(10, steps // 10))
+        out["e2e"] = e2e_tp(torch, bf, tp, dev, weights, a, args, N, max(10, steps // 10), space)
 
     if rank == 0:
         print(json.dumps(out))
     if world > 1:
+        torch.cuda.synchronize(dev)
         dist.barrier()
+        if space is not None:
+            space.close()
         dist.destroy_process_group()
 
 
@@ -436,30 +446,30 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
     x = (torch.randn((m, 5120), device=dev, generator=gen) / 64).half()
     attn = (torch.randn((m, 8192), device=dev, generator=gen) / 64).half()
     full = {name: torch.empty((m, n), dtype=torch.float16, device=dev) for name, (n, _) in shapes.items()}
-    loc = {name: torch.empty((m, tp.shard_rows(n, world, rank)[1] - tp.shard_rows(n, world, rank)[0]),
-                             dtype=torch.float16, device=dev) for name, (n, _) in shapes.items()}
     st = torch.cuda.Stream(device=dev)
+    # over several GPUs every GEMM's all-gather runs in its epilogue: one call
+    # site (output buffer, flags) per layer and projection
+    ops = ("qkv", "o", "gate", "down")
+    space = (tp.GatherSpace([(m, shapes[name][0]) for _ in range(L) for name in ops]) if world > 1 else None)
 
-    def gemm(name, w, a):
-        n = shapes[name][0]
-        if world == 1:
-            return bf.gemm_q4k(w, a, out=full[name], stream=st)
-        return tp.gemm_q4k_tp(w, a, n, out=full[name], local_out=loc[name])
-
-    def swiglu(lw, a):
-        n = shapes["gate"][0]
-        if world == 1:
-            return bf.gemm_q4k_swiglu(lw["gate"], lw["up"], a, out=full["gate"], stream=st)
-        bf.gemm_q4k_swiglu(lw["gate"], lw["up"], a, out=loc["gate"], stream=torch.cuda.current_stream())
-        return tp.gather_columns(loc["gate"], n, out=full["gate"])
+    def site(layer, name):
+        return layer * len(ops) + ops.index(name)
 
     def sweep():
-        h = x
-        for lw in layers:
-            gemm("qkv", lw["qkv"], h)             # its output would feed attention (outside the path)
-            o = gemm("o", lw["o"], attn)
-            g = swiglu(lw, o)
-            h = gemm("down", lw["down"], g)
+        h, h_site = x, None
+        for li, lw in enumerate(layers):
+            if space is None:
+                bf.gemm_q4k(lw["qkv"], h, out=full["qkv"], stream=st)   # would feed attention (outside the path)
+                o = bf.gemm_q4k(lw["o"], attn, out=full["o"], stream=st)
+                g = bf.gemm_q4k_swiglu(lw["gate"], lw["up"], o, out=full["gate"], stream=st)
+                h = bf.gemm_q4k(lw["down"], g, out=full["down"], stream=st)
+            else:
+                tp.gemm_q4k_gather(lw["qkv"], h, space, site(li, "qkv"), wait_site=h_site, stream=st)
+                o = tp.gemm_q4k_gather(lw["o"], attn, space, site(li, "o"), stream=st)
+                g = tp.gemm_q4k_swiglu_gather(lw["gate"], lw["up"], o, space, site(li, "gate"),
+                                              wait_site=site(li, "o"), stream=st)
+                h = tp.gemm_q4k_gather(lw["down"], g, space, site(li, "down"), wait_site=site(li, "gate"), stream=st)
+                h_site = site(li, "down")
 
     with torch.cuda.stream(st):
         sweep()
@@ -485,13 +495,17 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
         ms = float(t.item())
     del g
     del layers
+    if space is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        space.close()
     torch.cuda.empty_cache()
     return {"layers": L, "M": m, "ms_per_sweep": round(ms, 4), "tokens_per_s": round(m / (ms * 1e-3), 1),
             "weight_bytes_total": total_bytes, "weight_bytes_per_gpu": local_bytes,
             "GB_s_total": round(total_bytes / (ms * 1e-3) / 1e9, 1),
             "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / hbm_peak, 4),
-            "n_gpus": world, "parallelism": f"tp{world} column split + NCCL all-gather per GEMM" if world > 1
-            else "single GPU", "kernels": "busfill_gemm_q4k x3 + busfill_gemm_q4k_swiglu per layer",
+            "n_gpus": world, "parallelism": (f"tp{world} column split, all-gather fused into every GEMM's epilogue "
+                                             f"(NVLink peer stores + flags)") if world > 1 else "single GPU", "kernels": "busfill_gemm_q4k x3 + busfill_gemm_q4k_swiglu per layer",
             "timing": f"CUDA graph of one {L}-layer sweep, {sweeps} replays, CUDA events, max over ranks"}
 
 
@@ -617,11 +631,12 @@ def e2e(torch, bf, dev, weights, a, args, steps):
             "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* (C ABI via ctypes) -> pinned host C"}
 
 
-def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps):
+def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps, space=None):
     """e2e with the weight rows split over the ranks: every call copies the
     activations from pinned host memory, runs this rank's rows through the C
-    ABI, all-gathers the output slices (NCCL) and reads the full C back to
-    pinned host memory. Max over ranks."""
+    ABI with the all-gather in the GEMM epilogue (Q4_K; NCCL after the GEMM for
+    Q4_0), waits for the gathered output and reads the full C back to pinned
+    host memory. Max over ranks."""
     import torch.distributed as dist
 
     m, k = a.shape
@@ -633,13 +648,15 @@ def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps):
     st = torch.cuda.Stream(device=dev)
 
     def step():
-        for w in weights:
+        for i, w in enumerate(weights):
             d_a.copy_(h_a, non_blocking=True)
-            if args.fmt == "q4k":
-                tp.gemm_q4k_tp(w, d_a, n_total, out=d_c)
+            if space is not None:
+                out = tp.gemm_q4k_gather(w, d_a, space, i, stream=st)
+                space.wait(i, stream=st)
+                h_c.copy_(out, non_blocking=True)
             else:
                 tp.gemm_q4_0_tp(w[0], w[1], d_a, n_total, out=d_c)
-            h_c.copy_(d_c, non_blocking=True)
+                h_c.copy_(d_c, non_blocking=True)
 
     with torch.cuda.stream(st):
         for _ in range(2):
@@ -660,8 +677,11 @@ def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps):
     return {"value": round(m * calls / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": len(weights) * m * k * 2, "d2h_bytes_per_step": len(weights) * m * n_total * 2,
             "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps,
-            "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* on this rank's rows (C ABI) -> "
-                    "NCCL all-gather -> pinned host C (every rank), max over ranks"}
+            "path": ("pinned host A -> cudaMemcpyAsync -> busfill_gemm_q4k_gather on this rank's rows (C ABI; "
+                     "all-gather in the epilogue) -> busfill_gather_wait -> pinned host C (every rank), max over "
+                     "ranks") if space is not None else
+                    ("pinned host A -> cudaMemcpyAsync -> busfill_gemm_* on this rank's rows (C ABI) -> "
+                     "NCCL all-gather -> pinned host C (every rank), max over ranks")}
 
 
 # ---------------------------------------------------------------------------

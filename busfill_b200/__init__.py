@@ -77,6 +77,7 @@ _SIGS = {
     "busfill_gemm_kernel_for": [_I, _I],
     "busfill_gemm_q4k_gather": [_P, _P, _I, _I, _I, _P, _P],
     "busfill_gemm_q4k_swiglu_gather": [_P, _P, _P, _I, _I, _I, _P, _P],
+    "busfill_gather_wait": [_P, _P],
     "busfill_ipc_alloc": [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)],
     "busfill_ipc_free": [_P],
     "busfill_ipc_get_handle": [_P, _P],

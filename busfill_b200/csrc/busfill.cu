@@ -506,6 +506,22 @@ int grid_for(long long work, int sm_count) {
 }
 
 // ---------------------------------------------------------------------------
+// waiting for a gathered output outside a GEMM
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(32, 1) gather_wait_kernel(const unsigned* wait, unsigned* wait_gen, int nwait,
+                                                            unsigned* error) {
+  const unsigned target = *wait_gen + 1u;
+  bool got = true;
+  for (int i = threadIdx.x; i < nwait; i += 32) got = got && wait_flag_sys(wait + i, target);
+  got = __all_sync(0xffffffffu, got);
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    if (!got) atomicOr(error, kErrActProducer);
+    *wait_gen = target;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // statically allocated scratch (busfill_gemm_q4k_noalloc)
 // ---------------------------------------------------------------------------
 constexpr int kMaxDevices = 64;
@@ -616,6 +632,24 @@ int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int
 int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, int M, int N, int K,
                                    const busfill_gather* g, void* stream) {
   return gemm_gather_impl<WFmt::Q4K>(w_gate, w_up, true, a, M, N, K, g, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gather_wait(const busfill_gather* g, void* stream) {
+  if (!g || !g->wait || !g->wait_gen || g->nwait < 1 || g->nwait > 32) return BUSFILL_ERR_INVALID_ARG;
+  DeviceInfo di;
+  int dev = 0;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  unsigned* err = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = get_error_words(dev, s, &err);
+  }
+  if (st != BUSFILL_OK) return st;
+  gather_wait_kernel<<<1, 32, 0, s>>>(g->wait, g->wait_gen, g->nwait, err);
+  if (cudaGetLastError() != cudaSuccess) return BUSFILL_ERR_LAUNCH;
+  return BUSFILL_OK;
 }
 
 int busfill_ipc_alloc(size_t bytes, void** dev_ptr) {

@@ -548,7 +548,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (t < p.M) Cq[(size_t)t * p.gather.ldc] = to_out<OutT>(acc[t]);
           }
         }
-        __threadfence_system();  // visible to every rank before the flags go up
       } else if (ok && n < p.N) {
 #pragma unroll
         for (int t = 0; t < NB; ++t)
@@ -602,13 +601,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   // no CTA may leave while another CTA of its cluster can still read its
   // shared memory or arrive on its barriers
   if (csize > 1) cluster_wait();
-  // gathered output: the last CTA to finish raises this rank's flag in every
-  // rank's memory (each CTA fenced its peer stores at system scope first) to
-  // the call site's next generation, and advances this consumer's wait count
+  // Gathered output: the last CTA to finish raises this rank's flag in every
+  // rank's memory to the call site's next generation, and advances this
+  // consumer's wait count. Ordering: each CTA's peer stores precede its
+  // thread 0 (the CTA barrier above), thread 0 releases them at GPU scope
+  // with its counter increment, the last CTA acquires that and releases
+  // everything at system scope with the flag stores, which the consumers
+  // acquire (the pattern of a data-then-flag protocol over NVLink).
   if ((p.gather.signal || p.gather.nwait > 0) && threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(p.gather.counters, 1u);
     if (prev == gridDim.x - 1) {
+      __threadfence();
       p.gather.counters[0] = 0u;  // ready for the next launch
       if (p.gather.nwait > 0) *p.gather.wait_gen += 1u;
       if (p.gather.signal) {

@@ -224,6 +224,20 @@ class GatherSpace:
         self._structs[key] = g
         return g
 
+    def wait(self, site, stream=None):
+        """Make `stream` wait (on the device) until `site`'s gathered output is
+        complete on this rank, for consumers that are not busfill GEMMs."""
+        from . import _check, _lib, _stream
+        key = ("wait", site)
+        g = self._structs.get(key)
+        if g is None:
+            g = Gather()
+            g.wait = self._base + self._off[site][1]
+            g.wait_gen = self._base + self._off[site][2] + 12   # this site's standalone wait count
+            g.nwait = self.world
+            self._structs[key] = g
+        _check(_lib().busfill_gather_wait(ctypes.byref(g), _stream(stream)), "busfill_gather_wait")
+
     def close(self):
         from . import _lib
         lib = _lib()

@@ -124,6 +124,13 @@ BUSFILL_API int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a
 BUSFILL_API int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, int M,
                                                int N, int K, const busfill_gather* g, void* stream);
 
+/* Make `stream` wait until a gathered output is complete on this rank: one
+ * small kernel waits (acquire, bounded by 1 s) until every word of g->wait
+ * reaches *g->wait_gen + 1 and then advances *g->wait_gen, as a consuming
+ * GEMM would. For consumers that are not busfill GEMMs (a copy to the host,
+ * another library's kernel). Only the wait fields of `g` are read. */
+BUSFILL_API int busfill_gather_wait(const busfill_gather* g, void* stream);
+
 /* CUDA IPC for the peer buffers above: a 64-byte handle of a device
  * allocation (cudaIpcGetMemHandle), its mapping in another process of the
  * same node (cudaIpcOpenMemHandle, peer access enabled lazily), and unmapping. */
