@@ -19,7 +19,7 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q5k", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k",
     "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "uses_prefill", "probe_umma", "version",
 ]
 
@@ -62,6 +62,8 @@ _SIGS = {
     "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4_0_ggml": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k_swiglu": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q5k": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_dequant_q5k": [_P, _P, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
@@ -291,6 +293,32 @@ def dequant_q4k(blocks, k, out=None, stream=None):
     if out is None:
         out = torch.empty((n, k), dtype=torch.float16, device=blocks.device)
     _check(_lib().busfill_dequant_q4k(_ptr(blocks), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q4k")
+    return out
+
+
+def gemm_q5k(blocks, a, out=None, stream=None):
+    """C[M, N] = A[M, K] @ deq(W)[N, K]^T for llama.cpp block_q5_K rows
+    [N, K/256*176]; fp16 out."""
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = blocks.shape[0]
+    if k % 256 or blocks.shape[1] != k // 256 * 176:
+        raise ValueError(f"shape mismatch: blocks {tuple(blocks.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q5k(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)), "busfill_gemm_q5k")
+    return out
+
+
+def dequant_q5k(blocks, k, out=None, stream=None):
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks")
+    n = blocks.shape[0]
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.float16, device=blocks.device)
+    _check(_lib().busfill_dequant_q5k(_ptr(blocks), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q5k")
     return out
 
 

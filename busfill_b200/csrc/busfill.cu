@@ -188,19 +188,19 @@ cudaError_t launch(const void* func, dim3 grid, dim3 block, size_t smem, cudaStr
 // ---------------------------------------------------------------------------
 // decode GEMM launch
 // ---------------------------------------------------------------------------
-template <WFmt FMT, int NB, typename OutT, bool SW = false>
+template <WFmt FMT, int NB, typename OutT, bool SW = false, bool GA = false>
 const void* decode_kernel_ptr() {
-  return reinterpret_cast<const void*>(decode_gemm_kernel<FMT, NB, OutT, SW>);
+  return reinterpret_cast<const void*>(decode_gemm_kernel<FMT, NB, OutT, SW, GA>);
 }
 
 // Raise the kernel's dynamic shared memory limit, once per device.
-template <WFmt FMT, int NB, typename OutT, bool SW = false>
+template <WFmt FMT, int NB, typename OutT, bool SW = false, bool GA = false>
 bool decode_smem_attr(int dev) {
   static std::once_flag once[64];
   static cudaError_t err[64];
   std::call_once(once[dev & 63], [&] {
-    err[dev & 63] = cudaFuncSetAttribute(decode_kernel_ptr<FMT, NB, OutT, SW>(),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<NB>::kAlloc);
+    err[dev & 63] = cudaFuncSetAttribute(decode_kernel_ptr<FMT, NB, OutT, SW, GA>(),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, DecodeSmem<NB, FMT>::kAlloc);
   });
   return err[dev & 63] == cudaSuccess;
 }
@@ -219,7 +219,7 @@ int max_active_clusters(int dev, int csize, int sm_count) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(csize * std::max(1, sm_count / csize)));
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = DecodeSmem<NB>::kAlloc;
+  cfg.dynamicSmemBytes = DecodeSmem<NB, FMT>::kAlloc;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)csize;
@@ -262,7 +262,7 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count, int segs) {
     const long long rounds = (T + ncl - 1) / ncl;
     const long long units = rounds * segs * ((S + c - 1) / c);
     const double rate = std::min(kSmGBs, kHbmGBs / (double)(ncl * c));
-    const double ns = (double)units * kWStageBytes / rate;
+    const double ns = (double)units * wstage_bytes<FMT>() / rate;
     if (ns < best_ns * 0.999) {
       best_ns = ns;
       best.csize = c;
@@ -272,14 +272,14 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count, int segs) {
   return best;
 }
 
-template <WFmt FMT, int NB, typename OutT, bool SW = false>
+template <WFmt FMT, int NB, typename OutT, bool SW = false, bool GA = false>
 int launch_decode_nb(const DeviceInfo& di, const CUtensorMap& tw, const CUtensorMap& tws, const CUtensorMap& ta,
                      const DecodeParams& p, cudaStream_t s) {
-  const void* kern = decode_kernel_ptr<FMT, NB, OutT, SW>();
-  constexpr int smem = DecodeSmem<NB>::kAlloc;
+  const void* kern = decode_kernel_ptr<FMT, NB, OutT, SW, GA>();
+  constexpr int smem = DecodeSmem<NB, FMT>::kAlloc;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!decode_smem_attr<FMT, NB, OutT, SW>(dev)) return BUSFILL_ERR_LAUNCH;
+  if (!decode_smem_attr<FMT, NB, OutT, SW, GA>(dev)) return BUSFILL_ERR_LAUNCH;
   const int grid = p.nclusters * p.csize;
   void* args[] = {const_cast<CUtensorMap*>(&tw), const_cast<CUtensorMap*>(&tws), const_cast<CUtensorMap*>(&ta),
                   const_cast<DecodeParams*>(&p)};
@@ -313,14 +313,16 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
 
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
-  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4_0G) {
-    // 144 bytes per 256 values of a row: one block_q4_K or eight block_q4_0
-    const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
-    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, kTileRows,
+  if constexpr (aos_rows<FMT>()) {
+    // whole block rows: 144 bytes per 256 values (one block_q4_K, eight
+    // block_q4_0) or 176 (one block_q5_K)
+    constexpr int ub = unit_row_bytes<FMT>();
+    const uint64_t row = (uint64_t)S * ub;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, ub, kTileRows,
                       CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
     tws = tw;  // the up projection's map with SwiGLU, else unused
-    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, kQ4KBlockBytes,
+    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, ub,
                                 kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   } else {
@@ -370,13 +372,20 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     p.units_per_tile = S;
     p.csize = sch.csize;
     p.nclusters = sch.nclusters;
-    int st = BUSFILL_OK;
-    if constexpr (FMT != WFmt::Q4_0 && std::is_same<OutT, __half>::value) {
-      if (swiglu)
+    int st = BUSFILL_ERR_INVALID_ARG;
+    if constexpr (FMT == WFmt::Q4K && std::is_same<OutT, __half>::value) {
+      // the SwiGLU and gathered entry points are Q4_K
+      if (swiglu && gather)
+        st = nb == 16 ? launch_decode_nb<FMT, 16, OutT, true, true>(di, tw, tws, ta, p, s)
+                      : launch_decode_nb<FMT, 32, OutT, true, true>(di, tw, tws, ta, p, s);
+      else if (swiglu)
         st = nb == 16 ? launch_decode_nb<FMT, 16, OutT, true>(di, tw, tws, ta, p, s)
                       : launch_decode_nb<FMT, 32, OutT, true>(di, tw, tws, ta, p, s);
+      else if (gather)
+        st = nb == 16 ? launch_decode_nb<FMT, 16, OutT, false, true>(di, tw, tws, ta, p, s)
+                      : launch_decode_nb<FMT, 32, OutT, false, true>(di, tw, tws, ta, p, s);
     }
-    if (!swiglu)
+    if (!swiglu && !gather)
       st = nb == 16 ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
                     : launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
     if (st != BUSFILL_OK) return st;
@@ -394,15 +403,16 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   const int swiglu = w_up ? 1 : 0;
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
-  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4_0G) {
+  if constexpr (aos_rows<FMT>()) {
     // one 256-row box per unit, or with SwiGLU one 128-row box from each matrix
-    const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
+    constexpr int ub = unit_row_bytes<FMT>();
+    const uint64_t row = (uint64_t)S * ub;
     const uint32_t box_rows = swiglu ? kTileRows : prefill::kPairRows;
-    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, kQ4KBlockBytes, box_rows,
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, ub, box_rows,
                       CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
     tws = tw;
-    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, kQ4KBlockBytes,
+    if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, ub,
                                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   } else {
@@ -421,7 +431,7 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
     static std::once_flag once[64];
     static cudaError_t err[64];
     std::call_once(once[dev & 63], [&] {
-      err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::kAlloc);
+      err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::Smem<FMT>::kAlloc);
     });
     if (err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
   }
@@ -438,7 +448,7 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   const long long items = (long long)p.pairs * p.btiles;
   const int grid = (int)std::min<long long>(items, di.sm_count);
   void* args[] = {&tw, &tws, &ta, &p};
-  if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::kAlloc, s, args, g_use_pdl.load() != 0) !=
+  if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::Smem<FMT>::kAlloc, s, args, g_use_pdl.load() != 0) !=
       cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_LAUNCH;
@@ -624,6 +634,10 @@ int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const ui
                                       true);
 }
 
+int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
+  return gemm_impl<WFmt::Q5K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
 int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int N, int K, const busfill_gather* g,
                             void* stream) {
   return gemm_gather_impl<WFmt::Q4K>(blocks, nullptr, false, a, M, N, K, g, reinterpret_cast<cudaStream_t>(stream));
@@ -754,6 +768,20 @@ int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N, int K, void
   if (st != BUSFILL_OK) return st;
   const long long nc = (long long)N * (K / 256) * 4;
   dequant_q4k_kernel<<<grid_for(nc, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      blocks, reinterpret_cast<__half*>(out), nc);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_dequant_q5k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream) {
+  if (!blocks || !out) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 256 || K % 256 != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(blocks) || !aligned16(out)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nc = (long long)N * (K / 256) * 4;
+  dequant_q5k_kernel<<<grid_for(nc, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       blocks, reinterpret_cast<__half*>(out), nc);
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
 }

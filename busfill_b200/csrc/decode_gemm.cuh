@@ -136,8 +136,8 @@ constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
 // units of one parity and so waited on by one dequant group in phase order
 // (a group that skipped the other group's phase of a stage could see that
 // stale phase as complete: mbarrier waits only tell parities apart).
-template <int NB>
-constexpr int w_stages() { return 6; }
+template <int NB, WFmt FMT>
+constexpr int w_stages() { return FMT == WFmt::Q5K ? 4 : 6; }  // Q5_K stages are 22 KB
 
 // Activation ring depth (one unit per stage), separate from the TMEM operand
 // slots so that a unit's activations are requested several units ahead: a
@@ -146,16 +146,18 @@ constexpr int w_stages() { return 6; }
 template <int NB>
 constexpr int x_stages() { return NB == 32 ? 4 : 6; }
 
-template <int NB>
+template <int NB, WFmt FMT>
 struct DecodeSmem {
   static constexpr int kXChunkBytes = NB * 128;                      // one 64-value activation box
   static constexpr int kXSlotBytes = kChunksPerUnit * kXChunkBytes;  // one unit of activations
   static constexpr int kWOff = 0;
-  static constexpr int kWStages = w_stages<NB>();
+  static constexpr int kWStage = wstage_bytes<FMT>();               // one unit of 128 weight rows
+  static constexpr int kWStages = w_stages<NB, FMT>();
   static_assert(kWStages % 2 == 0, "each weight stage must belong to one dequant group");
   static constexpr int kXStages = x_stages<NB>();
   static_assert(kXStages >= kSlots, "an activation stage per operand slot at least");
-  static constexpr int kXOff = kWOff + kWStages * kWStageBytes;
+  static constexpr int kXOff = kWOff + kWStages * kWStage;
+  static_assert(kXOff % 1024 == 0, "swizzled activation stages need 1 KB alignment");
   static constexpr int kRedOff = kXOff + kXStages * kXSlotBytes;      // rank 0: [rank-1][128][NB] fp32 partials
   static constexpr int kRedRankBytes = kTileRows * NB * 4;
   static constexpr int kBarOff = kRedOff + (max_cluster<NB>() - 1) * kRedRankBytes;
@@ -205,15 +207,17 @@ __device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, in
 // SW: SwiGLU pair (144-byte formats): tmap_w is the gate, tmap_ws the up
 // projection, C = silu(A Wg^T) * (A Wu^T); every tile index of the cluster
 // becomes two segments (gate, up).
-template <WFmt FMT, int NB, typename OutT, bool SW = false>
+// GA: the output is gathered over a process group (GatherArgs); else it is
+// written to the local C only.
+template <WFmt FMT, int NB, typename OutT, bool SW = false, bool GA = false>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                        const __grid_constant__ CUtensorMap tmap_a, const DecodeParams p) {
   static_assert(NB == 16 || NB == 32, "batch tile");
-  using L = DecodeSmem<NB>;
+  using L = DecodeSmem<NB, FMT>;
   using TM = DecodeTmem<NB>;
-  constexpr bool kRows144 = (FMT != WFmt::Q4_0);  // 144-byte row units (block_q4_K, 8 x block_q4_0)
-  static_assert(!SW || kRows144, "SwiGLU pairs take 144-byte row formats");
+  constexpr bool kRows144 = aos_rows<FMT>();  // whole block rows per unit (block_q4_K / q5_K, 8 x block_q4_0)
+  static_assert(!SW || kRows144, "SwiGLU pairs take block-row formats");
   constexpr int kSw = SW ? 1 : 0;
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
   constexpr int kWStages = L::kWStages;
@@ -268,10 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto issue_w_thread = [&](int i) {
     const int s = i % kWStages;
     const UnitInfo ui = unit_info(i, len, sb0, g, p.nclusters, kSw);
-    const uint32_t dst = sbase + L::kWOff + s * kWStageBytes;
-    mbar_arrive_expect_tx(BAR(L::bWFull + s), kWStageBytes);
+    const uint32_t dst = sbase + L::kWOff + s * L::kWStage;
+    mbar_arrive_expect_tx(BAR(L::bWFull + s), L::kWStage);
     if constexpr (kRows144) {
-      tma_load_2d(dst, ui.up ? &tmap_ws : &tmap_w, ui.sb * kQ4KBlockBytes, ui.tile * kTileRows, BAR(L::bWFull + s),
+      tma_load_2d(dst, ui.up ? &tmap_ws : &tmap_w, ui.sb * unit_row_bytes<FMT>(), ui.tile * kTileRows, BAR(L::bWFull + s),
                   kPolicyEvictFirst);
     } else {
       tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
@@ -324,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
     named_bar_sync(1, 64);
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
-    if (p.gather.nwait > 0) {
+    if (GA && p.gather.nwait > 0) {
       // activations gathered by an earlier GEMM on every rank: wait for each
       // rank's flag, then let this thread's TMA copies see what it acquired
       const unsigned target = *p.gather.wait_gen + 1u;  // advanced by the previous call's last CTA
@@ -445,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // operand slot i % kSlots is free once the MMAs of unit i - kSlots completed
       if (i >= kSlots && !warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       tc_fence_after();
-      const uint8_t* stage = smem + L::kWOff + ws * kWStageBytes;
+      const uint8_t* stage = smem + L::kWOff + ws * L::kWStage;
       dequant_unit_row<FMT>(stage, stage + kQ40ScaleOffset, r, tmem + lane_off + TM::kA + (i % kSlots) * 128);
       tc_wait_st();
       tc_fence_before();
@@ -538,9 +542,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < NB; ++t) acc[t] = silu(gate[t]) * acc[t];
       }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
-      if (p.gather.npeers > 0) {
+      if (GA) {
         // this rank's slice into every rank's full output (peer stores over NVLink)
         if (ok && n < p.N) {
+#pragma unroll 1
           for (int q = 0; q < p.gather.npeers; ++q) {
             OutT* Cq = reinterpret_cast<OutT*>(p.gather.out[q]) + p.gather.col_off + n;
 #pragma unroll
@@ -608,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // with its counter increment, the last CTA acquires that and releases
   // everything at system scope with the flag stores, which the consumers
   // acquire (the pattern of a data-then-flag protocol over NVLink).
-  if ((p.gather.signal || p.gather.nwait > 0) && threadIdx.x == 0) {
+  if (GA && (p.gather.signal || p.gather.nwait > 0) && threadIdx.x == 0) {
     __threadfence();
     const unsigned prev = atomicAdd(p.gather.counters, 1u);
     if (prev == gridDim.x - 1) {

@@ -178,4 +178,41 @@ __global__ void __launch_bounds__(128, 1)
   }
 }
 
+// block_q5_K rows: one thread per 64-value chunk (sub-blocks 2cc, 2cc+1);
+// fp16_rn(fp32(d)*sc*q - fp32(dmin)*m) with q = nibble | (qh bit << 4), the
+// gguf-py 0.19.0 Q5_K dequant rounded once to fp16 (products exact in fp32).
+__global__ void dequant_q5k_kernel(const uint8_t* __restrict__ blocks, __half* __restrict__ out,
+                                   long long nchunks) {
+  for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < nchunks;
+       c += (long long)gridDim.x * blockDim.x) {
+    const long long sb = c >> 2;
+    const int cc = (int)(c & 3);
+    const uint8_t* blk = blocks + sb * kQ5KBlockBytes;
+    const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
+    const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+    const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
+    const uint32_t mw = cc < 2 ? m_lo : m_hi;
+    const int sh = 16 * (cc & 1);
+    const float d1a = d * (float)((scw >> sh) & 0xFFu);
+    const float m1a = dmin * (float)((mw >> sh) & 0xFFu);
+    const float d1b = d * (float)((scw >> (sh + 8)) & 0xFFu);
+    const float m1b = dmin * (float)((mw >> (sh + 8)) & 0xFFu);
+    const uint8_t* qh = blk + 16;
+    const uint8_t* qs = blk + 48 + cc * 32;
+    __half* o = out + sb * 256 + cc * 64;
+    for (int l = 0; l < 32; ++l) {
+      const uint32_t b = qs[l], h = qh[l];
+      const float qa = (float)((b & 0xFu) | (((h >> (2 * cc)) & 1u) << 4));
+      const float qb = (float)((b >> 4) | (((h >> (2 * cc + 1)) & 1u) << 4));
+      o[l] = __float2half_rn(fmaf(d1a, qa, -m1a));
+      o[32 + l] = __float2half_rn(fmaf(d1b, qb, -m1b));
+    }
+  }
+}
+
 }  // namespace busfill

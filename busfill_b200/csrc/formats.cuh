@@ -23,15 +23,27 @@
 namespace busfill {
 
 // Q4_0: the reference's split planes; Q4K: llama.cpp block_q4_K rows;
-// Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes).
-enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2 };
+// Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes);
+// Q5K: llama.cpp block_q5_K rows (176 bytes per 256 values).
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3 };
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
 constexpr int kUnitK = 256;          // K per unit
 constexpr int kChunkK = 64;          // K per activation box / 32 TMEM operand columns
 constexpr int kChunksPerUnit = kUnitK / kChunkK;
 constexpr int kQ4KBlockBytes = 144;
+constexpr int kQ5KBlockBytes = 176;
 constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
+
+// Formats stored as whole block rows (one TMA box per unit of 128 rows).
+template <WFmt F>
+constexpr bool aos_rows() { return F != WFmt::Q4_0; }
+// Bytes of one 256-value unit of a weight row as stored (Q4_0: its nibble plane).
+template <WFmt F>
+constexpr int unit_row_bytes() { return F == WFmt::Q5K ? kQ5KBlockBytes : F == WFmt::Q4_0 ? 128 : kQ4KBlockBytes; }
+// One unit of 128 weight rows in shared memory (Q4_0: nibbles, then 8 scales per row).
+template <WFmt F>
+constexpr int wstage_bytes() { return F == WFmt::Q4_0 ? kWStageBytes : kTileRows * unit_row_bytes<F>(); }
 constexpr int kQ40ScaleOffset = 16384;
 // ---------------------------------------------------------------------------
 // dequant helpers (one weight row per thread)
@@ -124,6 +136,37 @@ __device__ __forceinline__ void dequant_q4_0g_chunk(const uint32_t* w, uint32_t*
 // SwiGLU epilogues write fp16_rn(silu(gate) * up) of the fp32 accumulators
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// Q5_K, one 64-value chunk cc of a super-block: q0/q1 are the chunk's 32 qs
+// bytes (byte l: low nibble element l of sub-block 2cc, high nibble element l
+// of sub-block 2cc+1), h0/h1 the 32 qh bytes (bit G of byte l: the fifth bit
+// of element l of sub-block G). The fifth bit joins the magic bias: mantissa
+// bit 4 of 1024 + q (low nibbles) or bit 8 of 64 + q (high nibbles, mantissa
+// step 1/16) is worth 16, so both stay exact integers 0..31 above the bias.
+__device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1, int cc,
+                                                  const __half2 ds_lo, const __half2 ndm_lo, const __half2 ds_hi,
+                                                  const __half2 ndm_hi, uint32_t* out) {
+  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  const int bl = 2 * cc, bh = 2 * cc + 1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t t0 = prmt(w[i], w[i], 0x0100u);    // byte0 = b0, byte2 = b1
+    const uint32_t t1 = prmt(w[i], w[i], 0x0302u);    // byte0 = b2, byte2 = b3
+    const uint32_t u0 = prmt(hw[i], hw[i], 0x0100u);  // the same elements' qh bytes
+    const uint32_t u1 = prmt(hw[i], hw[i], 0x0302u);
+    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u | (((u0 >> bl) & 0x00010001u) << 4));
+    const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u | (((u1 >> bl) & 0x00010001u) << 4));
+    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u | (((u0 >> bh) & 0x00010001u) << 8));
+    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u | (((u1 >> bh) & 0x00010001u) << 8));
+    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
+    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
+    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
+    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
+  }
+}
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>
@@ -143,11 +186,12 @@ template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
 __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* q40_scales, int r,
                                                  uint32_t a_slot) {
   static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
-  if constexpr (FMT == WFmt::Q4K) {
+  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q5K) {
+    constexpr int kRow = unit_row_bytes<FMT>();
     // this row's block header: d, dmin and the 6-bit scales/mins of its
     // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
     // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7
-    const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kQ4KBlockBytes);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kRow);
     const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
     const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
     const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
@@ -165,15 +209,24 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
       const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
       const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
-      const uint8_t* qs = stage + r * kQ4KBlockBytes + 16 + cc * 32;
-      const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
       uint32_t P[32];
-      dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
+      if constexpr (FMT == WFmt::Q4K) {
+        const uint8_t* qs = stage + r * kRow + 16 + cc * 32;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
+        dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
+      } else {
+        const uint8_t* row = stage + r * kRow;  // qh at 16, qs at 48
+        const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
+        const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
+        dequant_q5k_chunk(q0, q1, h0, h1, cc, dsl, dml, dsh, dmh, P);
+      }
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     }
   } else if constexpr (FMT == WFmt::Q4_0G) {
-    const uint8_t* urow = stage + r * kQ4KBlockBytes;
+    const uint8_t* urow = stage + r * unit_row_bytes<FMT>();
     uint32_t P[32];
     auto chunk = [&](auto cc_tag) {
       constexpr int cc = decltype(cc_tag)::value;

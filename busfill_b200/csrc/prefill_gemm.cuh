@@ -58,9 +58,7 @@ namespace prefill {
 constexpr int kThreads = 512;
 constexpr int kBatchTile = 128;                 // batch rows per item = MMA N
 constexpr int kPairRows = 2 * kTileRows;        // weight rows per item
-constexpr int kWStages = 3;
 constexpr int kXStages = 3;                     // half units (2 chunks each)
-constexpr int kWStage = 2 * kWStageBytes;       // both tiles' unit (Q4_0: 32 KB nibbles, then 4 KB scales)
 constexpr int kQ40Scales = 2 * kQ40ScaleOffset; // Q4_0: scales of the 256 rows after the nibbles
 constexpr int kXChunk = kBatchTile * 128;       // 64 values x 128 rows, 16 KB
 constexpr int kXStage = 2 * kXChunk;            // one K half of a unit, 32 KB
@@ -70,21 +68,27 @@ constexpr int kSlot0 = 2 * kAccCols;
 constexpr int kTmemCols = 512;
 static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
 
-// shared memory map
-constexpr int kWOff = 0;
-constexpr int kXOff = kWOff + kWStages * kWStage;
-constexpr int kBarOff = kXOff + kXStages * kXStage;
-constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
-constexpr int bXFull = bWEmpty + kWStages, bXEmpty = bXFull + kXStages;
-constexpr int bReady = bXEmpty + kXStages;      // half slot s = 2t + h filled (4 dequant warps of tile t)
-constexpr int bSDone = bReady + 4;              // half slot s read by its MMAs (commit)
-constexpr int bAccFull = bSDone + 4, bAccEmpty = bAccFull + 1, bFinal = bAccEmpty + 1;
-constexpr int kNumBars = bFinal + 1;
-constexpr int kMiscOff = kBarOff + kNumBars * 8;
-constexpr int kBytes = kMiscOff + 64;
-constexpr int kAlloc = kBytes + 1024;
-static_assert(kXOff % 1024 == 0 && kXStage % 1024 == 0, "swizzled operands need 1 KB alignment");
-static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
+// shared memory map (the weight stage holds both tiles' unit: 256 rows; Q4_0:
+// 32 KB of nibbles, then 4 KB of scales)
+template <WFmt FMT>
+struct Smem {
+  static constexpr int kWStage = 2 * wstage_bytes<FMT>();
+  static constexpr int kWStages = FMT == WFmt::Q5K ? 2 : 3;   // Q5_K stages are 44 KB
+  static constexpr int kWOff = 0;
+  static constexpr int kXOff = kWOff + kWStages * kWStage;
+  static constexpr int kBarOff = kXOff + kXStages * kXStage;
+  static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
+  static constexpr int bXFull = bWEmpty + kWStages, bXEmpty = bXFull + kXStages;
+  static constexpr int bReady = bXEmpty + kXStages;   // half slot s = 2t + h filled (4 dequant warps of tile t)
+  static constexpr int bSDone = bReady + 4;           // half slot s read by its MMAs (commit)
+  static constexpr int bAccFull = bSDone + 4, bAccEmpty = bAccFull + 1, bFinal = bAccEmpty + 1;
+  static constexpr int kNumBars = bFinal + 1;
+  static constexpr int kMiscOff = kBarOff + kNumBars * 8;
+  static constexpr int kBytes = kMiscOff + 64;
+  static constexpr int kAlloc = kBytes + 1024;
+  static_assert(kXOff % 1024 == 0 && kXStage % 1024 == 0, "swizzled operands need 1 KB alignment");
+  static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
+};
 
 struct Params {
   void* c;            // [M, N] row-major, OutT
@@ -103,8 +107,15 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                         const __grid_constant__ CUtensorMap tmap_a, const prefill::Params p) {
   using namespace prefill;
+  using SM = Smem<FMT>;
+  constexpr int kWStage = SM::kWStage, kWStages = SM::kWStages, kWOff = SM::kWOff, kXOff = SM::kXOff;
+  constexpr int kBarOff = SM::kBarOff, kMiscOff = SM::kMiscOff, kNumBars = SM::kNumBars;
+  constexpr int bWFull = SM::bWFull, bWEmpty = SM::bWEmpty, bXFull = SM::bXFull, bXEmpty = SM::bXEmpty;
+  constexpr int bReady = SM::bReady, bSDone = SM::bSDone, bAccFull = SM::bAccFull, bAccEmpty = SM::bAccEmpty;
+  constexpr int bFinal = SM::bFinal;
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, kBatchTile);
-  constexpr bool kRows144 = (FMT != WFmt::Q4_0);
+  constexpr bool kRows144 = aos_rows<FMT>();
+  constexpr int kRowBytes = unit_row_bytes<FMT>();
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
@@ -150,11 +161,11 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     mbar_arrive_expect_tx(BAR(bWFull + s), kWStage);
     if constexpr (kRows144) {
       if (p.swiglu) {
-        tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kTileRows, BAR(bWFull + s), kPolicyEvictLast);
-        tma_load_2d(dst + kWStageBytes, &tmap_ws, k * kQ4KBlockBytes, pair * kTileRows, BAR(bWFull + s),
+        tma_load_2d(dst, &tmap_w, k * kRowBytes, pair * kTileRows, BAR(bWFull + s), kPolicyEvictLast);
+        tma_load_2d(dst + wstage_bytes<FMT>(), &tmap_ws, k * kRowBytes, pair * kTileRows, BAR(bWFull + s),
                     kPolicyEvictLast);
       } else {
-        tma_load_2d(dst, &tmap_w, k * kQ4KBlockBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+        tma_load_2d(dst, &tmap_w, k * kRowBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
       }
     } else {
       tma_load_2d(dst, &tmap_w, k * 128, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);

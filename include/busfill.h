@@ -152,6 +152,15 @@ BUSFILL_API int busfill_ipc_close(void* dev_ptr);
 BUSFILL_API int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,
                                        void* stream);
 
+/* Q5_K: llama.cpp block_q5_K rows, K/256 blocks of 176 bytes per weight row
+ * (fp16 d, fp16 dmin, the 12 scale/min bytes of Q4_K, 32 bytes qh holding
+ * each value's fifth bit, 128 nibble bytes); value = d*sc*q - dmin*m with q
+ * in 0..31.  a [M, K] fp16, c [M, N] fp16.  Requires K % 256 == 0; blocks and
+ * a 16-byte aligned.  No reference counterpart: one of the K-quant formats
+ * that Q4_K_M models mix in (the BASELINE "next" formats); same kernels and
+ * numerics as busfill_gemm_q4k (two fp16 roundings of the weight operand). */
+BUSFILL_API int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
+
 /* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
  * in the reference.
  *
@@ -205,6 +214,10 @@ BUSFILL_API int busfill_dequant_q4_0_ggml(const uint8_t* blocks, uint16_t* out, 
 /* fp16_rn(fp32(d)*sc*q - fp32(dmin)*m) per llama.cpp block_q4_K. K % 256 == 0.
  * No reference counterpart (the reference has no Q4_K code). */
 BUSFILL_API int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream);
+
+/* fp16_rn(fp32(d)*sc*q - fp32(dmin)*m) per llama.cpp block_q5_K. K % 256 == 0.
+ * No reference counterpart. */
+BUSFILL_API int busfill_dequant_q5k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Status, options, diagnostics

@@ -43,6 +43,7 @@ import numpy as np
 QK4_0 = 32          # values per Q4_0 block
 QK_K = 256          # values per Q4_K super-block
 Q4K_BLOCK_BYTES = 144
+Q5K_BLOCK_BYTES = 176
 Q4K_SCALE_BYTES = 12
 
 
@@ -229,6 +230,64 @@ def dequant_q4k(blocks: np.ndarray, k: int) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------
+# Q5_K (llama.cpp block_q5_K, 176 bytes per 256 values)
+# --------------------------------------------------------------------------
+def make_q5k_blocks(d16, dmin16, sc, m, q) -> np.ndarray:
+    """Assemble ``block_q5_K`` rows: fp16 d, fp16 dmin, the 12 scale/min
+    bytes of Q4_K, 32 bytes ``qh`` and 128 bytes ``qs``.
+
+    q: u8 [N, S*256] 5-bit values in element order. Element e of a
+    super-block (sub-block G = e // 32, l = e % 32) keeps its low 4 bits in
+    ``qs[32*(G//2) + l]`` (low nibble for even G, high nibble for odd G) and
+    its fifth bit as bit G of ``qh[l]`` (gguf-py 0.19.0 ``Q5_K``).
+    """
+    d16 = np.asarray(d16, dtype=np.float16)
+    n, s = d16.shape
+    q = np.asarray(q, dtype=np.uint8).reshape(n, s, 8, 32)
+    lo = q & 0x0F
+    qs = (lo[:, :, 0::2, :] | (lo[:, :, 1::2, :] << 4)).reshape(n, s, 128)
+    hi = (q >> 4) & 1                                     # [n, s, 8, 32]
+    qh = np.zeros((n, s, 32), dtype=np.uint8)
+    for g in range(8):
+        qh |= (hi[:, :, g, :] << g).astype(np.uint8)
+    hdr_d = d16.reshape(n, s, 1).view(np.uint8)
+    hdr_m = np.asarray(dmin16, dtype=np.float16).reshape(n, s, 1).view(np.uint8)
+    return np.concatenate([hdr_d, hdr_m, pack_q4k_scales(sc, m), qh, qs], axis=2).reshape(n, s * Q5K_BLOCK_BYTES)
+
+
+def split_q5k_blocks(blocks: np.ndarray, k: int):
+    """``block_q5_K`` rows -> (d16 [N,S], dmin16 [N,S], sc [N,S,8], m [N,S,8], q [N,K] in 0..31)."""
+    n = blocks.shape[0]
+    s = k // QK_K
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(n, s, Q5K_BLOCK_BYTES)
+    d16 = b[:, :, 0:2].copy().view(np.float16).reshape(n, s)
+    dmin16 = b[:, :, 2:4].copy().view(np.float16).reshape(n, s)
+    sc, m = unpack_q4k_scales(b[:, :, 4:16])
+    qh = b[:, :, 16:48]
+    qs = b[:, :, 48:176].reshape(n, s, 4, 1, 32)
+    lo = np.concatenate([qs & 0x0F, qs >> 4], axis=3).reshape(n, s, 8, 32)
+    hi = np.stack([(qh >> g) & 1 for g in range(8)], axis=2)   # [n, s, 8, 32]
+    q = (lo | (hi << 4)).reshape(n, s * QK_K)
+    return d16, dmin16, sc, m, q
+
+
+def dequant_q5k_f32(blocks: np.ndarray, k: int) -> np.ndarray:
+    """Q5_K dequant in fp32 (gguf-py 0.19.0 ``Q5_K.dequantize_blocks`` order):
+    ``fp32(d) * sc * q - fp32(dmin) * m``, one fp32 rounding (as Q4_K)."""
+    d16, dmin16, sc, m, q = split_q5k_blocks(blocks, k)
+    n, s = d16.shape
+    d1 = (d16.astype(np.float32)[:, :, None] * sc.astype(np.float32))
+    m1 = (dmin16.astype(np.float32)[:, :, None] * m.astype(np.float32))
+    qf = q.reshape(n, s, 8, 32).astype(np.float32)
+    return (d1[:, :, :, None] * qf - m1[:, :, :, None]).reshape(n, k).astype(np.float32)
+
+
+def dequant_q5k(blocks: np.ndarray, k: int) -> np.ndarray:
+    """Bit-exact Q5_K fp16 operand: ``fp16_rn(w32)``."""
+    return dequant_q5k_f32(blocks, k).astype(np.float16)
+
+
+# --------------------------------------------------------------------------
 # Seeded synthetic generators (BASELINE configs 0-4; no public dataset)
 # --------------------------------------------------------------------------
 def gen_activations(m: int, k: int, seed: int) -> np.ndarray:
@@ -263,6 +322,21 @@ def gen_q4k(n: int, k: int, seed: int):
     m = rng.integers(0, 64, size=(n, s, 8), dtype=np.uint8)
     q = rng.integers(0, 16, size=(n, k), dtype=np.uint8)
     return make_q4k_blocks(d16, dmin16, sc, m, q)
+
+
+def gen_q5k(n: int, k: int, seed: int):
+    """Q5_K weights with the config-2 scale distributions (d ~ U(0.001, 0.01),
+    dmin ~ U(0, 0.005), 6-bit scales and mins uniform) and 5-bit values
+    uniform [0, 31]. Returns ``block_q5_K`` rows u8 [N, K/256*176]."""
+    assert k % QK_K == 0
+    rng = np.random.default_rng(seed)
+    s = k // QK_K
+    d16 = rng.uniform(0.001, 0.01, size=(n, s)).astype(np.float16)
+    dmin16 = rng.uniform(0.0, 0.005, size=(n, s)).astype(np.float16)
+    sc = rng.integers(0, 64, size=(n, s, 8), dtype=np.uint8)
+    m = rng.integers(0, 64, size=(n, s, 8), dtype=np.uint8)
+    q = rng.integers(0, 32, size=(n, k), dtype=np.uint8)
+    return make_q5k_blocks(d16, dmin16, sc, m, q)
 
 
 # --------------------------------------------------------------------------

@@ -13,6 +13,8 @@ Fixtures written next to this script (small .npz files, committed):
 * ``q4k_gguf.npz`` -- gguf-py 0.19.0 ``Q4_K.dequantize_blocks`` (the published
   llama.cpp ``block_q4_K`` dequant in numpy) on seeded random blocks. The
   reference has no Q4_K code, so this third-party implementation is the anchor.
+* ``q5k_gguf.npz`` -- gguf-py 0.19.0 ``Q5_K.dequantize_blocks`` on seeded
+  random ``block_q5_K`` rows (a BASELINE "next" format; no reference code).
 * ``q4_0_gguf.npz`` -- gguf-py 0.19.0 ``Q4_0.dequantize_blocks`` on seeded
   random llama.cpp ``block_q4_0`` rows (the AoS Q4_0 layout).
 
@@ -103,6 +105,32 @@ def make_q4k_gguf():
     np.savez_compressed(os.path.join(HERE, "q4k_gguf.npz"), **out)
 
 
+def make_q5k_gguf():
+    from gguf import GGMLQuantizationType
+    from gguf.quants import dequantize
+
+    rng = np.random.default_rng(2025)
+    out = {}
+    # case a: config-2-like distributions; case b: every byte random
+    for name, n, k, wide in (("a", 16, 512, False), ("b", 24, 768, True)):
+        s = k // 256
+        if wide:
+            d = _random_f16(rng, (n, s), -10, 2, signed=False)
+            dmin = _random_f16(rng, (n, s), -12, 0, signed=True)
+        else:
+            d = rng.uniform(0.001, 0.01, size=(n, s)).astype(np.float16)
+            dmin = rng.uniform(0.0, 0.005, size=(n, s)).astype(np.float16)
+        rest = rng.integers(0, 256, size=(n, s, 12 + 32 + 128), dtype=np.uint8)
+        blocks = np.concatenate([d.reshape(n, s, 1).view(np.uint8), dmin.reshape(n, s, 1).view(np.uint8), rest],
+                                axis=2).reshape(n, s * 176)
+        w32 = dequantize(blocks, GGMLQuantizationType.Q5_K)
+        assert w32.shape == (n, k) and w32.dtype == np.float32
+        out[f"{name}_blocks"] = blocks
+        out[f"{name}_w32"] = w32
+        out[f"{name}_k"] = np.array(k)
+    np.savez_compressed(os.path.join(HERE, "q5k_gguf.npz"), **out)
+
+
 def make_q4_0_gguf():
     from gguf import GGMLQuantizationType
     from gguf.quants import dequantize
@@ -123,6 +151,7 @@ def main():
     args = ap.parse_args()
     make_q4_0_reference(args.reference)
     make_q4k_gguf()
+    make_q5k_gguf()
     make_q4_0_gguf()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):

@@ -47,6 +47,8 @@ def test_null_pointer_rejected_before_any_device_work():
     assert lib.busfill_gemm_q4_0(None, None, None, None, 8, 128, 256, None) == -1
     assert lib.busfill_gemm_q4_0_ggml(None, None, None, 8, 128, 256, None) == -1
     assert lib.busfill_gemm_q4k_swiglu(None, None, None, None, 8, 128, 256, None) == -1
+    assert lib.busfill_gemm_q5k(None, None, None, 8, 128, 256, None) == -1
+    assert lib.busfill_dequant_q5k(None, None, 4, 256, None) == -1
     assert lib.busfill_dequant_q4k(None, None, 4, 256, None) == -1
     assert lib.busfill_probe_umma(None, None, None, 16, None) == -1
 

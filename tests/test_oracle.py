@@ -4,6 +4,7 @@
   ``quantize_q4q`` (kernels/q4k_batched.py:65-79,100), fixture q4_0_reference.npz.
 * Q4_K dequant vs gguf-py 0.19.0 ``Q4_K.dequantize_blocks``, fixture q4k_gguf.npz.
 * llama.cpp AoS Q4_0 dequant vs gguf-py ``Q4_0.dequantize_blocks``, q4_0_gguf.npz.
+* Q5_K dequant vs gguf-py ``Q5_K.dequantize_blocks``, q5k_gguf.npz.
 * Exhaustive checks of the 6-bit scale/min packing.
 """
 import os
@@ -59,6 +60,27 @@ def test_dequant_q4k_matches_gguf(golden_dir, case):
     mine = orc.dequant_q4k_f32(blocks, k)
     assert np.array_equal(mine.view(np.uint32), w32.view(np.uint32))
     assert np.array_equal(orc.dequant_q4k(blocks, k).view(np.uint16), w32.astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_q5k_dequant_matches_gguf_golden(golden_dir, case):
+    """Q5_K dequant vs gguf-py 0.19.0 ``Q5_K.dequantize_blocks`` (q5k_gguf.npz)."""
+    g = _load(golden_dir, "q5k_gguf.npz")
+    blocks, w32, k = g[f"{case}_blocks"], g[f"{case}_w32"], int(g[f"{case}_k"])
+    assert np.array_equal(orc.dequant_q5k_f32(blocks, k).view(np.uint32), w32.view(np.uint32))
+    with np.errstate(over="ignore"):
+        want16 = w32.astype(np.float16)
+    assert np.array_equal(orc.dequant_q5k(blocks, k).view(np.uint16), want16.view(np.uint16))
+
+
+def test_q5k_block_split_make_roundtrip(golden_dir):
+    g = _load(golden_dir, "q5k_gguf.npz")
+    blocks, k = g["b_blocks"], int(g["b_k"])
+    assert np.array_equal(orc.make_q5k_blocks(*orc.split_q5k_blocks(blocks, k)), blocks)
+    # the generator's values come back out of the blocks
+    w = orc.gen_q5k(8, 512, seed=3)
+    d, dmin, sc, m, q = orc.split_q5k_blocks(w, 512)
+    assert q.max() <= 31 and q.min() >= 0 and sc.max() < 64 and m.max() < 64
 
 
 def test_q4k_block_split_make_roundtrip(golden_dir):
