@@ -75,7 +75,7 @@ def test_column_split_matches_oracle(fmt, n):
         assert max_abs <= orc.GATE_MAX_ABS and rel <= orc.GATE_REL_L2, (rank, max_abs, rel)
 
 
-def _worker_gather(rank, world, port, q):
+def _worker_gather(rank, world, port, q, m=8):
     """Two chained column-split GEMMs whose all-gathers run in the GEMM
     epilogues (peer stores + flags, no NCCL on the data path), and a fused
     SwiGLU site reading the first one's gathered output too; first eagerly,
@@ -98,7 +98,7 @@ def _worker_gather(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
     space = None
     try:
-        m, k0, n1, n2, n3 = 8, 2048, 1280, 768, 384
+        k0, n1, n2, n3 = 2048, 1280, 768, 384
         w1 = orc.gen_q4k(n1, k0, seed=21)
         w2 = orc.gen_q4k(n2, n1, seed=22)
         wg = orc.gen_q4k(n3, n1, seed=23)
@@ -167,14 +167,15 @@ def _worker_gather(rank, world, port, q):
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_gather_fused_into_epilogue():
+@pytest.mark.parametrize("m", [8, 40])  # 40 rows: two launches per call (the first waits, the last signals)
+def test_gather_fused_into_epilogue(m):
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 4)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker_gather, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker_gather, args=(r, world, port, q, m)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(world)]
