@@ -153,6 +153,26 @@ def make_q4k_weights(torch, n, k, gen, dev):
     return blocks.view(n, s * 144).contiguous()
 
 
+def make_q5k_weights(torch, n, k, gen, dev):
+    """block_q5_K rows [N, K/256*176] with config-2-like d / dmin; other bytes random."""
+    s = k // 256
+    blocks = torch.randint(0, 256, (n, s, 176), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, s), device=dev, generator=gen) * 0.009 + 0.001).half()
+    dmin = (torch.rand((n, s), device=dev, generator=gen) * 0.005).half()
+    blocks[:, :, 0:2] = d.view(torch.uint8).view(n, s, 2)
+    blocks[:, :, 2:4] = dmin.view(torch.uint8).view(n, s, 2)
+    return blocks.view(n, s * 176).contiguous()
+
+
+def make_q4_0_ggml_weights(torch, n, k, gen, dev):
+    """llama.cpp block_q4_0 rows [N, K/32*18] with config-0 scales (U(0.001, 0.02))."""
+    nb = k // 32
+    blocks = torch.randint(0, 256, (n, nb, 18), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, nb), device=dev, generator=gen) * 0.019 + 0.001).half()
+    blocks[:, :, 0:2] = d.view(torch.uint8).view(n, nb, 2)
+    return blocks.view(n, nb * 18).contiguous()
+
+
 def make_q4_0_weights(torch, n, k, gen, dev):
     wq = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=gen)
     ws = (torch.rand((n, k // 32), device=dev, generator=gen) * 0.019 + 0.001).half()
@@ -374,14 +394,24 @@ def isolated_no_pdl(bf, capture, time_graph, steps, R, M):
 def sweep(torch, bf, dev, l2, hbm_peak, args):
     rows = []
     cases = [("q4k", 1, 5120, 5120), ("q4k", 8, 5120, 5120), ("q4k", 32, 5120, 5120), ("q4k", 32, 17408, 5120),
-             ("q4_0", 1, 5120, 5120), ("q4_0", 8, 5120, 5120), ("q4_0", 32, 5120, 5120)]
+             ("q4_0", 1, 5120, 5120), ("q4_0", 8, 5120, 5120), ("q4_0", 32, 5120, 5120),
+             ("q4_0_ggml", 32, 5120, 5120), ("q5k", 32, 5120, 5120), ("q4k_swiglu", 32, 17408, 5120)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 99)
     for fmt, m, n, k in cases:
-        wbytes = n * k * 18 // 32
+        wbytes = n * k * (22 if fmt == "q5k" else 18) // 32 * (2 if fmt == "q4k_swiglu" else 1)
         R = max(2, math.ceil(2.2 * l2 / wbytes))
         if fmt == "q4k":
             w0 = make_q4k_weights(torch, n, k, gen, dev)
+            ws = [w0] + [w0.clone() for _ in range(R - 1)]
+        elif fmt == "q4k_swiglu":
+            g0, u0 = make_q4k_weights(torch, n, k, gen, dev), make_q4k_weights(torch, n, k, gen, dev)
+            ws = [(g0, u0)] + [(g0.clone(), u0.clone()) for _ in range(R - 1)]
+        elif fmt == "q5k":
+            w0 = make_q5k_weights(torch, n, k, gen, dev)
+            ws = [w0] + [w0.clone() for _ in range(R - 1)]
+        elif fmt == "q4_0_ggml":
+            w0 = make_q4_0_ggml_weights(torch, n, k, gen, dev)
             ws = [w0] + [w0.clone() for _ in range(R - 1)]
         else:
             q, s = make_q4_0_weights(torch, n, k, gen, dev)
@@ -394,6 +424,12 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
             for w in ws:
                 if fmt == "q4k":
                     bf.gemm_q4k(w, a, out=c, stream=st)
+                elif fmt == "q4k_swiglu":
+                    bf.gemm_q4k_swiglu(w[0], w[1], a, out=c, stream=st)
+                elif fmt == "q5k":
+                    bf.gemm_q5k(w, a, out=c, stream=st)
+                elif fmt == "q4_0_ggml":
+                    bf.gemm_q4_0_ggml(w, a, out=c, stream=st)
                 else:
                     bf.gemm_q4_0(w[0], w[1], a, out=c, stream=st)
 
@@ -409,7 +445,7 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         ms = _time_on(torch, g, st)
         assert bf.stream_status(st) == 0
         us = ms * 1e3 / (nsteps * R)
-        gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
+        gbs = (wbytes + 2 * m * k + 2 * m * n) / (us * 1e-6) / 1e9
         rows.append({"format": fmt, "M": m, "N": n, "K": k, "us_per_gemm": round(us, 3),
                      "tokens_per_s": round(m / (us * 1e-6), 1), "GB_s": round(gbs, 1),
                      "hbm_frac": round(gbs / hbm_peak, 4)})
