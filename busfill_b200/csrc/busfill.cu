@@ -355,12 +355,12 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
         p.gather.out[q] = reinterpret_cast<OutT*>(gather->out[q]) + (size_t)m0 * gather->ldc;
         p.gather.flag[q] = gather->flag[q];
       }
-      p.gather.counters = gather->counters;
       p.gather.signal = (m0 + 32 >= M) ? 1 : 0;
       if (m0 == 0 && gather->wait && gather->nwait > 0) {
         p.gather.wait = gather->wait;
         p.gather.wait_gen = gather->wait_gen;
         p.gather.nwait = gather->nwait;
+        for (int r = 0; r < gather->nwait; ++r) p.gather.wait_tiles[r] = gather->wait_tiles[r];
       }
     }
     p.c = reinterpret_cast<OutT*>(c) + (size_t)m0 * N;
@@ -469,9 +469,10 @@ int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws
 template <WFmt FMT>
 int gemm_gather_impl(const uint8_t* w, const uint8_t* w_up, bool swiglu, const uint16_t* a, int M, int N, int K,
                      const busfill_gather* g, cudaStream_t s) {
-  if (!g || !g->counters || (swiglu && !w_up)) return BUSFILL_ERR_INVALID_ARG;
+  if (!g || (swiglu && !w_up)) return BUSFILL_ERR_INVALID_ARG;
   if (g->npeers < 1 || g->npeers > kMaxPeers || g->col_off < 0 || g->ldc < g->col_off + N) return BUSFILL_ERR_SHAPE;
-  if (g->nwait < 0 || g->nwait > 32 || (g->nwait > 0 && (!g->wait || !g->wait_gen))) return BUSFILL_ERR_INVALID_ARG;
+  if (g->nwait < 0 || g->nwait > kMaxPeers || (g->nwait > 0 && (!g->wait || !g->wait_gen)))
+    return BUSFILL_ERR_INVALID_ARG;
   for (int q = 0; q < g->npeers; ++q)
     if (!g->out[q] || !g->flag[q]) return BUSFILL_ERR_INVALID_ARG;
   int st = check_gemm_args<FMT>(w, nullptr, a, g->out[0], M, N, K);
@@ -518,16 +519,19 @@ int grid_for(long long work, int sm_count) {
 // ---------------------------------------------------------------------------
 // waiting for a gathered output outside a GEMM
 // ---------------------------------------------------------------------------
+struct WaitTiles {
+  int n[kMaxPeers];
+};
 __global__ void __launch_bounds__(32, 1) gather_wait_kernel(const unsigned* wait, unsigned* wait_gen, int nwait,
-                                                            unsigned* error) {
-  const unsigned target = *wait_gen + 1u;
+                                                            WaitTiles tiles, unsigned* error) {
+  const unsigned calls = *reinterpret_cast<volatile unsigned*>(wait_gen);  // one CTA: one per call
   bool got = true;
-  for (int i = threadIdx.x; i < nwait; i += 32) got = got && wait_flag_sys(wait + i, target);
+  if ((int)threadIdx.x < nwait) got = wait_flag_sys(wait + threadIdx.x, (calls + 1u) * (unsigned)tiles.n[threadIdx.x]);
   got = __all_sync(0xffffffffu, got);
   __syncwarp();
   if (threadIdx.x == 0) {
     if (!got) atomicOr(error, kErrActProducer);
-    *wait_gen = target;
+    *wait_gen = calls + 1u;
   }
 }
 
@@ -649,7 +653,7 @@ int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint8_t* w_up, c
 }
 
 int busfill_gather_wait(const busfill_gather* g, void* stream) {
-  if (!g || !g->wait || !g->wait_gen || g->nwait < 1 || g->nwait > 32) return BUSFILL_ERR_INVALID_ARG;
+  if (!g || !g->wait || !g->wait_gen || g->nwait < 1 || g->nwait > kMaxPeers) return BUSFILL_ERR_INVALID_ARG;
   DeviceInfo di;
   int dev = 0;
   int st = current_device(&di, &dev);
@@ -661,7 +665,9 @@ int busfill_gather_wait(const busfill_gather* g, void* stream) {
     st = get_error_words(dev, s, &err);
   }
   if (st != BUSFILL_OK) return st;
-  gather_wait_kernel<<<1, 32, 0, s>>>(g->wait, g->wait_gen, g->nwait, err);
+  WaitTiles tiles{};
+  for (int r = 0; r < g->nwait; ++r) tiles.n[r] = g->wait_tiles[r];
+  gather_wait_kernel<<<1, 32, 0, s>>>(g->wait, g->wait_gen, g->nwait, tiles, err);
   if (cudaGetLastError() != cudaSuccess) return BUSFILL_ERR_LAUNCH;
   return BUSFILL_OK;
 }

@@ -87,21 +87,24 @@ constexpr unsigned kErrTeardown = 32u;
 
 // Column split over a process group, with the all-gather in the epilogue:
 // every rank writes its slice of the output straight into each rank's full
-// output (peer memory over NVLink), and when the whole grid's slice has
-// landed the last CTA sets this rank's flag word in every rank's memory. A
-// later GEMM that reads the gathered output waits on those words first.
+// output (peer memory over NVLink). Each CTA that wrote tiles then adds their
+// number to this rank's counter word in every rank's memory with one
+// system-scope release reduction (no returning atomic, no last-CTA chain: on
+// B200 that chain cost ~4 us per call). A later GEMM that reads the gathered
+// output waits until each source rank's word reaches (calls so far + 1) x that
+// rank's tiles per call.
 constexpr int kMaxPeers = 8;
 struct GatherArgs {
   int npeers;                 // ranks receiving the output (this one included); 0 = local C only
   int col_off;                // first column of this rank's slice in the full rows
   int ldc;                    // row length of the full outputs
-  int signal;                 // this launch raises the flags (the last launch of a call)
+  int signal;                 // this launch counts its tiles (the last launch of a call)
   void* out[kMaxPeers];       // each rank's full output [rows, ldc], at this launch's first row
-  unsigned* flag[kMaxPeers];  // per rank: the word this rank sets in that rank's memory
-  unsigned* counters;         // this rank's [CTA count (zero between calls), signal generation]
-  const unsigned* wait;       // nwait local words to wait on (acquire) before reading A; may be null
-  unsigned* wait_gen;         // waits done so far on them: wait for *wait_gen + 1, then advance it
+  unsigned* flag[kMaxPeers];  // per rank: this rank's tile counter in that rank's memory
+  const unsigned* wait;       // nwait local counter words (one per source rank); may be null
+  unsigned* wait_gen;         // each waiting CTA adds 1 after its wait: value / grid = calls so far
   int nwait;
+  int wait_tiles[kMaxPeers];  // tiles each source rank writes per call
 };
 
 struct DecodeParams {
@@ -331,14 +334,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (GA && p.gather.nwait > 0) {
       // activations gathered by an earlier GEMM on every rank: wait for each
       // rank's flag, then let this thread's TMA copies see what it acquired
-      const unsigned target = *p.gather.wait_gen + 1u;  // advanced by the previous call's last CTA
+      // calls completed so far: every earlier call's CTAs each added 1; this
+      // call's CTAs that already got through add less than one grid's worth
+      const unsigned calls = *reinterpret_cast<volatile unsigned*>(p.gather.wait_gen) / gridDim.x;
       bool got = true;
-      if (lane < p.gather.nwait) got = wait_flag_sys(p.gather.wait + lane, target);
+      if (lane < p.gather.nwait)
+        got = wait_flag_sys(p.gather.wait + lane, (calls + 1u) * (unsigned)p.gather.wait_tiles[lane]);
       if (!__all_sync(0xffffffffu, got) && lane == 0) {
         atomicOr(p.error, kErrActProducer);
         atomicCAS(p.error + 1, 0u, 0x80000000u | ((unsigned)warp << 24) | 0xFFFu << 12);
       }
       fence_proxy_async_global();
+      if (lane == 0) atomicAdd(p.gather.wait_gen, 1u);
     }
     if (lane < x_early) issue_x_thread(lane);
     __syncwarp();
@@ -606,27 +613,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   // no CTA may leave while another CTA of its cluster can still read its
   // shared memory or arrive on its barriers
   if (csize > 1) cluster_wait();
-  // Gathered output: the last CTA to finish raises this rank's flag in every
-  // rank's memory to the call site's next generation, and advances this
-  // consumer's wait count. Ordering: each CTA's peer stores precede its
-  // thread 0 (the CTA barrier above), thread 0 releases them at GPU scope
-  // with its counter increment, the last CTA acquires that and releases
-  // everything at system scope with the flag stores, which the consumers
-  // acquire (the pattern of a data-then-flag protocol over NVLink).
-  if (GA && (p.gather.signal || p.gather.nwait > 0) && threadIdx.x == 0) {
-    __threadfence();
-    const unsigned prev = atomicAdd(p.gather.counters, 1u);
-    if (prev == gridDim.x - 1) {
-      __threadfence();
-      p.gather.counters[0] = 0u;  // ready for the next launch
-      if (p.gather.nwait > 0) *p.gather.wait_gen += 1u;
-      if (p.gather.signal) {
-        const unsigned gen = p.gather.counters[1] + 1u;
-        p.gather.counters[1] = gen;
-        __threadfence_system();
-        for (int q = 0; q < p.gather.npeers; ++q) st_release_sys(p.gather.flag[q], gen);
-      }
-    }
+  // Gathered output: a CTA that wrote tiles (rank 0 of its cluster) adds
+  // their number to this rank's counter in every rank's memory. The CTA
+  // barrier above orders the epilogue warps' peer stores before thread 0, and
+  // the reduction's system-scope release makes them visible to a consumer
+  // that acquires the counter (a data-then-flag protocol over NVLink).
+  if (GA && p.gather.signal && crank == 0 && threadIdx.x == 0) {
+    const unsigned tiles = (unsigned)(ntiles >> kSw);
+    for (int q = 0; q < p.gather.npeers; ++q) red_release_sys_add(p.gather.flag[q], tiles);
   }
 }
 

@@ -180,6 +180,11 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 __device__ __forceinline__ void st_release_sys(unsigned* addr, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
+// add to a (possibly peer) word without a result, releasing this thread's
+// prior writes (and those ordered before them) at system scope
+__device__ __forceinline__ void red_release_sys_add(unsigned* addr, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
   unsigned v;
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");

@@ -126,8 +126,9 @@ def _empty_slice(a):
 class Gather(ctypes.Structure):
     """ctypes mirror of busfill_gather (include/busfill.h)."""
     _fields_ = [("npeers", ctypes.c_int), ("col_off", ctypes.c_int), ("ldc", ctypes.c_int),
-                ("out", ctypes.c_void_p * 8), ("flag", ctypes.c_void_p * 8), ("counters", ctypes.c_void_p),
-                ("wait", ctypes.c_void_p), ("wait_gen", ctypes.c_void_p), ("nwait", ctypes.c_int)]
+                ("out", ctypes.c_void_p * 8), ("flag", ctypes.c_void_p * 8),
+                ("wait", ctypes.c_void_p), ("wait_gen", ctypes.c_void_p), ("nwait", ctypes.c_int),
+                ("wait_tiles", ctypes.c_int * 8)]
 
 
 class _DevArray:
@@ -143,9 +144,9 @@ class GatherSpace:
     sites, in one device allocation per rank that every rank maps (CUDA IPC).
 
     Site i owns, in every rank's allocation, a full output [rows_i, cols_i]
-    fp16, one flag word per source rank (rank r writes word r) and two counter
-    words; plus, for its own wait on an earlier site's flags, one wait-count
-    word. A site's output is written by every rank's GEMM for that site and
+    fp16, one tile-counter word per source rank (rank r adds to word r), and
+    two local words that count this site's waits (as a GEMM consumer and
+    through `wait`). A site's output is written by every rank's GEMM for that site and
     read by later sites; a separate buffer per call site keeps a rank from
     overwriting data another rank has not read yet.
     """
@@ -216,13 +217,19 @@ class GatherSpace:
         for q in range(self.world):
             g.out[q] = self.bases[q] + o_out
             g.flag[q] = self.bases[q] + o_flag + 4 * self.rank
-        g.counters = self._base + o_cnt
         if wait_site is not None:
             g.wait = self._base + self._off[wait_site][1]
-            g.wait_gen = self._base + o_cnt + 8      # this site's count of waits on wait_site's flags
+            g.wait_gen = self._base + o_cnt          # this site's count of waits on wait_site's counters
             g.nwait = self.world
+            for r in range(self.world):
+                g.wait_tiles[r] = self._tiles(wait_site, r)
         self._structs[key] = g
         return g
+
+    def _tiles(self, site, r):
+        """128-row output tiles rank r writes per call of `site`."""
+        s0, s1 = shard_rows(self.sites[site][1], self.world, r)
+        return (s1 - s0 + TILE_ROWS - 1) // TILE_ROWS
 
     def wait(self, site, stream=None):
         """Make `stream` wait (on the device) until `site`'s gathered output is
@@ -233,8 +240,10 @@ class GatherSpace:
         if g is None:
             g = Gather()
             g.wait = self._base + self._off[site][1]
-            g.wait_gen = self._base + self._off[site][2] + 12   # this site's standalone wait count
+            g.wait_gen = self._base + self._off[site][2] + 4    # this site's standalone wait count
             g.nwait = self.world
+            for r in range(self.world):
+                g.wait_tiles[r] = self._tiles(site, r)
             self._structs[key] = g
         _check(_lib().busfill_gather_wait(ctypes.byref(g), _stream(stream)), "busfill_gather_wait")
 

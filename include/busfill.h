@@ -88,18 +88,18 @@ BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_
  * rows [col_off, col_off + N) of a weight whose full output has `ldc`
  * columns. Each rank's GEMM writes its [M, N] slice straight into every
  * rank's full output buffer (out[q] is rank q's [M, ldc] buffer, mapped into
- * this process, e.g. with busfill_ipc_open), over NVLink, and once the whole
- * slice has landed it sets flag[q] (a word in rank q's memory that only this
- * rank writes) to the call site's next generation. A later GEMM whose
- * activations are that gathered output passes the nwait local words it must
- * wait on (`wait`, one per source rank) and `wait_gen`, a local word counting
- * how often this consumer has waited on them; its kernel waits (acquire,
- * bounded by 1 s, else BUSFILL_ERR_DEVICE_TIMEOUT) until every word reaches
- * *wait_gen + 1, then advances *wait_gen. Generations live in device memory,
- * so the calls can be captured in a CUDA graph and replayed. No NCCL call, no
- * host round trip. `counters` is two zeroed device words of this rank per
- * call site (a CTA count the kernel leaves at zero, and the generation).
- * Every rank must make the same calls in the same order. The reference is
+ * this process, e.g. with busfill_ipc_open), over NVLink, and adds the number
+ * of 128-row output tiles it wrote to flag[q] (a zeroed word in rank q's
+ * memory that only this rank adds to; a running total over the call site's
+ * calls). A later GEMM whose activations are that gathered output passes the
+ * nwait local words it must wait on (`wait`, one per source rank), the tiles
+ * each source rank writes per call (`wait_tiles`) and `wait_gen`, a zeroed
+ * local word for its own call site; its kernel waits (acquire, bounded by
+ * 1 s, else BUSFILL_ERR_DEVICE_TIMEOUT) until word r reaches (calls so far +
+ * 1) x wait_tiles[r], counting its calls in *wait_gen. All state lives in
+ * device memory, so the calls can be captured in a CUDA graph and replayed.
+ * No NCCL call, no host round trip. Every rank must make the same calls in
+ * the same order. The reference is
  * single-GPU (no counterpart); this is BASELINE's N-split with its
  * all-gather moved into the GEMM.
  * ------------------------------------------------------------------------- */
@@ -109,11 +109,11 @@ typedef struct busfill_gather {
   int col_off;                       /* first column of this rank's slice */
   int ldc;                           /* columns of the full outputs */
   uint16_t* out[BUSFILL_MAX_PEERS];  /* each rank's full output [M, ldc] fp16 (device pointers) */
-  uint32_t* flag[BUSFILL_MAX_PEERS]; /* per rank q: the word this rank sets in rank q's memory */
-  uint32_t* counters;                /* this rank's 2 zeroed words for this call site */
-  const uint32_t* wait;              /* optional: nwait local flag words to wait on before reading a */
-  uint32_t* wait_gen;                /* with wait: local word, waits done so far on those flags */
-  int nwait;
+  uint32_t* flag[BUSFILL_MAX_PEERS]; /* per rank q: this rank's tile counter in rank q's memory */
+  const uint32_t* wait;              /* optional: nwait local counter words to wait on before reading a */
+  uint32_t* wait_gen;                /* with wait: zeroed local word of this call site */
+  int nwait;                         /* source ranks waited on, <= 8 */
+  int wait_tiles[BUSFILL_MAX_PEERS]; /* with wait: 128-row tiles source rank r writes per call */
 } busfill_gather;
 
 /* busfill_gemm_q4k on this rank's weight rows [N, K/256 x 144 B], output

@@ -30,7 +30,7 @@ def test_wait_that_runs_out_reports_timeout_and_context_survives():
     a_np = orc.gen_activations(m, k, seed=6)
     a = torch.from_numpy(a_np).to(DEV)
     out = torch.zeros((m, n), dtype=torch.float16, device=DEV)
-    words = torch.zeros(16, dtype=torch.int32, device=DEV)   # flag, counters, the never-set wait word, wait count
+    words = torch.zeros(16, dtype=torch.int32, device=DEV)   # tile counter, the never-raised wait word, wait count
     base = words.data_ptr()
     g = tp.Gather()
     g.npeers = 1
@@ -38,10 +38,10 @@ def test_wait_that_runs_out_reports_timeout_and_context_survives():
     g.ldc = n
     g.out[0] = out.data_ptr()
     g.flag[0] = base
-    g.counters = base + 16
-    g.wait = base + 32          # stays 0: the wait for generation 1 never completes
+    g.wait = base + 32          # stays 0: the wait for 2 tiles never completes
     g.wait_gen = base + 48
     g.nwait = 1
+    g.wait_tiles[0] = n // 128
     lib = bf.load_library()
     st = lib.busfill_gemm_q4k_gather(ctypes.c_void_p(blocks.data_ptr()), ctypes.c_void_p(a.data_ptr()), m, n, k,
                                      ctypes.byref(g), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
