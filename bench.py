@@ -164,6 +164,16 @@ def make_q5k_weights(torch, n, k, gen, dev):
     return blocks.view(n, s * 176).contiguous()
 
 
+def make_q6k_weights(torch, bf, n, k, gen, dev):
+    """Q6_K in the GEMM's layout (busfill_repack_q6k of random block_q6_K rows):
+    body [N, K/256*208] random bytes, d [K/256, N] ~ U(0.0001, 0.0005)."""
+    s = k // 256
+    blocks = torch.randint(0, 256, (n, s, 210), dtype=torch.uint8, device=dev, generator=gen)
+    d = (torch.rand((n, s), device=dev, generator=gen) * 0.0004 + 0.0001).half()
+    blocks[:, :, 208:210] = d.view(torch.uint8).view(n, s, 2)
+    return bf.repack_q6k(blocks.view(n, s * 210).contiguous(), k)
+
+
 def make_q4_0_ggml_weights(torch, n, k, gen, dev):
     """llama.cpp block_q4_0 rows [N, K/32*18] with config-0 scales (U(0.001, 0.02))."""
     nb = k // 32
@@ -395,11 +405,13 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
     rows = []
     cases = [("q4k", 1, 5120, 5120), ("q4k", 8, 5120, 5120), ("q4k", 32, 5120, 5120), ("q4k", 32, 17408, 5120),
              ("q4_0", 1, 5120, 5120), ("q4_0", 8, 5120, 5120), ("q4_0", 32, 5120, 5120),
-             ("q4_0_ggml", 32, 5120, 5120), ("q5k", 32, 5120, 5120), ("q4k_swiglu", 32, 17408, 5120)]
+             ("q4_0_ggml", 32, 5120, 5120), ("q5k", 32, 5120, 5120), ("q6k", 32, 5120, 5120),
+             ("q4k_swiglu", 32, 17408, 5120)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 99)
     for fmt, m, n, k in cases:
-        wbytes = n * k * (22 if fmt == "q5k" else 18) // 32 * (2 if fmt == "q4k_swiglu" else 1)
+        wbytes = n * k * {"q5k": 22, "q6k": 26.25}.get(fmt, 18) // 32 * (2 if fmt == "q4k_swiglu" else 1)
+        wbytes = int(wbytes)
         R = max(2, math.ceil(2.2 * l2 / wbytes))
         if fmt == "q4k":
             w0 = make_q4k_weights(torch, n, k, gen, dev)
@@ -410,6 +422,9 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         elif fmt == "q5k":
             w0 = make_q5k_weights(torch, n, k, gen, dev)
             ws = [w0] + [w0.clone() for _ in range(R - 1)]
+        elif fmt == "q6k":
+            b0, d0 = make_q6k_weights(torch, bf, n, k, gen, dev)
+            ws = [(b0, d0)] + [(b0.clone(), d0.clone()) for _ in range(R - 1)]
         elif fmt == "q4_0_ggml":
             w0 = make_q4_0_ggml_weights(torch, n, k, gen, dev)
             ws = [w0] + [w0.clone() for _ in range(R - 1)]
@@ -428,6 +443,8 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
                     bf.gemm_q4k_swiglu(w[0], w[1], a, out=c, stream=st)
                 elif fmt == "q5k":
                     bf.gemm_q5k(w, a, out=c, stream=st)
+                elif fmt == "q6k":
+                    bf.gemm_q6k(w[0], w[1], a, out=c, stream=st)
                 elif fmt == "q4_0_ggml":
                     bf.gemm_q4_0_ggml(w, a, out=c, stream=st)
                 else:

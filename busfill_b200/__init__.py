@@ -19,7 +19,8 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q5k", "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q5k", "gemm_q6k", "repack_q6k",
+    "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
     "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "uses_prefill", "probe_umma", "version",
 ]
 
@@ -64,6 +65,9 @@ _SIGS = {
     "busfill_gemm_q4k_swiglu": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q5k": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q5k": [_P, _P, _I, _I, _P],
+    "busfill_gemm_q6k": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_repack_q6k": [_P, _P, _P, _I, _I, _P],
+    "busfill_dequant_q6k": [_P, _P, _P, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
@@ -319,6 +323,47 @@ def dequant_q5k(blocks, k, out=None, stream=None):
     if out is None:
         out = torch.empty((n, k), dtype=torch.float16, device=blocks.device)
     _check(_lib().busfill_dequant_q5k(_ptr(blocks), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q5k")
+    return out
+
+
+def repack_q6k(blocks, k, stream=None):
+    """llama.cpp block_q6_K rows u8 [N, K/256*210] -> (body u8 [N, K/256*208],
+    d fp16 [K/256, N]), the layout of gemm_q6k (busfill_repack_q6k)."""
+    torch = _torch()
+    _need(blocks, torch.uint8, "blocks")
+    n = blocks.shape[0]
+    if k % 256 or blocks.shape[1] != k // 256 * 210:
+        raise ValueError(f"shape mismatch: blocks {tuple(blocks.shape)}, k {k}")
+    body = torch.empty((n, k // 256 * 208), dtype=torch.uint8, device=blocks.device)
+    d = torch.empty((k // 256, n), dtype=torch.float16, device=blocks.device)
+    _check(_lib().busfill_repack_q6k(_ptr(blocks), _ptr(body), _ptr(d), n, k, _stream(stream)), "busfill_repack_q6k")
+    return body, d
+
+
+def gemm_q6k(body, d, a, out=None, stream=None):
+    """C[M, N] = A[M, K] @ deq(W)[N, K]^T for Q6_K weights in the repacked
+    layout (repack_q6k); fp16 out."""
+    torch = _torch()
+    _need(body, torch.uint8, "body"); _need(d, torch.float16, "d"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = body.shape[0]
+    if k % 256 or body.shape[1] != k // 256 * 208 or d.shape != (k // 256, n):
+        raise ValueError(f"shape mismatch: body {tuple(body.shape)}, d {tuple(d.shape)}, a {tuple(a.shape)}")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q6k(_ptr(body), _ptr(d), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
+           "busfill_gemm_q6k")
+    return out
+
+
+def dequant_q6k(body, d, k, out=None, stream=None):
+    torch = _torch()
+    _need(body, torch.uint8, "body"); _need(d, torch.float16, "d")
+    n = body.shape[0]
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.float16, device=body.device)
+    _check(_lib().busfill_dequant_q6k(_ptr(body), _ptr(d), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q6k")
     return out
 
 

@@ -293,8 +293,9 @@ int launch_decode_nb(const DeviceInfo& di, const CUtensorMap& tw, const CUtensor
 // Checks shared by every GEMM entry point.
 template <WFmt FMT>
 int check_gemm_args(const uint8_t* w, const uint16_t* ws, const uint16_t* a, const void* c, int M, int N, int K) {
-  if (!w || !a || !c || (FMT == WFmt::Q4_0 && !ws)) return BUSFILL_ERR_INVALID_ARG;
+  if (!w || !a || !c || ((FMT == WFmt::Q4_0 || FMT == WFmt::Q6K) && !ws)) return BUSFILL_ERR_INVALID_ARG;
   if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  if (FMT == WFmt::Q6K && N % 8 != 0) return BUSFILL_ERR_SHAPE;  // the d plane's rows: 16-byte multiples
   if (!aligned16(w) || !aligned16(a) || (ws && !aligned16(ws))) return BUSFILL_ERR_ALIGNMENT;
   return BUSFILL_OK;
 }
@@ -324,6 +325,10 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
     tws = tw;  // the up projection's map with SwiGLU, else unused
     if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, ub,
                                 kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    // Q6_K: the d plane [S][N], one box of a tile's 128 d per unit
+    if (FMT == WFmt::Q6K && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)N, (uint64_t)S,
+                                          (uint64_t)N * 2, kTileRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   } else {
     if (swiglu) return BUSFILL_ERR_INVALID_ARG;
@@ -414,6 +419,9 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
     tws = tw;
     if (swiglu && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT8, w_up, row, (uint64_t)N, row, ub,
                                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    if (FMT == WFmt::Q6K && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)N, (uint64_t)S,
+                                          (uint64_t)N * 2, prefill::kPairRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   } else {
     if (swiglu) return BUSFILL_ERR_INVALID_ARG;
@@ -642,6 +650,25 @@ int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int 
   return gemm_impl<WFmt::Q5K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
 
+int busfill_gemm_q6k(const uint8_t* body, const uint16_t* d, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                     void* stream) {
+  return gemm_impl<WFmt::Q6K, __half>(body, d, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_t* d, int N, int K, void* stream) {
+  if (!blocks || !body || !d) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 256 || K % 256 != 0) return BUSFILL_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(blocks) & 1u) || !aligned16(body) || !aligned16(d)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long words = (long long)N * (K / 256) * (kQ6KBodyBytes / 2 + 1);
+  repack_q6k_kernel<<<grid_for(words, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<const uint16_t*>(blocks), reinterpret_cast<uint16_t*>(body), d, N, K / 256);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
 int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int N, int K, const busfill_gather* g,
                             void* stream) {
   return gemm_gather_impl<WFmt::Q4K>(blocks, nullptr, false, a, M, N, K, g, reinterpret_cast<cudaStream_t>(stream));
@@ -789,6 +816,20 @@ int busfill_dequant_q5k(const uint8_t* blocks, uint16_t* out, int N, int K, void
   const long long nc = (long long)N * (K / 256) * 4;
   dequant_q5k_kernel<<<grid_for(nc, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       blocks, reinterpret_cast<__half*>(out), nc);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_dequant_q6k(const uint8_t* body, const uint16_t* d, uint16_t* out, int N, int K, void* stream) {
+  if (!body || !d || !out) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < 256 || K % 256 != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(body) || !aligned16(d) || !aligned16(out)) return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nc = (long long)N * (K / 256) * 4;
+  dequant_q6k_kernel<<<grid_for(nc, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      body, reinterpret_cast<const __half*>(d), reinterpret_cast<__half*>(out), N, K / 256);
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
 }
 

@@ -140,7 +140,7 @@ constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
 // (a group that skipped the other group's phase of a stage could see that
 // stale phase as complete: mbarrier waits only tell parities apart).
 template <int NB, WFmt FMT>
-constexpr int w_stages() { return FMT == WFmt::Q5K ? 4 : 6; }  // Q5_K stages are 22 KB
+constexpr int w_stages() { return FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 4 : 6; }  // Q5_K / Q6_K: 22 / 26 KB
 
 // Activation ring depth (one unit per stage), separate from the TMEM operand
 // slots so that a unit's activations are requested several units ahead: a
@@ -207,6 +207,8 @@ __device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, in
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
+// tmap_w: the weight rows; tmap_ws: the second plane (Q4_0 block scales
+// [N][K/32], Q6_K block d [K/256][N]) or, with SW, the up projection's rows.
 // SW: SwiGLU pair (144-byte formats): tmap_w is the gate, tmap_ws the up
 // projection, C = silu(A Wg^T) * (A Wu^T); every tile index of the cluster
 // becomes two segments (gate, up).
@@ -220,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = DecodeSmem<NB, FMT>;
   using TM = DecodeTmem<NB>;
   constexpr bool kRows144 = aos_rows<FMT>();  // whole block rows per unit (block_q4_K / q5_K, 8 x block_q4_0)
-  static_assert(!SW || kRows144, "SwiGLU pairs take block-row formats");
+  static_assert(!SW || (kRows144 && FMT != WFmt::Q6K), "SwiGLU pairs take one-plane block-row formats");
   constexpr int kSw = SW ? 1 : 0;
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, NB);
   constexpr int kWStages = L::kWStages;
@@ -280,6 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (kRows144) {
       tma_load_2d(dst, ui.up ? &tmap_ws : &tmap_w, ui.sb * unit_row_bytes<FMT>(), ui.tile * kTileRows, BAR(L::bWFull + s),
                   kPolicyEvictFirst);
+      if constexpr (FMT == WFmt::Q6K)  // the tile's 128 block scales d of this unit ([K/256][N] plane)
+        tma_load_2d(dst + kTileRows * kQ6KBodyBytes, &tmap_ws, ui.tile * kTileRows, ui.sb, BAR(L::bWFull + s),
+                    kPolicyEvictFirst);
     } else {
       tma_load_2d(dst, &tmap_w, ui.sb * 128, ui.tile * kTileRows, BAR(L::bWFull + s), kPolicyEvictFirst);
       tma_load_2d(dst + kQ40ScaleOffset, &tmap_ws, ui.sb * 8, ui.tile * kTileRows, BAR(L::bWFull + s),
@@ -317,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kWarpWProducer) {
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
-      if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
+      if (FMT == WFmt::Q4_0 || FMT == WFmt::Q6K) tma_prefetch_desc(&tmap_ws);
       tma_prefetch_desc(&tmap_a);
     }
     for (int b = lane; b < L::kNumBars; b += 32) mbar_init(BAR(b), bar_count(b));
@@ -457,7 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (i >= kSlots && !warp_wait(BAR(L::bUDone + i % kSlots), ((i / kSlots) & 1) ^ 1)) break;
       tc_fence_after();
       const uint8_t* stage = smem + L::kWOff + ws * L::kWStage;
-      dequant_unit_row<FMT>(stage, stage + kQ40ScaleOffset, r, tmem + lane_off + TM::kA + (i % kSlots) * 128);
+      dequant_unit_row<FMT>(stage, stage + kTileRows * unit_row_bytes<FMT>(), r,
+                            tmem + lane_off + TM::kA + (i % kSlots) * 128);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();

@@ -215,4 +215,56 @@ __global__ void dequant_q5k_kernel(const uint8_t* __restrict__ blocks, __half* _
   }
 }
 
+// block_q6_K rows [N][S x 210 B] -> the GEMM's Q6_K layout: block bodies
+// (ql, qh, scales: the first 208 bytes of each block) [N][S x 208 B] and the
+// blocks' fp16 d as a plane [S][N]. One thread per 2-byte word of the source
+// (210-byte blocks are 2-byte aligned), so loads and stores are coalesced.
+__global__ void repack_q6k_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ body,
+                                  uint16_t* __restrict__ dplane, int n, int s) {
+  constexpr int kWords = kQ6KBodyBytes / 2 + 1;  // 105 words per block, d last
+  const long long row_words = (long long)s * kWords;
+  const long long total = (long long)n * row_words;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long row = i / row_words;
+    const long long rem = i - row * row_words;
+    const int b = (int)(rem / kWords);
+    const int w = (int)(rem - (long long)b * kWords);
+    const uint16_t v = src[i];
+    if (w < kWords - 1)
+      body[(row * s + b) * (kWords - 1) + w] = v;
+    else
+      dplane[(long long)b * n + row] = v;
+  }
+}
+
+// Q6_K (repacked) -> fp16 [N, K]: one thread per 64-value chunk of a block;
+// fp16_rn((fp32(d) * sc) * (q - 32)), the gguf-py 0.19.0 Q6_K dequant rounded
+// once to fp16 (d * sc is exact in fp32; the second product rounds once).
+__global__ void dequant_q6k_kernel(const uint8_t* __restrict__ body, const __half* __restrict__ dplane,
+                                   __half* __restrict__ out, int n, int s) {
+  const long long nchunks = (long long)n * s * 4;
+  for (long long c = blockIdx.x * (long long)blockDim.x + threadIdx.x; c < nchunks;
+       c += (long long)gridDim.x * blockDim.x) {
+    const long long blk_i = c >> 2;        // row * s + block
+    const int cc = (int)(c & 3);
+    const long long row = blk_i / s;
+    const int b = (int)(blk_i - row * s);
+    const uint8_t* blk = body + blk_i * kQ6KBodyBytes;
+    const float d = __half2float(dplane[(long long)b * n + row]);
+    const int h = cc >> 1, odd = cc & 1;
+    __half* o = out + blk_i * 256 + cc * 64;
+    for (int jj = 0; jj < 2; ++jj) {
+      for (int l = 0; l < 32; ++l) {
+        const int e = 64 * cc + 32 * jj + l;   // element within the block
+        const uint32_t qlb = blk[64 * h + 32 * jj + l];
+        const uint32_t qhb = blk[128 + 32 * h + l];
+        const int q = (int)(((odd ? qlb >> 4 : qlb) & 0xFu) | (((qhb >> (4 * odd + 2 * jj)) & 3u) << 4));
+        const float ds = d * (float)(int)(int8_t)blk[192 + e / 16];
+        o[32 * jj + l] = __float2half_rn(ds * (float)(q - 32));
+      }
+    }
+  }
+}
+
 }  // namespace busfill

@@ -12,6 +12,11 @@
 //   bias 0x6400 = 1024 + q, high nibbles via 0x5400, whose mantissa step is
 //   1/16, = 64 + q). Two fp16 roundings per weight (~3e-4 relative rms); the
 //   bit-exact fp16 dequant is busfill_dequant_q4k.
+//   Q6_K: operand (q-32)*ds with ds = fp16_rn(d*sc) per 16-value group; q is
+//   exact above the bias (a byte-permute writes each 6-bit q under the fp16
+//   exponent byte 0x64: 1024 + q), hsub2 by 1056 is exact, hmul2 rounds. Two
+//   fp16 roundings per weight; the bit-exact fp16 dequant is
+//   busfill_dequant_q6k.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -24,8 +29,12 @@ namespace busfill {
 
 // Q4_0: the reference's split planes; Q4K: llama.cpp block_q4_K rows;
 // Q4_0G: llama.cpp block_q4_0 rows (18-byte blocks: fp16 d, 16 nibble bytes);
-// Q5K: llama.cpp block_q5_K rows (176 bytes per 256 values).
-enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3 };
+// Q5K: llama.cpp block_q5_K rows (176 bytes per 256 values);
+// Q6K: llama.cpp block_q6_K rows repacked by busfill_repack_q6k into 208-byte
+// block bodies (ql, qh, scales) per row and a plane of the blocks' fp16 d,
+// block-major [K/256][N] (210-byte rows have no 16-byte row stride, which the
+// tensor-memory-access copies need, unless K is a multiple of 2048).
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3, Q6K = 4 };
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
 constexpr int kUnitK = 256;          // K per unit
@@ -33,17 +42,26 @@ constexpr int kChunkK = 64;          // K per activation box / 32 TMEM operand c
 constexpr int kChunksPerUnit = kUnitK / kChunkK;
 constexpr int kQ4KBlockBytes = 144;
 constexpr int kQ5KBlockBytes = 176;
+constexpr int kQ6KBodyBytes = 208;   // block_q6_K without its trailing fp16 d
 constexpr int kWStageBytes = 18432;  // 128 x 144 B (Q4_K) or 128 x 128 B + 128 x 16 B (Q4_0)
 
 // Formats stored as whole block rows (one TMA box per unit of 128 rows).
 template <WFmt F>
 constexpr bool aos_rows() { return F != WFmt::Q4_0; }
-// Bytes of one 256-value unit of a weight row as stored (Q4_0: its nibble plane).
+// Bytes of one 256-value unit of a weight row as stored (Q4_0: its nibble
+// plane; Q6_K: its block body).
 template <WFmt F>
-constexpr int unit_row_bytes() { return F == WFmt::Q5K ? kQ5KBlockBytes : F == WFmt::Q4_0 ? 128 : kQ4KBlockBytes; }
-// One unit of 128 weight rows in shared memory (Q4_0: nibbles, then 8 scales per row).
+constexpr int unit_row_bytes() {
+  return F == WFmt::Q5K ? kQ5KBlockBytes : F == WFmt::Q6K ? kQ6KBodyBytes : F == WFmt::Q4_0 ? 128 : kQ4KBlockBytes;
+}
+// Bytes per row and unit of the format's second plane, which a weight stage
+// holds after the rows of the unit (Q4_0: 8 fp16 block scales; Q6_K: fp16 d).
 template <WFmt F>
-constexpr int wstage_bytes() { return F == WFmt::Q4_0 ? kWStageBytes : kTileRows * unit_row_bytes<F>(); }
+constexpr int aux_row_bytes() { return F == WFmt::Q4_0 ? 16 : F == WFmt::Q6K ? 2 : 0; }
+// One unit of 128 weight rows in shared memory: the rows, then their second plane.
+template <WFmt F>
+constexpr int wstage_bytes() { return kTileRows * (unit_row_bytes<F>() + aux_row_bytes<F>()); }
+static_assert(wstage_bytes<WFmt::Q4_0>() == kWStageBytes && wstage_bytes<WFmt::Q4K>() == kWStageBytes, "stages");
 constexpr int kQ40ScaleOffset = 16384;
 // ---------------------------------------------------------------------------
 // dequant helpers (one weight row per thread)
@@ -167,6 +185,41 @@ __device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1
   }
 }
 
+// Q6_K, one 64-value chunk cc of a block (half h = cc / 2; odd = cc % 2):
+// qlp points at the half's 64 ql bytes (shared memory, 16-byte aligned),
+// qh[0..7] are its 32 qh bytes. Element l
+// of group jj (elements 32 jj + l of the chunk) has its low 4 bits in ql byte
+// 32 jj + l (low nibble for even chunks, high nibble for odd ones) and its
+// top 2 bits at bit 4 odd + 2 jj of qh byte l. ds[t]: fp16 d*sc of the
+// chunk's 16-value group t. Writes (q-32)*ds: out[16 jj + i] = elements
+// 32 jj + 2i, +1.
+template <int ODD>
+__device__ __forceinline__ void dequant_q6k_chunk(const uint8_t* qlp, const uint32_t* qh, const __half2* ds,
+                                                  uint32_t* out) {
+  const __half2 b1056 = __halves2half2(__ushort_as_half(0x6420), __ushort_as_half(0x6420));  // 1024 + 32
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    constexpr int kLoSh = 4 * ODD;  // nibble of the ql bytes
+    const uint4 x0 = *reinterpret_cast<const uint4*>(qlp + 32 * jj);
+    const uint4 x1 = *reinterpret_cast<const uint4*>(qlp + 32 * jj + 16);
+    const uint32_t ql[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      // the top 2 bits sit at bit s = 4 ODD + 2 jj of each qh byte; move them
+      // to bits 4-5 (bits that cross into a neighbouring byte are masked off)
+      const int s = 4 * ODD + 2 * jj;
+      const uint32_t hq = s <= 4 ? qh[i] << (4 - s) : qh[i] >> (s - 4);
+      // four 6-bit values (bytes) of elements 4i .. 4i+3 of the group
+      const uint32_t q4 = lop3_and_or(ql[i] >> kLoSh, 0x0F0F0F0Fu, hq & 0x30303030u);
+      const uint32_t v01 = prmt(q4, 0x64u, 0x4140u);  // {0x64 q0, 0x64 q1}: fp16 1024 + q
+      const uint32_t v23 = prmt(q4, 0x64u, 0x4342u);
+      const __half2 d = ds[2 * jj + (i >> 2)];
+      out[16 * jj + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v01), b1056), d));
+      out[16 * jj + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v23), b1056), d));
+    }
+  }
+}
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>
@@ -176,14 +229,15 @@ __device__ __forceinline__ float to_out<float>(float v) { return v; }
 
 // Dequantize chunks [C0, C1) of this thread's weight row r of one unit held
 // in a weight stage (the TMA box of the unit: Q4_K / Q4_0G rows of 144 B;
+// Q5_K rows of 176 B; Q6_K rows of 208 B and the rows' fp16 d at `aux` + 2 r;
 // Q4_0 rows of 128 B of nibbles with the 128-byte swizzle, and 8 fp16 scales
-// per row at `q40_scales` + 16 r) and store them as TMEM operand columns from
+// per row at `aux` + 16 r) and store them as TMEM operand columns from
 // `a_slot` (this warp's lane quarter already in the address): chunk cc goes
 // to columns 32 (cc - C0) .. +31, column c of a chunk holding k = 64 cc + 2c,
 // 2c+1 as an fp16 pair. The caller waits for the stores (tcgen05.wait::st)
 // before publishing the slot.
 template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
-__device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* q40_scales, int r,
+__device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* aux, int r,
                                                  uint32_t a_slot) {
   static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
   if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q5K) {
@@ -225,6 +279,32 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       }
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     }
+  } else if constexpr (FMT == WFmt::Q6K) {
+    const uint8_t* row = stage + r * kQ6KBodyBytes;   // ql at 0, qh at 128, int8 scales at 192
+    const float d = __half2float(*reinterpret_cast<const __half*>(aux + 2 * r));
+    const uint4 scv = *reinterpret_cast<const uint4*>(row + 192);
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    auto chunk = [&](auto cc_tag) {
+      constexpr int cc = decltype(cc_tag)::value;
+      constexpr int h = cc >> 1;
+      uint32_t qh[8];
+#pragma unroll
+      for (int v = 0; v < 2; ++v) {
+        const uint4 x = *reinterpret_cast<const uint4*>(row + 128 + 32 * h + 16 * v);
+        qh[4 * v] = x.x; qh[4 * v + 1] = x.y; qh[4 * v + 2] = x.z; qh[4 * v + 3] = x.w;
+      }
+      __half2 ds[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        ds[t] = __float2half2_rn(d * (float)(int)(int8_t)((scw[cc] >> (8 * t)) & 0xFFu));
+      uint32_t P[32];
+      dequant_q6k_chunk<cc & 1>(row + 64 * h, qh, ds, P);
+      tmem_st_x32(a_slot + (cc - C0) * 32, P);
+    };
+    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
+    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
+    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
+    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
   } else if constexpr (FMT == WFmt::Q4_0G) {
     const uint8_t* urow = stage + r * unit_row_bytes<FMT>();
     uint32_t P[32];
@@ -247,7 +327,7 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
   } else {
     const uint8_t* wrow = stage + r * 128;
     const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
-    const uint4 dd = *reinterpret_cast<const uint4*>(q40_scales + r * 16);  // 8 block scales
+    const uint4 dd = *reinterpret_cast<const uint4*>(aux + r * 16);  // 8 block scales
 #pragma unroll 1
     for (int cc = C0; cc < C1; ++cc) {
       uint32_t P[32];

@@ -59,7 +59,6 @@ constexpr int kThreads = 512;
 constexpr int kBatchTile = 128;                 // batch rows per item = MMA N
 constexpr int kPairRows = 2 * kTileRows;        // weight rows per item
 constexpr int kXStages = 3;                     // half units (2 chunks each)
-constexpr int kQ40Scales = 2 * kQ40ScaleOffset; // Q4_0: scales of the 256 rows after the nibbles
 constexpr int kXChunk = kBatchTile * 128;       // 64 values x 128 rows, 16 KB
 constexpr int kXStage = 2 * kXChunk;            // one K half of a unit, 32 KB
 constexpr int kAccCols = kBatchTile;            // per weight tile
@@ -68,12 +67,13 @@ constexpr int kSlot0 = 2 * kAccCols;
 constexpr int kTmemCols = 512;
 static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
 
-// shared memory map (the weight stage holds both tiles' unit: 256 rows; Q4_0:
-// 32 KB of nibbles, then 4 KB of scales)
+// shared memory map (the weight stage holds both tiles' unit: 256 rows, then
+// the rows' second plane: Q4_0 32 KB of nibbles and 4 KB of scales; Q6_K
+// 52 KB of block bodies and 512 B of d)
 template <WFmt FMT>
 struct Smem {
   static constexpr int kWStage = 2 * wstage_bytes<FMT>();
-  static constexpr int kWStages = FMT == WFmt::Q5K ? 2 : 3;   // Q5_K stages are 44 KB
+  static constexpr int kWStages = FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 2 : 3;   // Q5_K / Q6_K: 44 / 52.5 KB
   static constexpr int kWOff = 0;
   static constexpr int kXOff = kWOff + kWStages * kWStage;
   static constexpr int kBarOff = kXOff + kXStages * kXStage;
@@ -116,6 +116,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, kBatchTile);
   constexpr bool kRows144 = aos_rows<FMT>();
   constexpr int kRowBytes = unit_row_bytes<FMT>();
+  constexpr int kAuxOff = kPairRows * kRowBytes;   // second plane of the stage's 256 rows
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
@@ -166,10 +167,12 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
                     kPolicyEvictLast);
       } else {
         tma_load_2d(dst, &tmap_w, k * kRowBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+        if constexpr (FMT == WFmt::Q6K)  // the 256 rows' block scales d of unit k ([K/256][N] plane)
+          tma_load_2d(dst + kAuxOff, &tmap_ws, pair * kPairRows, k, BAR(bWFull + s), kPolicyEvictLast);
       }
     } else {
       tma_load_2d(dst, &tmap_w, k * 128, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
-      tma_load_2d(dst + kQ40Scales, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+      tma_load_2d(dst + kAuxOff, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
     }
   };
   // activations of half unit v = 2u + h (chunks 2h, 2h+1 of unit u) into stage v % kXStages
@@ -189,7 +192,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   if (warp == 0) {
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
-      if (FMT == WFmt::Q4_0) tma_prefetch_desc(&tmap_ws);
+      if (FMT == WFmt::Q4_0 || FMT == WFmt::Q6K) tma_prefetch_desc(&tmap_ws);
       tma_prefetch_desc(&tmap_a);
     }
     for (int b = lane; b < kNumBars; b += 32) mbar_init(BAR(b), bar_count(b));
@@ -305,9 +308,9 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         tc_fence_after();
         const uint32_t a_col = tmem + lane_off + (uint32_t)(kSlot0 + sl * kSlotCols);
         if (h == 0)
-          dequant_unit_row<FMT, 0, 2>(stage, stage + kQ40Scales, row, a_col);
+          dequant_unit_row<FMT, 0, 2>(stage, stage + kAuxOff, row, a_col);
         else
-          dequant_unit_row<FMT, 2, 4>(stage, stage + kQ40Scales, row, a_col);
+          dequant_unit_row<FMT, 2, 4>(stage, stage + kAuxOff, row, a_col);
         tc_wait_st();
         tc_fence_before();
         __syncwarp();

@@ -161,6 +161,23 @@ BUSFILL_API int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a,
  * numerics as busfill_gemm_q4k (two fp16 roundings of the weight operand). */
 BUSFILL_API int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
 
+/* Q6_K weights (llama.cpp block_q6_K: 128 B ql, 64 B qh, 16 int8 scales,
+ * fp16 d per 256 values), in the layout busfill_repack_q6k writes:
+ *   body [N, K/256 * 208] u8  every block's first 208 bytes (ql, qh, scales)
+ *   d    [K/256, N] fp16      the blocks' d, block-major
+ * A 210-byte block row has a 16-byte row stride (which the kernels'
+ * tensor-memory-access copies need) only when K % 2048 == 0, so the blocks
+ * are split once at load time; the bytes per weight stay 6.5625 bits.
+ * Operand (q-32)*fp16_rn(d*sc), two fp16 roundings (as Q4_K); N % 8 == 0
+ * (d's row stride), K % 256 == 0, body/d/a 16-byte aligned.  No reference
+ * counterpart: the other K-quant format that Q4_K_M models mix in. */
+BUSFILL_API int busfill_gemm_q6k(const uint8_t* body, const uint16_t* d, const uint16_t* a, uint16_t* c, int M, int N,
+                                 int K, void* stream);
+
+/* block_q6_K rows [N, K/256 * 210] (2-byte aligned) -> body and d as above.
+ * Asynchronous on `stream`; `blocks` and the outputs must not overlap. */
+BUSFILL_API int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_t* d, int N, int K, void* stream);
+
 /* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
  * in the reference.
  *
@@ -218,6 +235,10 @@ BUSFILL_API int busfill_dequant_q4k(const uint8_t* blocks, uint16_t* out, int N,
 /* fp16_rn(fp32(d)*sc*q - fp32(dmin)*m) per llama.cpp block_q5_K. K % 256 == 0.
  * No reference counterpart. */
 BUSFILL_API int busfill_dequant_q5k(const uint8_t* blocks, uint16_t* out, int N, int K, void* stream);
+
+/* fp16_rn((fp32(d)*sc)*(q-32)) per llama.cpp block_q6_K, from the repacked
+ * layout of busfill_gemm_q6k. K % 256 == 0. No reference counterpart. */
+BUSFILL_API int busfill_dequant_q6k(const uint8_t* body, const uint16_t* d, uint16_t* out, int N, int K, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Status, options, diagnostics

@@ -35,6 +35,9 @@ Parity pins (tests/test_oracle.py):
 * Q4_K -- pinned against golden vectors produced by gguf-py 0.19.0's
   ``Q4_K.dequantize_blocks`` (fixture ``q4k_gguf.npz``); the reference itself
   has no Q4_K code, so this is the only available anchor.
+* Q5_K and Q6_K (llama.cpp ``block_q5_K`` / ``block_q6_K``, the formats that
+  Q4_K_M models mix in) -- pinned the same way against gguf-py 0.19.0
+  (``q5k_gguf.npz``, ``q6k_gguf.npz``).
 """
 from __future__ import annotations
 
@@ -44,6 +47,8 @@ QK4_0 = 32          # values per Q4_0 block
 QK_K = 256          # values per Q4_K super-block
 Q4K_BLOCK_BYTES = 144
 Q5K_BLOCK_BYTES = 176
+Q6K_BLOCK_BYTES = 210
+Q6K_PACKED_BYTES = 208   # a block_q6_K without its trailing fp16 d
 Q4K_SCALE_BYTES = 12
 
 
@@ -288,6 +293,86 @@ def dequant_q5k(blocks: np.ndarray, k: int) -> np.ndarray:
 
 
 # --------------------------------------------------------------------------
+# Q6_K (llama.cpp block_q6_K, 210 bytes per 256 values)
+# --------------------------------------------------------------------------
+def make_q6k_blocks(d16, sc, q) -> np.ndarray:
+    """Assemble ``block_q6_K`` rows: 128 bytes ``ql``, 64 bytes ``qh``, 16
+    int8 sub-block scales, fp16 d (gguf-py 0.19.0 ``Q6_K`` layout).
+
+    q: u8 [N, S*256] 6-bit values in element order. Element e of a block
+    (half h = e // 128, group j = (e % 128) // 32, l = e % 32) keeps its low 4
+    bits in ``ql[64h + 32(j % 2) + l]`` (low nibble for j < 2, high nibble for
+    j >= 2) and its top 2 bits in bits 2j, 2j+1 of ``qh[32h + l]``; scale
+    ``sc[e // 16]`` (int8) multiplies it.
+    """
+    d16 = np.asarray(d16, dtype=np.float16)
+    n, s = d16.shape
+    q = np.asarray(q, dtype=np.uint8).reshape(n, s, 2, 4, 32)
+    lo = q & 0x0F
+    ql = np.concatenate([lo[:, :, :, 0] | (lo[:, :, :, 2] << 4), lo[:, :, :, 1] | (lo[:, :, :, 3] << 4)],
+                        axis=3).reshape(n, s, 128)
+    hi = (q >> 4) & 3
+    qh = (hi[:, :, :, 0] | (hi[:, :, :, 1] << 2) | (hi[:, :, :, 2] << 4) | (hi[:, :, :, 3] << 6)).reshape(n, s, 64)
+    scb = np.asarray(sc, dtype=np.int8).reshape(n, s, 16).view(np.uint8)
+    hdr_d = d16.reshape(n, s, 1).view(np.uint8)
+    return np.concatenate([ql, qh.astype(np.uint8), scb, hdr_d], axis=2).reshape(n, s * Q6K_BLOCK_BYTES)
+
+
+def split_q6k_blocks(blocks: np.ndarray, k: int):
+    """``block_q6_K`` rows -> (d16 [N,S], sc int8 [N,S,16], q [N,K] in 0..63)."""
+    n = blocks.shape[0]
+    s = k // QK_K
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(n, s, Q6K_BLOCK_BYTES)
+    ql = b[:, :, 0:128].reshape(n, s, 2, 2, 32)          # [h][j % 2][l]
+    qh = b[:, :, 128:192].reshape(n, s, 2, 32)           # [h][l]
+    sc = b[:, :, 192:208].copy().view(np.int8)
+    d16 = b[:, :, 208:210].copy().view(np.float16).reshape(n, s)
+    lo = np.stack([ql[:, :, :, 0] & 0x0F, ql[:, :, :, 1] & 0x0F, ql[:, :, :, 0] >> 4, ql[:, :, :, 1] >> 4], axis=2)
+    hi = np.stack([(qh >> (2 * j)) & 3 for j in range(4)], axis=2)   # [n, s, 4(j), 2(h), 32]
+    q = (lo | (hi << 4)).transpose(0, 1, 3, 2, 4).reshape(n, s * QK_K)
+    return d16, sc, q
+
+
+def dequant_q6k_f32(blocks: np.ndarray, k: int) -> np.ndarray:
+    """Q6_K dequant in fp32 (gguf-py 0.19.0 ``Q6_K.dequantize_blocks`` order):
+    ``(fp32(d) * sc) * (q - 32)``; ``d * sc`` is exact (19 bits), the product
+    rounds once."""
+    d16, sc, q = split_q6k_blocks(blocks, k)
+    n, s = d16.shape
+    ds = d16.astype(np.float32)[:, :, None] * sc.astype(np.float32)          # [n, s, 16]
+    qf = (q.astype(np.int16) - 32).astype(np.float32).reshape(n, s, 16, 16)
+    return (ds[:, :, :, None] * qf).reshape(n, k).astype(np.float32)
+
+
+def dequant_q6k(blocks: np.ndarray, k: int) -> np.ndarray:
+    """Bit-exact Q6_K fp16 operand: ``fp16_rn(w32)``."""
+    return dequant_q6k_f32(blocks, k).astype(np.float16)
+
+
+def repack_q6k(blocks: np.ndarray, k: int):
+    """The device layout ``busfill_repack_q6k`` writes: every block's first
+    208 bytes (``ql``, ``qh``, scales) as rows u8 [N, S*208], and the blocks'
+    fp16 d as a plane [S, N] (block-major), so that both have row strides of
+    whole 16-byte multiples (the tensor-memory-access copy rule; 210-byte
+    rows have none unless K is a multiple of 2048)."""
+    n = blocks.shape[0]
+    s = k // QK_K
+    b = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(n, s, Q6K_BLOCK_BYTES)
+    qb = b[:, :, :Q6K_PACKED_BYTES].reshape(n, s * Q6K_PACKED_BYTES).copy()
+    d = b[:, :, Q6K_PACKED_BYTES:].copy().view(np.float16).reshape(n, s).T.copy()
+    return qb, d
+
+
+def unpack_q6k(qb: np.ndarray, d: np.ndarray, k: int) -> np.ndarray:
+    """Inverse of repack_q6k: ``block_q6_K`` rows u8 [N, S*210]."""
+    n = qb.shape[0]
+    s = k // QK_K
+    body = np.ascontiguousarray(qb, dtype=np.uint8).reshape(n, s, Q6K_PACKED_BYTES)
+    hdr = np.ascontiguousarray(np.asarray(d, dtype=np.float16).T).reshape(n, s, 1).view(np.uint8)
+    return np.concatenate([body, hdr], axis=2).reshape(n, s * Q6K_BLOCK_BYTES)
+
+
+# --------------------------------------------------------------------------
 # Seeded synthetic generators (BASELINE configs 0-4; no public dataset)
 # --------------------------------------------------------------------------
 def gen_activations(m: int, k: int, seed: int) -> np.ndarray:
@@ -337,6 +422,19 @@ def gen_q5k(n: int, k: int, seed: int):
     m = rng.integers(0, 64, size=(n, s, 8), dtype=np.uint8)
     q = rng.integers(0, 32, size=(n, k), dtype=np.uint8)
     return make_q5k_blocks(d16, dmin16, sc, m, q)
+
+
+def gen_q6k(n: int, k: int, seed: int):
+    """Q6_K weights: d ~ U(0.0001, 0.0005) fp16, int8 sub-block scales
+    uniform [-128, 127], 6-bit values uniform [0, 63] (weights of the same
+    order as config 2's). Returns ``block_q6_K`` rows u8 [N, K/256*210]."""
+    assert k % QK_K == 0
+    rng = np.random.default_rng(seed)
+    s = k // QK_K
+    d16 = rng.uniform(0.0001, 0.0005, size=(n, s)).astype(np.float16)
+    sc = rng.integers(-128, 128, size=(n, s, 16)).astype(np.int8)
+    q = rng.integers(0, 64, size=(n, k), dtype=np.uint8)
+    return make_q6k_blocks(d16, sc, q)
 
 
 # --------------------------------------------------------------------------

@@ -15,6 +15,8 @@ Fixtures written next to this script (small .npz files, committed):
   reference has no Q4_K code, so this third-party implementation is the anchor.
 * ``q5k_gguf.npz`` -- gguf-py 0.19.0 ``Q5_K.dequantize_blocks`` on seeded
   random ``block_q5_K`` rows (a BASELINE "next" format; no reference code).
+* ``q6k_gguf.npz`` -- gguf-py 0.19.0 ``Q6_K.dequantize_blocks`` on seeded
+  random ``block_q6_K`` rows (the other "next" k-quant format).
 * ``q4_0_gguf.npz`` -- gguf-py 0.19.0 ``Q4_0.dequantize_blocks`` on seeded
   random llama.cpp ``block_q4_0`` rows (the AoS Q4_0 layout).
 
@@ -131,6 +133,30 @@ def make_q5k_gguf():
     np.savez_compressed(os.path.join(HERE, "q5k_gguf.npz"), **out)
 
 
+def make_q6k_gguf():
+    from gguf import GGMLQuantizationType
+    from gguf.quants import dequantize
+
+    rng = np.random.default_rng(2026)
+    out = {}
+    # case a: the generator's distributions; case b: every byte random except
+    # d, whose exponents are spread over the normal fp16 range (either sign)
+    for name, n, k, wide in (("a", 16, 512, False), ("b", 24, 768, True)):
+        s = k // 256
+        if wide:
+            d = _random_f16(rng, (n, s), -14, 3, signed=True)
+        else:
+            d = rng.uniform(0.0001, 0.0005, size=(n, s)).astype(np.float16)
+        body = rng.integers(0, 256, size=(n, s, 208), dtype=np.uint8)
+        blocks = np.concatenate([body, d.reshape(n, s, 1).view(np.uint8)], axis=2).reshape(n, s * 210)
+        w32 = dequantize(blocks, GGMLQuantizationType.Q6_K)
+        assert w32.shape == (n, k) and w32.dtype == np.float32
+        out[f"{name}_blocks"] = blocks
+        out[f"{name}_w32"] = w32
+        out[f"{name}_k"] = np.array(k)
+    np.savez_compressed(os.path.join(HERE, "q6k_gguf.npz"), **out)
+
+
 def make_q4_0_gguf():
     from gguf import GGMLQuantizationType
     from gguf.quants import dequantize
@@ -152,6 +178,7 @@ def main():
     make_q4_0_reference(args.reference)
     make_q4k_gguf()
     make_q5k_gguf()
+    make_q6k_gguf()
     make_q4_0_gguf()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):

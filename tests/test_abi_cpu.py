@@ -49,6 +49,9 @@ def test_null_pointer_rejected_before_any_device_work():
     assert lib.busfill_gemm_q4k_swiglu(None, None, None, None, 8, 128, 256, None) == -1
     assert lib.busfill_gemm_q5k(None, None, None, 8, 128, 256, None) == -1
     assert lib.busfill_dequant_q5k(None, None, 4, 256, None) == -1
+    assert lib.busfill_gemm_q6k(None, None, None, None, 8, 128, 256, None) == -1
+    assert lib.busfill_repack_q6k(None, None, None, 4, 256, None) == -1
+    assert lib.busfill_dequant_q6k(None, None, None, 4, 256, None) == -1
     assert lib.busfill_dequant_q4k(None, None, 4, 256, None) == -1
     assert lib.busfill_probe_umma(None, None, None, 16, None) == -1
 
@@ -160,6 +163,61 @@ def test_q4k_operand_chain_is_within_two_roundings_of_oracle():
     assert np.all(np.abs(got.astype(np.float64) - w32) <= bound)
     rel = np.linalg.norm(got.astype(np.float64) - w32) / np.linalg.norm(w32)
     assert rel < 5e-4, rel
+
+
+def test_q6k_shape_and_alignment_checked_before_any_device_work():
+    lib = bf.load_library()
+    fake = 0x10000                     # never dereferenced: the checks come first
+    # the d plane [K/256][N] fp16 needs a 16-byte row stride: N % 8 == 0
+    assert lib.busfill_gemm_q6k(fake, fake, fake, fake, 4, 100, 256, None) == -2
+    assert lib.busfill_gemm_q6k(fake, fake, fake, fake, 4, 128, 300, None) == -2
+    assert lib.busfill_gemm_q6k(fake + 8, fake, fake, fake, 4, 128, 256, None) == -3
+    assert lib.busfill_repack_q6k(fake + 1, fake, fake, 4, 256, None) == -3
+    assert lib.busfill_repack_q6k(fake, fake, fake, 4, 100, None) == -2
+
+
+def q6k_chunk_chain(body, d16, cc):
+    """Bit-level model of dequant_q6k_chunk<cc % 2> (formats.cuh) on one
+    208-byte block body: returns the chunk's 64 exact integers q - 32 (from
+    the biased fp16 words) and its 64 fp16 operands, in column order."""
+    h, odd = cc >> 1, cc & 1
+    ql = body[64 * h: 64 * h + 64].copy().view(np.uint32)
+    qh = body[128 + 32 * h: 128 + 32 * h + 32].copy().view(np.uint32)
+    sc = body[192 + 4 * cc: 196 + 4 * cc].copy().view(np.int8)
+    ds = [(np.float32(d16) * np.float32(sc[t])).astype(np.float16) for t in range(4)]
+    ints, vals = [], []
+    for jj in range(2):
+        s = 4 * odd + 2 * jj
+        for i in range(8):
+            w = int(qh[i])
+            hq = ((w << (4 - s)) & 0xFFFFFFFF) if s <= 4 else (w >> (s - 4))
+            q4 = ((int(ql[8 * jj + i]) >> (4 * odd)) & 0x0F0F0F0F) | (hq & 0x30303030)
+            for sel in (0x4140, 0x4342):
+                for half in h2(prmt(q4, 0x64, sel)):
+                    qm = np.float16(np.float64(half) - 1056.0)     # hsub2 by 1056: exact
+                    ints.append(float(qm))
+                    vals.append(rn16(np.float64(qm) * np.float64(ds[2 * jj + i // 4])))
+    return ints, np.array(vals, dtype=np.float16)
+
+
+def test_q6k_chunk_chain_order_exactness_and_rounding():
+    blocks = orc.gen_q6k(6, 512, seed=11)
+    d16, sc, q = orc.split_q6k_blocks(blocks, 512)
+    body, dplane = orc.repack_q6k(blocks, 512)
+    w32 = orc.dequant_q6k_f32(blocks, 512)
+    for r in range(6):
+        for b in range(2):
+            blk = body[r, 208 * b: 208 * (b + 1)]
+            for cc in range(4):
+                ints, vals = q6k_chunk_chain(blk, dplane[b, r], cc)
+                e0 = 256 * b + 64 * cc
+                assert ints == [float(v) - 32 for v in q[r, e0: e0 + 64]]
+                want = w32[r, e0: e0 + 64].astype(np.float64)
+                dsa = np.abs(np.float64(d16[r, b]) * np.repeat(sc[r, b, 4 * cc: 4 * cc + 4], 16).astype(np.float64))
+                qa = np.abs(np.array(ints))
+                # |err| <= ulp(ds)/2 * |q-32| + ulp(w)/2, ulps <= 2^-10 of the value
+                bound = 2.0 ** -11 * (dsa * qa + np.abs(want)) + 1e-9
+                assert np.all(np.abs(vals.astype(np.float64) - want) <= bound)
 
 
 def test_q4k_chunk_extraction_and_order():

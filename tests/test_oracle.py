@@ -5,6 +5,8 @@
 * Q4_K dequant vs gguf-py 0.19.0 ``Q4_K.dequantize_blocks``, fixture q4k_gguf.npz.
 * llama.cpp AoS Q4_0 dequant vs gguf-py ``Q4_0.dequantize_blocks``, q4_0_gguf.npz.
 * Q5_K dequant vs gguf-py ``Q5_K.dequantize_blocks``, q5k_gguf.npz.
+* Q6_K dequant vs gguf-py ``Q6_K.dequantize_blocks``, q6k_gguf.npz, and the
+  device layout of busfill_repack_q6k (208-byte block bodies + a d plane).
 * Exhaustive checks of the 6-bit scale/min packing.
 """
 import os
@@ -81,6 +83,46 @@ def test_q5k_block_split_make_roundtrip(golden_dir):
     w = orc.gen_q5k(8, 512, seed=3)
     d, dmin, sc, m, q = orc.split_q5k_blocks(w, 512)
     assert q.max() <= 31 and q.min() >= 0 and sc.max() < 64 and m.max() < 64
+
+
+@pytest.mark.parametrize("case", ["a", "b"])
+def test_q6k_dequant_matches_gguf_golden(golden_dir, case):
+    """Q6_K dequant vs gguf-py 0.19.0 ``Q6_K.dequantize_blocks`` (q6k_gguf.npz)."""
+    g = _load(golden_dir, "q6k_gguf.npz")
+    blocks, w32, k = g[f"{case}_blocks"], g[f"{case}_w32"], int(g[f"{case}_k"])
+    assert np.array_equal(orc.dequant_q6k_f32(blocks, k).view(np.uint32), w32.view(np.uint32))
+    with np.errstate(over="ignore"):
+        want16 = w32.astype(np.float16)
+    assert np.array_equal(orc.dequant_q6k(blocks, k).view(np.uint16), want16.view(np.uint16))
+
+
+def test_q6k_block_split_make_repack_roundtrip(golden_dir):
+    g = _load(golden_dir, "q6k_gguf.npz")
+    blocks, k = g["b_blocks"], int(g["b_k"])
+    assert np.array_equal(orc.make_q6k_blocks(*orc.split_q6k_blocks(blocks, k)), blocks)
+    qb, d = orc.repack_q6k(blocks, k)
+    n, s = blocks.shape[0], k // 256
+    assert qb.shape == (n, s * 208) and d.shape == (s, n) and d.dtype == np.float16
+    assert (s * 208) % 16 == 0
+    assert np.array_equal(orc.unpack_q6k(qb, d, k), blocks)
+    # the generator's values come back out of the blocks
+    w = orc.gen_q6k(8, 512, seed=3)
+    d16, sc, q = orc.split_q6k_blocks(w, 512)
+    assert q.min() >= 0 and q.max() <= 63 and sc.min() >= -128 and sc.max() <= 127
+
+
+def test_q6k_element_placement():
+    """One non-zero 6-bit value at a time lands at its own element index."""
+    n, k = 1, 256
+    d = np.full((n, 1), 1.0, dtype=np.float16)
+    sc = np.arange(1, 17, dtype=np.int8).reshape(n, 1, 16)
+    for e in (0, 17, 31, 32, 63, 64, 100, 127, 128, 161, 200, 255):
+        q = np.full((n, k), 32, dtype=np.uint8)
+        q[0, e] = 32 + 29
+        w = orc.dequant_q6k_f32(orc.make_q6k_blocks(d, sc, q), k)
+        want = np.zeros((n, k), dtype=np.float32)
+        want[0, e] = 29.0 * (e // 16 + 1)
+        assert np.array_equal(w, want), e
 
 
 def test_q4k_block_split_make_roundtrip(golden_dir):
