@@ -157,31 +157,31 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 // Q5_K, one 64-value chunk cc of a super-block: q0/q1 are the chunk's 32 qs
 // bytes (byte l: low nibble element l of sub-block 2cc, high nibble element l
 // of sub-block 2cc+1), h0/h1 the 32 qh bytes (bit G of byte l: the fifth bit
-// of element l of sub-block G). The fifth bit joins the magic bias: mantissa
-// bit 4 of 1024 + q (low nibbles) or bit 8 of 64 + q (high nibbles, mantissa
-// step 1/16) is worth 16, so both stay exact integers 0..31 above the bias.
-__device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1, int cc,
+// of element l of sub-block G). Each byte of a word is first made the whole
+// 5-bit value (nibble | fifth bit << 4); a byte-permute then sets each value
+// under the fp16 exponent byte 0x64, giving the exact fp16 1024 + q.
+template <int CC>
+__device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1,
                                                   const __half2 ds_lo, const __half2 ndm_lo, const __half2 ds_hi,
                                                   const __half2 ndm_hi, uint32_t* out) {
   const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-  const int bl = 2 * cc, bh = 2 * cc + 1;
+  constexpr int bl = 2 * CC, bh = 2 * CC + 1;   // the fifth bits' positions in the qh bytes
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t t0 = prmt(w[i], w[i], 0x0100u);    // byte0 = b0, byte2 = b1
-    const uint32_t t1 = prmt(w[i], w[i], 0x0302u);    // byte0 = b2, byte2 = b3
-    const uint32_t u0 = prmt(hw[i], hw[i], 0x0100u);  // the same elements' qh bytes
-    const uint32_t u1 = prmt(hw[i], hw[i], 0x0302u);
-    const uint32_t l01 = lop3_and_or(t0, 0x000F000Fu, 0x64006400u | (((u0 >> bl) & 0x00010001u) << 4));
-    const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u | (((u1 >> bl) & 0x00010001u) << 4));
-    const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u | (((u0 >> bh) & 0x00010001u) << 8));
-    const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u | (((u1 >> bh) & 0x00010001u) << 8));
+    // move bit b of every qh byte to bit 4 of the same byte (bits pushed into
+    // a neighbouring byte never land on bit 4 and are masked off)
+    const uint32_t fl = (bl <= 4 ? hw[i] << (4 - bl) : hw[i] >> (bl - 4)) & 0x10101010u;
+    const uint32_t fh = (bh <= 4 ? hw[i] << (4 - bh) : hw[i] >> (bh - 4)) & 0x10101010u;
+    const uint32_t ql = lop3_and_or(w[i], 0x0F0F0F0Fu, fl);        // four 5-bit values, sub-block 2cc
+    const uint32_t qh = lop3_and_or(w[i] >> 4, 0x0F0F0F0Fu, fh);   // sub-block 2cc+1
+    const uint32_t l01 = prmt(ql, 0x64u, 0x4140u), l23 = prmt(ql, 0x64u, 0x4342u);  // {1024 + q}
+    const uint32_t h01 = prmt(qh, 0x64u, 0x4140u), h23 = prmt(qh, 0x64u, 0x4342u);
     out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
     out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
-    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
-    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
+    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k1024), ds_hi, ndm_hi));
+    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k1024), ds_hi, ndm_hi));
   }
 }
 
@@ -240,7 +240,7 @@ template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
 __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* aux, int r,
                                                  uint32_t a_slot) {
   static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
-  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q5K) {
+  if constexpr (FMT == WFmt::Q4K) {
     constexpr int kRow = unit_row_bytes<FMT>();
     // this row's block header: d, dmin and the 6-bit scales/mins of its
     // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
@@ -252,33 +252,59 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
     const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
     const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
     const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-#pragma unroll 1
-    for (int cc = C0; cc < C1; ++cc) {
+    auto chunk = [&](auto cc_tag) {
+      constexpr int cc = decltype(cc_tag)::value;
       // chunk cc covers sub-blocks 2cc, 2cc+1: bytes 2(cc&1), 2(cc&1)+1 of the
       // _lo words (cc < 2) or of the _hi words (cc >= 2)
       const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
       const uint32_t mw = cc < 2 ? m_lo : m_hi;
-      const int sh = 16 * (cc & 1);
+      constexpr int sh = 16 * (cc & 1);
       const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
       const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
       const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
       const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
       uint32_t P[32];
-      if constexpr (FMT == WFmt::Q4K) {
-        const uint8_t* qs = stage + r * kRow + 16 + cc * 32;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-        dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
-      } else {
-        const uint8_t* row = stage + r * kRow;  // qh at 16, qs at 48
-        const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
-        const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
-        const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
-        dequant_q5k_chunk(q0, q1, h0, h1, cc, dsl, dml, dsh, dmh, P);
-      }
+      const uint8_t* qs = stage + r * kRow + 16 + cc * 32;
+      const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
+      dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
-    }
+    };
+    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
+    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
+    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
+    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
+  } else if constexpr (FMT == WFmt::Q5K) {
+    // header as Q4_K; qh at 16, qs at 48
+    const uint8_t* row = stage + r * kQ5KBlockBytes;
+    const uint4 hdr = *reinterpret_cast<const uint4*>(row);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
+    const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
+    auto chunk = [&](auto cc_tag) {
+      constexpr int cc = decltype(cc_tag)::value;
+      const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
+      const uint32_t mw = cc < 2 ? m_lo : m_hi;
+      constexpr int sh = 16 * (cc & 1);
+      const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
+      const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
+      const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
+      const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
+      const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
+      const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
+      const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
+      const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
+      uint32_t P[32];
+      dequant_q5k_chunk<cc>(q0, q1, h0, h1, dsl, dml, dsh, dmh, P);
+      tmem_st_x32(a_slot + (cc - C0) * 32, P);
+    };
+    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
+    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
+    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
+    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
   } else if constexpr (FMT == WFmt::Q6K) {
     const uint8_t* row = stage + r * kQ6KBodyBytes;   // ql at 0, qh at 128, int8 scales at 192
     const float d = __half2float(*reinterpret_cast<const __half*>(aux + 2 * r));

@@ -176,6 +176,34 @@ def test_q6k_shape_and_alignment_checked_before_any_device_work():
     assert lib.busfill_repack_q6k(fake, fake, fake, 4, 100, None) == -2
 
 
+def test_q5k_chunk_chain_values_and_order():
+    """Bit-level model of dequant_q5k_chunk<cc> (formats.cuh): each byte made
+    the 5-bit value, then set under the fp16 exponent byte 0x64 by a
+    byte-permute; hsub2 by 1024 leaves the exact integer q."""
+    blocks = orc.gen_q5k(4, 512, seed=12)
+    _, _, _, _, q = orc.split_q5k_blocks(blocks, 512)
+    b = blocks.reshape(4, 2, 176)
+    for r in range(4):
+        for blk in range(2):
+            row = b[r, blk]
+            hw = row[16:48].copy().view(np.uint32)
+            for cc in range(4):
+                w = row[48 + 32 * cc: 80 + 32 * cc].copy().view(np.uint32)
+                lo, hi = [], []
+                for i in range(8):
+                    def fifth(bit):
+                        x = int(hw[i])
+                        return ((x << (4 - bit)) & 0xFFFFFFFF if bit <= 4 else x >> (bit - 4)) & 0x10101010
+                    ql = (int(w[i]) & 0x0F0F0F0F) | fifth(2 * cc)
+                    qh = ((int(w[i]) >> 4) & 0x0F0F0F0F) | fifth(2 * cc + 1)
+                    for src, dst in ((ql, lo), (qh, hi)):
+                        for sel in (0x4140, 0x4342):
+                            for half in h2(prmt(src, 0x64, sel)):
+                                dst.append(float(np.float16(np.float64(half) - 1024.0)))
+                e0 = 256 * blk + 64 * cc
+                assert lo + hi == [float(v) for v in q[r, e0: e0 + 64]]
+
+
 def q6k_chunk_chain(body, d16, cc):
     """Bit-level model of dequant_q6k_chunk<cc % 2> (formats.cuh) on one
     208-byte block body: returns the chunk's 64 exact integers q - 32 (from
