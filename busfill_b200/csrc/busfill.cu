@@ -38,17 +38,25 @@ std::atomic<int> g_use_pdl{1};
 std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 // Batch size from which GEMMs take the prefill kernel (one pass over the
 // weights for all rows) instead of the decode kernel (32 rows a launch).
-// 0 = automatic: M >= 128 and at least kPrefillMinItems work items (256
-// weight rows x 128 batch rows each), since the prefill kernel runs one item
-// per SM at a time; with fewer items the decode kernel's K split over
-// clusters uses the GPU better (measured on B200: M = 128, N = 5120,
-// K = 17408 takes 157 us as 20 prefill items, 93 us as four decode launches).
+// 0 = automatic:
+//  * with the stream-K workspace (plain GEMMs): M > kStreamKMinM. Every SM
+//    gets an equal share of the units however few work items there are;
+//    measured on B200 (Q4_K), three or more decode launches lose to it on
+//    every config-4 shape (M = 96: 29 vs 31 us at K = N = 5120, 44 vs 59 us at
+//    N = 5120, K = 17408, 44 vs 47 us at N = 17408, K = 5120) and two win
+//    (M = 64: 21 vs 29, 39 vs 44, 32 vs 44 us).
+//  * without it (SwiGLU pairs, the no-allocation entry point, a first call
+//    inside a graph capture): M >= 128 and at least kPrefillMinItems work
+//    items, since whole items go one per SM (measured: M = 128, N = 5120,
+//    K = 17408 takes 157 us as 20 items, 93 us as four decode launches).
+constexpr int kStreamKMinM = 64;
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
 
-bool use_prefill(int M, int N, bool swiglu = false) {
+bool use_prefill(int M, int N, bool swiglu = false, bool stream_k = false) {
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
+  if (stream_k && !swiglu) return M > kStreamKMinM;
   const int pair_rows = swiglu ? kTileRows : prefill::kPairRows;  // SwiGLU items: gate tile j + up tile j
   const long long items = (long long)((N + pair_rows - 1) / pair_rows) *
                           ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
@@ -155,6 +163,30 @@ int get_error_words(int dev, cudaStream_t s, unsigned** out) {
   }
   *out = w;
   return BUSFILL_OK;
+}
+
+// The prefill kernel's stream-K partial tiles: two fp32 tiles of 128 batch
+// rows x 256 weight rows per CTA, one workspace per (device, stream) so that
+// GEMMs on different streams never share one. Allocated on first use; never
+// while the stream is capturing a graph (an allocation would end the
+// capture), in which case the kernel runs without stream-K.
+std::map<std::pair<int, cudaStream_t>, float*> g_part;
+
+float* prefill_workspace(int dev, cudaStream_t s, int sm_count) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  float*& w = g_part[{dev, s}];
+  if (!w) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    if (cudaMalloc(&w, (size_t)2 * sm_count * prefill::kPartElems * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      w = nullptr;
+    }
+  }
+  return w;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -401,9 +433,12 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
 // ---------------------------------------------------------------------------
 // prefill GEMM launch
 // ---------------------------------------------------------------------------
+// `part`: the stream's partial-tile workspace (stream-K), or nullptr for whole
+// items round-robin; SwiGLU pairs always take whole items.
 template <WFmt FMT, typename OutT>
 int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-                int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
+                int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr,
+                float* part = nullptr) {
   const int S = K / kUnitK;
   const int swiglu = w_up ? 1 : 0;
   CUtensorMap tw, tws, ta;
@@ -454,12 +489,27 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   p.btiles = (M + prefill::kBatchTile - 1) / prefill::kBatchTile;
   p.units = S;
   const long long items = (long long)p.pairs * p.btiles;
-  const int grid = (int)std::min<long long>(items, di.sm_count);
+  const long long units = items * S;
+  p.part = swiglu ? nullptr : part;
+  const int grid = p.part ? (int)std::min<long long>(units, di.sm_count) : (int)std::min<long long>(items, di.sm_count);
   void* args[] = {&tw, &tws, &ta, &p};
   if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::Smem<FMT>::kAlloc, s, args, g_use_pdl.load() != 0) !=
       cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_LAUNCH;
+  }
+  if (p.part && grid > 1) {
+    // items split between CTAs: their partial tiles summed in CTA order
+    const float* cpart = p.part;
+    OutT* cc = reinterpret_cast<OutT*>(c);
+    int m = M, n = N, su = S, bts = p.btiles, g = grid;
+    long long t = units;
+    void* rargs[] = {&cpart, &cc, &m, &n, &su, &bts, &g, &t};
+    if (launch(reinterpret_cast<const void*>(prefill_reduce_kernel<OutT>), dim3(grid - 1, prefill::kBatchTile / 16),
+               dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
+      cudaGetLastError();
+      return BUSFILL_ERR_LAUNCH;
+    }
   }
   return BUSFILL_OK;
 }
@@ -467,9 +517,12 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
 // Decode (M < prefill threshold) or prefill kernel for one GEMM.
 template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
-             int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr) {
-  if (use_prefill(M, N, w_up != nullptr))
-    return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
+             int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr, bool may_alloc = true) {
+  // the stream-K workspace is only looked up (and made) for GEMMs that may use it
+  const bool want_sk = may_alloc && !w_up && (g_prefill_min_m.load() > 0 || M > kStreamKMinM);
+  float* part = want_sk ? prefill_workspace(dev, s, di.sm_count) : nullptr;
+  if (use_prefill(M, N, w_up != nullptr, part != nullptr))
+    return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
   return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
 }
 
@@ -582,7 +635,8 @@ int gemm_q4k_static(const uint8_t* w, const uint16_t* a, uint16_t* c, int M, int
     cudaGetLastError();
     return BUSFILL_ERR_CUDA;
   }
-  return run_gemm<WFmt::Q4K, __half>(di, dev, w, nullptr, a, c, M, N, K, reinterpret_cast<unsigned*>(scratch), s);
+  return run_gemm<WFmt::Q4K, __half>(di, dev, w, nullptr, a, c, M, N, K, reinterpret_cast<unsigned*>(scratch), s,
+                                     nullptr, false);
 }
 
 }  // namespace
@@ -596,7 +650,7 @@ int busfill_version(void) { return kVersion; }
 
 unsigned busfill_last_failure_detail(void) { return g_last_detail.load(); }
 
-int busfill_gemm_kernel_for(int M, int N) { return use_prefill(M, N) ? 1 : 0; }
+int busfill_gemm_kernel_for(int M, int N) { return use_prefill(M, N, false, true) ? 1 : 0; }
 
 const char* busfill_status_string(int status) {
   switch (status) {

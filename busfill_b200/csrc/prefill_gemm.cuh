@@ -37,9 +37,15 @@
 //   12-15  epilogue: reads both accumulators once per item, writes C
 //   2      idle
 //
-// Work order: item = pair * B + batch_tile, so the CTAs running at the same
-// time share weight tiles (one HBM read, the rest from L2) and stream the
-// activations, which stay L2-resident (evict-last hint).
+// Work order: item = pair * B + batch_tile. With a partial-tile workspace
+// (stream-K), CTA c of G takes the contiguous range [c T / G, (c+1) T / G) of
+// the T = items x S units in item-major order, so every CTA gets the same
+// number of units whatever the item count (20 items of K = 17408 fill 148
+// SMs): an item that lies wholly inside one CTA's range is written to C by
+// that CTA; an item split between CTAs leaves fp32 partial tiles (two slots
+// per CTA: its first and its last item), which prefill_reduce_kernel adds in
+// CTA order (deterministic) and writes to C. Without a workspace, whole items
+// go round-robin (item = c + j G).
 //
 // Every wait is bounded (ptx.cuh: kWaitTimeoutNs).
 #pragma once
@@ -98,7 +104,16 @@ struct Params {
   int btiles;         // B = ceil(M / 128)
   int units;          // S = K / 256
   int swiglu;         // 1: C = silu(A Wg^T) * (A Wu^T); tmap_w gate, tmap_ws up (128-row boxes)
+  float* part;        // stream-K partial tiles [2 G][128 batch rows][256 weight rows], or nullptr
 };
+
+// Stream-K range of CTA c of g over t units: [first_unit(c), first_unit(c + 1)).
+__host__ __device__ __forceinline__ long long first_unit(long long t, int c, int g) { return t * c / g; }
+// The CTA whose range holds unit x.
+__host__ __device__ __forceinline__ int cta_of_unit(long long t, long long x, int g) {
+  return (int)(((x + 1) * g - 1) / t);
+}
+constexpr int kPartElems = kPairRows * kBatchTile;   // one partial tile, fp32
 
 }  // namespace prefill
 
@@ -130,9 +145,26 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   const int lane = threadIdx.x & 31;
   const int S = p.units;
   const int items = p.pairs * p.btiles;
-  const int my_items = (items - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  const int nunits = my_items * S;
-  auto item_of = [&](int j) { return (int)blockIdx.x + j * (int)gridDim.x; };
+  const int G = (int)gridDim.x, bid = (int)blockIdx.x;
+  const bool sk = p.part != nullptr;   // stream-K ranges, else whole items round-robin
+  const long long T = (long long)items * S;
+  const long long g0 = sk ? first_unit(T, bid, G) : 0;
+  const int nunits = sk ? (int)(first_unit(T, bid + 1, G) - g0) : ((items - bid + G - 1) / G) * S;
+  // item and unit k of this CTA's u-th unit
+  auto unit_at = [&](int u, int& it, int& k) {
+    if (sk) {
+      const long long gu = g0 + u;
+      it = (int)(gu / S);
+      k = (int)(gu - (long long)it * S);
+    } else {
+      const int j = u / S;
+      k = u - j * S;
+      it = bid + j * G;
+    }
+  };
+  // pieces: the (partial) items of this CTA, in order
+  const int npieces = nunits == 0 ? 0 : sk ? (int)((g0 + nunits - 1) / S - g0 / S + 1) : nunits / S;
+  auto piece_item = [&](int j) { return sk ? (int)(g0 / S) + j : bid + j * G; };
 
   bool ok = true;
   int diag_unit = -1;
@@ -153,9 +185,10 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     return 1;                                              // TMA expect_tx arrivals, MMA commits
   };
 
-  // weight TMA of unit u (item j = u / S, unit k = u % S) into stage u % kWStages
+  // weight TMA of this CTA's unit u into stage u % kWStages
   auto issue_w = [&](int u) {
-    const int it = item_of(u / S), k = u % S;
+    int it, k;
+    unit_at(u, it, k);
     const int pair = it / p.btiles;
     const int s = u % kWStages;
     const uint32_t dst = sbase + kWOff + s * kWStage;
@@ -178,7 +211,8 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   // activations of half unit v = 2u + h (chunks 2h, 2h+1 of unit u) into stage v % kXStages
   auto issue_x = [&](int v) {
     const int u = v >> 1, h = v & 1;
-    const int it = item_of(u / S), k = u % S;
+    int it, k;
+    unit_at(u, it, k);
     const int bt = it % p.btiles;
     const int s = v % kXStages;
     mbar_arrive_expect_tx(BAR(bXFull + s), kXStage);
@@ -248,11 +282,14 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   } else if (warp == 3) {
     // ---------------- MMA issuer ----------------
     const uint64_t bdesc0 = make_sdesc_sw128(sbase + kXOff);
+    int j = 0;   // piece
     for (int u = 0; u < nunits; ++u) {
       diag_unit = u;
-      const int j = u / S, k = u % S;
-      // the accumulators are free once the epilogue has read item j - 1
-      if (k == 0 && j >= 1 && !warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1))) break;
+      int it, k;
+      unit_at(u, it, k);
+      const bool first = u == 0 || k == 0, last = u == nunits - 1 || k == S - 1;
+      // the accumulators are free once the epilogue has read piece j - 1
+      if (first && j >= 1 && !warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1))) break;
       bool good = true;
 #pragma unroll 1
       for (int h = 0; h < 2 && good; ++h) {
@@ -272,7 +309,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
                 mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks, bx + (uint64_t)(((cl * kXChunk) + 32 * ks) >> 4), kIdesc,
-                           (k == 0 && h == 0 && cl == 0 && ks == 0) ? 0u : 1u);
+                           (first && h == 0 && cl == 0 && ks == 0) ? 0u : 1u);
             tc_commit(BAR(bSDone + sl));  // half slot free once these MMAs complete
           }
           __syncwarp();
@@ -281,8 +318,9 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         __syncwarp();
       }
       if (!good) break;
-      if (elect_one() && k == S - 1) tc_commit(BAR(bAccFull));  // item's accumulators complete
+      if (elect_one() && last) tc_commit(BAR(bAccFull));  // piece's accumulators complete
       __syncwarp();
+      if (last) ++j;
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrMma);
     if (elect_one()) tc_commit(BAR(bFinal));
@@ -328,10 +366,16 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     OutT* C = reinterpret_cast<OutT*>(p.c);
     bool waited_pdl = false;
-    for (int j = 0; j < my_items; ++j) {
-      diag_unit = j * S + S - 1;
-      const int it = item_of(j);
+    for (int j = 0; j < npieces; ++j) {
+      diag_unit = j;
+      const int it = piece_item(j);
       const int pair = it / p.btiles, bt = it % p.btiles;
+      // stream-K: a piece that is not the whole item goes to the CTA's partial
+      // slot (2 bid for its first item, 2 bid + 1 for its last)
+      const bool whole = !sk || ((long long)it * S >= g0 && (long long)(it + 1) * S <= g0 + nunits);
+      float* part = whole ? nullptr : p.part + (size_t)(2 * bid + (j == 0 ? 0 : 1)) * kPartElems;
+      // batch rows of the item that exist: only those are read from TMEM and written
+      const int mv = min(kBatchTile, p.M - bt * kBatchTile);
       const bool have = warp_wait(BAR(bAccFull), (uint32_t)(j & 1));
       tc_fence_after();
       if (!waited_pdl) {
@@ -342,7 +386,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         // accumulator 0 holds the gate tile, 1 the up tile of the same rows
         const int n = pair * kTileRows + r;
 #pragma unroll 1
-        for (int cb = 0; cb < kBatchTile; cb += 16) {
+        for (int cb = 0; cb < mv; cb += 16) {
           uint32_t xg[16], xu[16];
           tmem_ld_x16(tmem + lane_off + (uint32_t)cb, xg);
           tmem_ld_x16(tmem + lane_off + (uint32_t)(kAccCols + cb), xu);
@@ -361,12 +405,17 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         for (int t = 0; t < 2; ++t) {
           const int n = pair * kPairRows + t * kTileRows + r;
 #pragma unroll 1
-          for (int cb = 0; cb < kBatchTile; cb += 32) {
+          for (int cb = 0; cb < mv; cb += 32) {
             uint32_t x[32];
             tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb), x);
             tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb + 16), x + 16);
             tc_wait_ld();
-            if (have && n < p.N) {
+            if (have && part) {
+              // [batch row][weight row] of the pair, the item's existing batch rows
+#pragma unroll
+              for (int i = 0; i < 32; ++i)
+                if (cb + i < mv) part[(cb + i) * kPairRows + t * kTileRows + r] = __uint_as_float(x[i]);
+            } else if (have && n < p.N) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
                 const int b = bt * kBatchTile + cb + i;
@@ -393,6 +442,49 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     if (!done && lane == 0) atomicOr(p.error, kErrTeardown);
     tc_fence_after();
     tmem_dealloc(tmem, prefill::kTmemCols);
+  }
+}
+
+// Stream-K fix-up: each item split between CTAs of the prefill launch (grid
+// g over t = items x S units) is summed from its CTAs' partial tiles, in CTA
+// order, and written to C. Block (x, y): the item holding the first unit of
+// CTA x + 1, if that unit is not an item's first and CTA x + 1 is the first
+// boundary inside the item (else the block exits); batch rows 16 y .. 16 y + 15
+// of the item; thread t owns weight row t of the pair.
+template <typename OutT>
+__global__ void __launch_bounds__(256) prefill_reduce_kernel(const float* __restrict__ part, OutT* __restrict__ c,
+                                                           int M, int N, int S, int btiles, int g, long long t) {
+  using namespace prefill;
+  pdl_wait_prerequisites();   // the partial tiles are the previous kernel's output
+  // the next kernel may start its set-up and weight loads; it reads C, and
+  // writes partial tiles, only after its own wait for this grid to finish
+  pdl_launch_dependents();
+  const int cb = (int)blockIdx.x + 1;
+  const long long gb = first_unit(t, cb, g);
+  if (gb % S == 0) return;
+  const int it = (int)(gb / S);
+  const int c_lo = cta_of_unit(t, (long long)it * S, g);
+  if (c_lo != cb - 1) return;   // an earlier boundary owns this item
+  const int c_hi = cta_of_unit(t, (long long)(it + 1) * S - 1, g);
+  const int pair = it / btiles, bt = it % btiles;
+  const int n = pair * kPairRows + (int)threadIdx.x;
+  const int mv = min(kBatchTile, M - bt * kBatchTile) - 16 * (int)blockIdx.y;   // rows of this block that exist
+  if (mv <= 0) return;
+  float acc[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+  for (int cc = c_lo; cc <= c_hi; ++cc) {
+    const int slot = 2 * cc + ((long long)it == first_unit(t, cc, g) / S ? 0 : 1);
+    const float* src = part + (size_t)slot * kPartElems + (size_t)(16 * blockIdx.y) * kPairRows + threadIdx.x;
+#pragma unroll
+    for (int e = 0; e < 16; ++e)
+      if (e < mv) acc[e] += src[e * kPairRows];
+  }
+  if (n >= N) return;
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    const int b = bt * kBatchTile + 16 * (int)blockIdx.y + e;
+    if (b < M) c[(size_t)b * N + n] = to_out<OutT>(acc[e]);
   }
 }
 

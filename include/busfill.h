@@ -277,18 +277,23 @@ BUSFILL_API int busfill_version(void);
  *     1..8 forces that split where K/256 allows it (a tuning and test knob).
  *   BUSFILL_OPT_PREFILL_MIN_M: GEMMs with M >= value rows run the large-batch
  *     (prefill) kernel, one pass over the weights for all rows, instead of
- *     the decode kernel's launches of 32 rows; 0 (default) chooses by shape
- *     (M >= 128 and at least 64 work items of 256 weight rows x 128 batch
- *     rows). A tuning and test knob; results agree within the accuracy gate.
+ *     the decode kernel's launches of 32 rows; 0 (default) chooses by shape:
+ *     M > 64 for the plain GEMMs, whose prefill kernel splits the units of
+ *     work evenly over all SMs (stream-K, with a per-stream workspace of
+ *     2 x SMs x 128 KB allocated on first use); M >= 128 and at least 64 work
+ *     items of 256 weight rows x 128 batch rows for SwiGLU pairs and
+ *     busfill_gemm_q4k_noalloc, which take whole items. A tuning and test
+ *     knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
 #define BUSFILL_OPT_PREFILL_MIN_M 3
 BUSFILL_API int busfill_set_option(int option, int value);
 
-/* Which kernel a GEMM of M batch rows and N output columns runs with the
- * current options: 0 = decode kernel (launches of 32 rows), 1 = prefill
- * kernel (one pass over the weights). Diagnostic; no reference counterpart. */
+/* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows
+ * and N output columns runs with the current options: 0 = decode kernel
+ * (launches of 32 rows), 1 = prefill kernel (one pass over the weights; by
+ * default from M = 65 on). Diagnostic; no reference counterpart. */
 BUSFILL_API int busfill_gemm_kernel_for(int M, int N);
 
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the

@@ -339,14 +339,14 @@ def test_ksplit_option_values():
 
 
 def test_kernel_choice_by_shape():
-    """Default dispatch: prefill kernel for M >= 128 with >= 64 work items
-    (256 weight rows x 128 batch rows each), decode kernel otherwise; the
-    option forces a plain M threshold and 0 restores the default."""
+    """Default dispatch of the plain GEMMs: the stream-K prefill kernel for
+    M > 64, the decode kernel otherwise; the option forces a plain M threshold
+    and 0 restores the default."""
     bf.load_library()
     assert not bf.uses_prefill(32, 5120)
-    assert not bf.uses_prefill(127, 17408)
-    assert not bf.uses_prefill(128, 5120)        # 20 items: the decode kernel's K split does better
-    assert bf.uses_prefill(128, 17408)           # 68 items
+    assert not bf.uses_prefill(64, 17408)        # two decode launches beat the prefill pass
+    assert bf.uses_prefill(65, 5120)             # stream-K: from three decode launches on
+    assert bf.uses_prefill(128, 5120) and bf.uses_prefill(128, 17408)
     assert bf.uses_prefill(512, 5120) and bf.uses_prefill(2048, 5120)
     bf.set_prefill_min_m(1)
     try:
@@ -354,3 +354,54 @@ def test_kernel_choice_by_shape():
     finally:
         bf.set_prefill_min_m(0)
     assert not bf.uses_prefill(1, 128)
+
+
+# ---------------------------------------------------------------------------
+# stream-K partition of the prefill kernel (prefill_gemm.cuh), restated
+# ---------------------------------------------------------------------------
+def _first_unit(t, c, g):
+    return t * c // g
+
+
+def _cta_of_unit(t, x, g):
+    return ((x + 1) * g - 1) // t
+
+
+@pytest.mark.parametrize("items,s,g", [(20, 68, 148), (80, 68, 148), (1088, 20, 148), (3, 2, 5), (1, 1, 1),
+                                       (7, 3, 21), (68, 20, 148), (2, 20, 40), (5, 1, 5)])
+def test_stream_k_partition_covers_every_unit_once(items, s, g):
+    t = items * s
+    g = min(g, t)
+    covered = np.zeros(t, dtype=np.int32)
+    slots = {}          # (cta, item) -> slot of a partial piece
+    for c in range(g):
+        g0, g1 = _first_unit(t, c, g), _first_unit(t, c + 1, g)
+        assert g1 > g0                                    # every CTA has work
+        covered[g0:g1] += 1
+        for x in (g0, g1 - 1):
+            assert _cta_of_unit(t, x, g) == c
+        pieces = list(range(g0 // s, (g1 - 1) // s + 1))
+        for j, it in enumerate(pieces):
+            whole = it * s >= g0 and (it + 1) * s <= g1
+            if not whole:
+                assert j in (0, len(pieces) - 1)          # only the first or last piece is partial
+                slots[(c, it)] = 2 * c + (0 if j == 0 else 1)
+    assert np.all(covered == 1)
+    # the fix-up: one owner block per split item, summing exactly its CTAs' slots
+    owned = {}
+    for cb in range(1, g):
+        gb = _first_unit(t, cb, g)
+        if gb % s == 0:
+            continue
+        it = gb // s
+        c_lo = _cta_of_unit(t, it * s, g)
+        if c_lo != cb - 1:
+            continue
+        c_hi = _cta_of_unit(t, (it + 1) * s - 1, g)
+        assert it not in owned
+        owned[it] = [2 * cc + (0 if it == _first_unit(t, cc, g) // s else 1) for cc in range(c_lo, c_hi + 1)]
+        assert all(0 <= sl < 2 * g for sl in owned[it])
+    split_items = {it for (_, it) in slots}
+    assert set(owned) == split_items
+    for it, sl in owned.items():
+        assert sorted(sl) == sorted(v for (c, i), v in slots.items() if i == it)

@@ -1,8 +1,9 @@
 """GPU parity of the large-batch (prefill) kernel, through the C ABI.
 
-Large batches (by default M >= 128 with at least 64 work items of 256 weight
-rows x 128 batch rows) run one pass over the weights for all rows; the decode
-kernel covers the rest. These tests force the prefill kernel
+Large batches (by default M > 64 for the plain GEMMs, whose prefill kernel
+spreads the work over all SMs stream-K style; M >= 128 with at least 64 work
+items of 256 weight rows x 128 batch rows where whole items are dealt out)
+run one pass over the weights for all rows; the decode kernel covers the rest. These tests force the prefill kernel
 (BUSFILL_OPT_PREFILL_MIN_M) onto small, ragged and multi-item shapes, and run
 the BASELINE config-4 shapes at full size through the default dispatch,
 checked on sampled rows and columns against the oracle.
@@ -125,3 +126,44 @@ def test_prefill_config4_sampled(m, n, k):
     w32 = orc.dequant_q4k_f32(blocks[cols], k)
     check(c[rows][:, cols], a[rows], w32, w32)
     assert torch.isfinite(c.float()).all()
+
+
+@pytest.mark.parametrize("m,n,k", [(128, 5120, 17408), (128, 17408, 5120), (64, 1024, 17408)])
+def test_prefill_stream_k_split_items_sampled(prefill_always, m, n, k):
+    """Few work items over many units: with stream-K every item of N = 5120,
+    K = 17408 is split between about seven CTAs and summed by the fix-up
+    kernel; the output is checked on sampled columns against the oracle."""
+    blocks = orc.gen_q4k(n, k, seed=3 * m + n + k)
+    a = orc.gen_activations(m, k, seed=m + 2 * k)
+    c = bf.gemm_q4k(cu(blocks), cu(a))
+    assert bf.stream_status() == 0
+    rng = np.random.default_rng(n + k)
+    cols = np.sort(rng.choice(n, 512, replace=False))
+    w32 = orc.dequant_q4k_f32(blocks[cols], k)
+    check(c[:, cols], a, w32, w32)
+    assert torch.isfinite(c.float()).all()
+
+
+def test_prefill_stream_k_is_deterministic(prefill_always):
+    """The split points depend only on the shape and the SM count, and split
+    items are summed in CTA order: two runs give the same bits."""
+    m, n, k = 96, 2048, 17408
+    blocks = cu(orc.gen_q4k(n, k, seed=8))
+    a = cu(orc.gen_activations(m, k, seed=9))
+    c1 = bf.gemm_q4k(blocks, a).clone()
+    c2 = bf.gemm_q4k(blocks, a)
+    assert bf.stream_status() == 0
+    assert torch.equal(c1.view(torch.int16), c2.view(torch.int16))
+
+
+def test_prefill_without_workspace_round_robin(prefill_always):
+    """The no-allocation entry point has no partial-tile workspace: whole
+    items go round-robin over the CTAs (the path without stream-K)."""
+    m, n, k = 200, 1280, 2048
+    blocks = orc.gen_q4k(n, k, seed=21)
+    a = orc.gen_activations(m, k, seed=22)
+    out = torch.empty((m, n), dtype=torch.float16, device=DEV)
+    bf.gemm_q4k_noalloc(cu(blocks), cu(a), out)
+    assert bf.stream_status() == 0
+    w32 = orc.dequant_q4k_f32(blocks, k)
+    check(out, a, w32, w32)
