@@ -599,7 +599,7 @@ def config4(torch, bf, dev, args, hbm_peak, tc_peak, peak_src):
             fl = 2.0 * m * n * k
             tf = fl / (us * 1e-6) / 1e12
             gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
-            rows.append({"M": m, "N": n, "K": k, "kernel": "prefill" if bf.uses_prefill(m, n) else "decode",
+            rows.append({"M": m, "N": n, "K": k, "kernel": "prefill" if bf.uses_prefill(m, n, k) else "decode",
                          "us": round(us, 2), "tflops": round(tf, 1), "tensor_frac": round(tf / tc_peak, 4),
                          "GB_s": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 4),
                          "cublas_fp16_us": round(us_cb, 2)})

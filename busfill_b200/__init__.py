@@ -80,7 +80,7 @@ _SIGS = {
     "busfill_version": [],
     "busfill_set_option": [_I, _I],
     "busfill_probe_umma": [_P, _P, _P, _I, _P],
-    "busfill_gemm_kernel_for": [_I, _I],
+    "busfill_gemm_kernel_for": [_I, _I, _I],
     "busfill_gemm_q4k_gather": [_P, _P, _I, _I, _I, _P, _P],
     "busfill_gemm_q4k_swiglu_gather": [_P, _P, _P, _I, _I, _I, _P, _P],
     "busfill_gather_wait": [_P, _P],
@@ -132,9 +132,9 @@ def set_ksplit(csize: int) -> None:
     _check(_lib().busfill_set_option(2, int(csize)), "busfill_set_option")
 
 
-def uses_prefill(m: int, n: int) -> bool:
-    """True if a GEMM of m batch rows and n output columns runs the prefill kernel."""
-    return _lib().busfill_gemm_kernel_for(int(m), int(n)) == 1
+def uses_prefill(m: int, n: int, k: int) -> bool:
+    """True if a GEMM of m batch rows, n output columns and depth k runs the prefill kernel."""
+    return _lib().busfill_gemm_kernel_for(int(m), int(n), int(k)) == 1
 
 
 def set_prefill_min_m(m: int) -> None:

@@ -39,12 +39,14 @@ std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 // Batch size from which GEMMs take the prefill kernel (one pass over the
 // weights for all rows) instead of the decode kernel (32 rows a launch).
 // 0 = automatic:
-//  * with the stream-K workspace (plain GEMMs): M > kStreamKMinM. Every SM
-//    gets an equal share of the units however few work items there are;
-//    measured on B200 (Q4_K), three or more decode launches lose to it on
-//    every config-4 shape (M = 96: 29 vs 31 us at K = N = 5120, 44 vs 59 us at
-//    N = 5120, K = 17408, 44 vs 47 us at N = 17408, K = 5120) and two win
-//    (M = 64: 21 vs 29, 39 vs 44, 32 vs 44 us).
+//  * with the stream-K workspace (plain GEMMs): M > kStreamKMinM, or M > 32
+//    when N <= K. Every SM gets an equal share of the units however few work
+//    items there are. Measured on B200 (Q4_K, us, decode vs prefill): three
+//    or more decode launches lose on every config-4 shape (M = 96: 31 vs 18
+//    at K = N = 5120, 59 vs 33 at N = 5120, K = 17408, 48 vs 37 at N = 17408,
+//    K = 5120); two lose where N <= K (M = 33: 19.8 vs 15.5, 38.6 vs 32.3) and
+//    win where the decode kernel has many tiles (N = 17408, K = 5120, M = 33:
+//    32.3 vs 38.0).
 //  * without it (SwiGLU pairs, the no-allocation entry point, a first call
 //    inside a graph capture): M >= 128 and at least kPrefillMinItems work
 //    items, since whole items go one per SM (measured: M = 128, N = 5120,
@@ -53,10 +55,10 @@ constexpr int kStreamKMinM = 64;
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
 
-bool use_prefill(int M, int N, bool swiglu = false, bool stream_k = false) {
+bool use_prefill(int M, int N, int K, bool swiglu = false, bool stream_k = false) {
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
-  if (stream_k && !swiglu) return M > kStreamKMinM;
+  if (stream_k && !swiglu) return M > kStreamKMinM || (M > 32 && N <= K);
   const int pair_rows = swiglu ? kTileRows : prefill::kPairRows;  // SwiGLU items: gate tile j + up tile j
   const long long items = (long long)((N + pair_rows - 1) / pair_rows) *
                           ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
@@ -433,6 +435,22 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
 // ---------------------------------------------------------------------------
 // prefill GEMM launch
 // ---------------------------------------------------------------------------
+// The items that a stream-K prefill launch of g CTAs over t = items x s units
+// splits between CTAs (prefill_gemm.cuh: the CTA ranges and partial slots).
+void split_items(long long t, int s, int g, prefill::SplitItems* out) {
+  out->n = 0;
+  for (int cb = 1; cb < g; ++cb) {
+    const long long gb = prefill::first_unit(t, cb, g);
+    if (gb % s == 0) continue;                       // a boundary on an item edge splits nothing
+    const int it = (int)(gb / s);
+    const int c_lo = prefill::cta_of_unit(t, (long long)it * s, g);
+    if (c_lo != cb - 1) continue;                    // an earlier boundary of the same item
+    const int c_hi = prefill::cta_of_unit(t, (long long)(it + 1) * s - 1, g);
+    const int slot_lo = 2 * c_lo + (prefill::first_unit(t, c_lo, g) / s == it ? 0 : 1);
+    out->e[out->n++] = make_int4(it, c_lo, c_hi, slot_lo);
+  }
+}
+
 // `part`: the stream's partial-tile workspace (stream-K), or nullptr for whole
 // items round-robin; SwiGLU pairs always take whole items.
 template <WFmt FMT, typename OutT>
@@ -491,21 +509,24 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   const long long items = (long long)p.pairs * p.btiles;
   const long long units = items * S;
   p.part = swiglu ? nullptr : part;
-  const int grid = p.part ? (int)std::min<long long>(units, di.sm_count) : (int)std::min<long long>(items, di.sm_count);
+  const int grid = p.part ? (int)std::min<long long>(std::min<long long>(units, di.sm_count), prefill::kMaxSplitItems + 1)
+                           : (int)std::min<long long>(items, di.sm_count);
   void* args[] = {&tw, &tws, &ta, &p};
   if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::Smem<FMT>::kAlloc, s, args, g_use_pdl.load() != 0) !=
       cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_LAUNCH;
   }
-  if (p.part && grid > 1) {
+  prefill::SplitItems si;
+  if (p.part) split_items(units, S, grid, &si);
+  if (p.part && si.n > 0) {
     // items split between CTAs: their partial tiles summed in CTA order
     const float* cpart = p.part;
     OutT* cc = reinterpret_cast<OutT*>(c);
-    int m = M, n = N, su = S, bts = p.btiles, g = grid;
-    long long t = units;
-    void* rargs[] = {&cpart, &cc, &m, &n, &su, &bts, &g, &t};
-    if (launch(reinterpret_cast<const void*>(prefill_reduce_kernel<OutT>), dim3(grid - 1, prefill::kBatchTile / 16),
+    int m = M, n = N, bts = p.btiles;
+    void* rargs[] = {&cpart, &cc, &m, &n, &bts, &si};
+    const int rows = std::min(M, prefill::kBatchTile);
+    if (launch(reinterpret_cast<const void*>(prefill_reduce_kernel<OutT>), dim3(si.n, (rows + 3) / 4),
                dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
       cudaGetLastError();
       return BUSFILL_ERR_LAUNCH;
@@ -519,9 +540,9 @@ template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
              int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr, bool may_alloc = true) {
   // the stream-K workspace is only looked up (and made) for GEMMs that may use it
-  const bool want_sk = may_alloc && !w_up && (g_prefill_min_m.load() > 0 || M > kStreamKMinM);
+  const bool want_sk = may_alloc && !w_up && (g_prefill_min_m.load() > 0 || M > 32);
   float* part = want_sk ? prefill_workspace(dev, s, di.sm_count) : nullptr;
-  if (use_prefill(M, N, w_up != nullptr, part != nullptr))
+  if (use_prefill(M, N, K, w_up != nullptr, part != nullptr))
     return run_prefill<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
   return run_decode<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, w_up);
 }
@@ -650,7 +671,7 @@ int busfill_version(void) { return kVersion; }
 
 unsigned busfill_last_failure_detail(void) { return g_last_detail.load(); }
 
-int busfill_gemm_kernel_for(int M, int N) { return use_prefill(M, N, false, true) ? 1 : 0; }
+int busfill_gemm_kernel_for(int M, int N, int K) { return use_prefill(M, N, K, false, true) ? 1 : 0; }
 
 const char* busfill_status_string(int status) {
   switch (status) {

@@ -445,47 +445,65 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   }
 }
 
-// Stream-K fix-up: each item split between CTAs of the prefill launch (grid
-// g over t = items x S units) is summed from its CTAs' partial tiles, in CTA
-// order, and written to C. Block (x, y): the item holding the first unit of
-// CTA x + 1, if that unit is not an item's first and CTA x + 1 is the first
-// boundary inside the item (else the block exits); batch rows 16 y .. 16 y + 15
-// of the item; thread t owns weight row t of the pair.
+// The items a stream-K prefill launch splits between CTAs, listed by the host
+// (split_items): for each, the item, its first and last CTA and the first
+// CTA's partial slot (every later CTA holds the item as its first piece, slot
+// 2 c). A launch of G CTAs splits at most G - 1 items.
+namespace prefill {
+constexpr int kMaxSplitItems = 200;
+struct SplitItems {
+  int n;
+  int4 e[kMaxSplitItems];   // {item, c_lo, c_hi, slot of c_lo}
+};
+}  // namespace prefill
+
+// Stream-K fix-up: each split item is summed from its CTAs' partial tiles, in
+// CTA order, and written to C. Block (x, y): split item x, batch rows 4 y ..
+// 4 y + 3 of the item, 64 threads per row, each owning 4 consecutive weight
+// rows of the pair (one 16-byte load per partial tile). The loads of up to
+// eight partial tiles are issued together and added in CTA order.
 template <typename OutT>
 __global__ void __launch_bounds__(256) prefill_reduce_kernel(const float* __restrict__ part, OutT* __restrict__ c,
-                                                           int M, int N, int S, int btiles, int g, long long t) {
+                                                           int M, int N, int btiles,
+                                                           const __grid_constant__ prefill::SplitItems si) {
   using namespace prefill;
   pdl_wait_prerequisites();   // the partial tiles are the previous kernel's output
   // the next kernel may start its set-up and weight loads; it reads C, and
   // writes partial tiles, only after its own wait for this grid to finish
   pdl_launch_dependents();
-  const int cb = (int)blockIdx.x + 1;
-  const long long gb = first_unit(t, cb, g);
-  if (gb % S == 0) return;
-  const int it = (int)(gb / S);
-  const int c_lo = cta_of_unit(t, (long long)it * S, g);
-  if (c_lo != cb - 1) return;   // an earlier boundary owns this item
-  const int c_hi = cta_of_unit(t, (long long)(it + 1) * S - 1, g);
-  const int pair = it / btiles, bt = it % btiles;
-  const int n = pair * kPairRows + (int)threadIdx.x;
-  const int mv = min(kBatchTile, M - bt * kBatchTile) - 16 * (int)blockIdx.y;   // rows of this block that exist
-  if (mv <= 0) return;
-  float acc[16];
+  const int4 e = si.e[blockIdx.x];
+  const int it = e.x, c_lo = e.y, c_hi = e.z, slot_lo = e.w;
+  const int pair = it / btiles, bt = it - (it / btiles) * btiles;
+  const int row = 4 * (int)blockIdx.y + ((int)threadIdx.x >> 6);          // batch row within the item
+  const int col = 4 * ((int)threadIdx.x & 63);                            // weight row within the pair
+  if (bt * kBatchTile + row >= M) return;
+  const size_t off = (size_t)row * kPairRows + col;
+  auto slot_ptr = [&](int cc) {
+    const int slot = cc == c_lo ? slot_lo : 2 * cc;
+    return reinterpret_cast<const float4*>(part + (size_t)slot * kPartElems + off);
+  };
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = c_lo; c0 <= c_hi; c0 += 8) {
+    float4 v[8];
 #pragma unroll
-  for (int e = 0; e < 16; ++e) acc[e] = 0.f;
-  for (int cc = c_lo; cc <= c_hi; ++cc) {
-    const int slot = 2 * cc + ((long long)it == first_unit(t, cc, g) / S ? 0 : 1);
-    const float* src = part + (size_t)slot * kPartElems + (size_t)(16 * blockIdx.y) * kPairRows + threadIdx.x;
+    for (int i = 0; i < 8; ++i)
+      if (c0 + i <= c_hi) v[i] = *slot_ptr(c0 + i);
 #pragma unroll
-    for (int e = 0; e < 16; ++e)
-      if (e < mv) acc[e] += src[e * kPairRows];
+    for (int i = 0; i < 8; ++i)
+      if (c0 + i <= c_hi) {
+        acc.x += v[i].x;
+        acc.y += v[i].y;
+        acc.z += v[i].z;
+        acc.w += v[i].w;
+      }
   }
-  if (n >= N) return;
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    const int b = bt * kBatchTile + 16 * (int)blockIdx.y + e;
-    if (b < M) c[(size_t)b * N + n] = to_out<OutT>(acc[e]);
-  }
+  const int b = bt * kBatchTile + row;
+  const int n = pair * kPairRows + col;
+  OutT* dst = c + (size_t)b * N + n;
+  if (n < N) dst[0] = to_out<OutT>(acc.x);
+  if (n + 1 < N) dst[1] = to_out<OutT>(acc.y);
+  if (n + 2 < N) dst[2] = to_out<OutT>(acc.z);
+  if (n + 3 < N) dst[3] = to_out<OutT>(acc.w);
 }
 
 }  // namespace busfill

@@ -278,9 +278,10 @@ BUSFILL_API int busfill_version(void);
  *   BUSFILL_OPT_PREFILL_MIN_M: GEMMs with M >= value rows run the large-batch
  *     (prefill) kernel, one pass over the weights for all rows, instead of
  *     the decode kernel's launches of 32 rows; 0 (default) chooses by shape:
- *     M > 64 for the plain GEMMs, whose prefill kernel splits the units of
- *     work evenly over all SMs (stream-K, with a per-stream workspace of
- *     2 x SMs x 128 KB allocated on first use); M >= 128 and at least 64 work
+ *     M > 64, or M > 32 when N <= K, for the plain GEMMs, whose prefill
+ *     kernel splits the units of work evenly over all SMs (stream-K, with a
+ *     per-stream workspace of 2 x SMs x 128 KB allocated on first use, never
+ *     during a graph capture); M >= 128 and at least 64 work
  *     items of 256 weight rows x 128 batch rows for SwiGLU pairs and
  *     busfill_gemm_q4k_noalloc, which take whole items. A tuning and test
  *     knob; results agree within the accuracy gate.
@@ -290,11 +291,12 @@ BUSFILL_API int busfill_version(void);
 #define BUSFILL_OPT_PREFILL_MIN_M 3
 BUSFILL_API int busfill_set_option(int option, int value);
 
-/* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows
- * and N output columns runs with the current options: 0 = decode kernel
- * (launches of 32 rows), 1 = prefill kernel (one pass over the weights; by
- * default from M = 65 on). Diagnostic; no reference counterpart. */
-BUSFILL_API int busfill_gemm_kernel_for(int M, int N);
+/* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,
+ * N output columns and depth K runs with the current options: 0 = decode
+ * kernel (launches of 32 rows), 1 = prefill kernel (one pass over the
+ * weights; by default for M > 64, and for M > 32 when N <= K). Diagnostic;
+ * no reference counterpart. */
+BUSFILL_API int busfill_gemm_kernel_for(int M, int N, int K);
 
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the
  * spirit of kernels/frag_probe.cu:1-48: d[128, nb] = a[128, 64] * b[nb, 64]^T

@@ -340,20 +340,21 @@ def test_ksplit_option_values():
 
 def test_kernel_choice_by_shape():
     """Default dispatch of the plain GEMMs: the stream-K prefill kernel for
-    M > 64, the decode kernel otherwise; the option forces a plain M threshold
-    and 0 restores the default."""
+    M > 64, and for M > 32 when N <= K; the decode kernel otherwise. The option
+    forces a plain M threshold and 0 restores the default."""
     bf.load_library()
-    assert not bf.uses_prefill(32, 5120)
-    assert not bf.uses_prefill(64, 17408)        # two decode launches beat the prefill pass
-    assert bf.uses_prefill(65, 5120)             # stream-K: from three decode launches on
-    assert bf.uses_prefill(128, 5120) and bf.uses_prefill(128, 17408)
-    assert bf.uses_prefill(512, 5120) and bf.uses_prefill(2048, 5120)
+    assert not bf.uses_prefill(32, 5120, 5120)
+    assert not bf.uses_prefill(64, 17408, 5120)   # many decode tiles: two decode launches win
+    assert bf.uses_prefill(33, 5120, 5120) and bf.uses_prefill(64, 5120, 17408)   # N <= K: stream-K wins
+    assert bf.uses_prefill(65, 17408, 5120)       # from three decode launches on
+    assert bf.uses_prefill(128, 5120, 17408) and bf.uses_prefill(128, 17408, 5120)
+    assert bf.uses_prefill(512, 5120, 5120) and bf.uses_prefill(2048, 5120, 17408)
     bf.set_prefill_min_m(1)
     try:
-        assert bf.uses_prefill(1, 128)
+        assert bf.uses_prefill(1, 128, 256)
     finally:
         bf.set_prefill_min_m(0)
-    assert not bf.uses_prefill(1, 128)
+    assert not bf.uses_prefill(1, 128, 256)
 
 
 # ---------------------------------------------------------------------------
@@ -400,6 +401,8 @@ def test_stream_k_partition_covers_every_unit_once(items, s, g):
         c_hi = _cta_of_unit(t, (it + 1) * s - 1, g)
         assert it not in owned
         owned[it] = [2 * cc + (0 if it == _first_unit(t, cc, g) // s else 1) for cc in range(c_lo, c_hi + 1)]
+        # the fix-up kernel's shortcut: every CTA after c_lo holds the item as its first piece
+        assert owned[it][1:] == [2 * cc for cc in range(c_lo + 1, c_hi + 1)]
         assert all(0 <= sl < 2 * g for sl in owned[it])
     split_items = {it for (_, it) in slots}
     assert set(owned) == split_items
