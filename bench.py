@@ -644,44 +644,101 @@ def cublas_comparator(torch, bf, dev, l2, weights, a, args):
 
 
 def e2e(torch, bf, dev, weights, a, args, steps):
-    """The same metric through the public API with HOST buffers: every call
-    copies its activations from pinned host memory, runs the C-ABI GEMM
-    (ctypes, no graph) and reads the output back to pinned host memory."""
+    """The same metric through the public API with HOST buffers. Each call
+    copies its activations from pinned host memory, runs the C-ABI GEMM and
+    reads its output back to pinned host memory; every call has its own host
+    and device buffers, as independent requests do. Two measurements:
+
+    * value: the calls of a step (one per weight copy) captured once as a
+      CUDA graph with the copies on their own streams, so that call i+1's
+      input copy and call i-1's output copy overlap call i's GEMM (the way a
+      serving loop drives the library); the graph is replayed `steps` times,
+      replays one after another, CUDA events around them.
+    * eager_serial: the same calls issued one by one from Python on a single
+      stream (copy, GEMM, copy), host overheads included.
+    """
     m, k = a.shape
     n = weights[0].shape[0] if args.fmt == "q4k" else weights[0][0].shape[0]
-    h_a = torch.empty((m, k), dtype=torch.float16).pin_memory()
-    h_a.copy_(a.cpu())
-    h_c = torch.empty((m, n), dtype=torch.float16).pin_memory()
-    d_a = torch.empty_like(a)
-    d_c = torch.empty((m, n), dtype=torch.float16, device=dev)
-    st = torch.cuda.Stream(device=dev)
+    R = len(weights)
+    h_a = torch.empty((R, m, k), dtype=torch.float16).pin_memory()
+    h_a.copy_(a.cpu().expand(R, m, k))
+    h_c = torch.empty((R, m, n), dtype=torch.float16).pin_memory()
+    d_a = torch.empty((R, m, k), dtype=torch.float16, device=dev)
+    d_c = torch.empty((R, m, n), dtype=torch.float16, device=dev)
+    s_cmp, s_in, s_out = (torch.cuda.Stream(device=dev) for _ in range(3))
 
-    def step():
-        for w in weights:
-            d_a.copy_(h_a, non_blocking=True)
-            if args.fmt == "q4k":
-                bf.gemm_q4k(w, d_a, out=d_c, stream=st)
-            else:
-                bf.gemm_q4_0(w[0], w[1], d_a, out=d_c, stream=st)
-            h_c.copy_(d_c, non_blocking=True)
+    def gemm(i, w, st):
+        if args.fmt == "q4k":
+            bf.gemm_q4k(w, d_a[i], out=d_c[i], stream=st)
+        else:
+            bf.gemm_q4_0(w[0], w[1], d_a[i], out=d_c[i], stream=st)
 
-    with torch.cuda.stream(st):
+    def serial_step():
+        for i, w in enumerate(weights):
+            d_a[i].copy_(h_a[i], non_blocking=True)
+            gemm(i, w, s_cmp)
+            h_c[i].copy_(d_c[i], non_blocking=True)
+
+    def pipelined_step():
+        fork = torch.cuda.Event()
+        fork.record(s_cmp)
+        s_in.wait_event(fork)
+        s_out.wait_event(fork)
+        for i, w in enumerate(weights):
+            e_in, e_cmp = torch.cuda.Event(), torch.cuda.Event()
+            with torch.cuda.stream(s_in):
+                d_a[i].copy_(h_a[i], non_blocking=True)
+                e_in.record(s_in)
+            s_cmp.wait_event(e_in)
+            gemm(i, w, s_cmp)
+            e_cmp.record(s_cmp)
+            s_out.wait_event(e_cmp)
+            with torch.cuda.stream(s_out):
+                h_c[i].copy_(d_c[i], non_blocking=True)
+        join_in, join_out = torch.cuda.Event(), torch.cuda.Event()
+        join_in.record(s_in)
+        join_out.record(s_out)
+        s_cmp.wait_event(join_in)
+        s_cmp.wait_event(join_out)
+
+    def timed(fn):
+        with torch.cuda.stream(s_cmp):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s_cmp)
+            for _ in range(steps):
+                fn()
+            e1.record(s_cmp)
+        e1.synchronize()
+        return e0.elapsed_time(e1)
+
+    # warm-up, eager (also makes the library's per-stream words before capture)
+    with torch.cuda.stream(s_cmp):
         for _ in range(2):
-            step()
-        st.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(steps):
-            step()
-        e1.record(st)
-    e1.synchronize()
-    ms = e0.elapsed_time(e1)
-    assert bf.stream_status(st) == 0
-    calls = steps * len(weights)
+            serial_step()
+            pipelined_step()
+    torch.cuda.synchronize(dev)
+    ms_serial = timed(serial_step)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s_cmp):
+        pipelined_step()
+    with torch.cuda.stream(s_cmp):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    ms = timed(g.replay)
+    assert bf.stream_status(s_cmp) == 0
+    # every call's output reached the host
+    want = d_c[R - 1].cpu()
+    assert torch.equal(h_c[R - 1], want) and torch.equal(h_c[0], d_c[0].cpu())
+    del g
+    calls = steps * R
     return {"value": round(m * calls / (ms / 1e3), 1), "unit": "tokens/s",
-            "h2d_bytes_per_step": len(weights) * m * k * 2, "d2h_bytes_per_step": len(weights) * m * n * 2,
-            "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps,
-            "path": "pinned host A -> cudaMemcpyAsync -> busfill_gemm_* (C ABI via ctypes) -> pinned host C"}
+            "h2d_bytes_per_step": R * m * k * 2, "d2h_bytes_per_step": R * m * n * 2,
+            "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps, "calls_per_step": R,
+            "path": "pinned host A -> cudaMemcpyAsync (stream 2) -> busfill_gemm_* (C ABI via ctypes, stream 1) -> "
+                    "cudaMemcpyAsync (stream 3) -> pinned host C; one step's calls captured as a CUDA graph",
+            "eager_serial": {"value": round(m * calls / (ms_serial / 1e3), 1), "unit": "tokens/s",
+                             "us_per_call": round(ms_serial * 1e3 / calls, 3),
+                             "path": "the same calls from Python, one stream, no graph"}}
 
 
 def e2e_tp(torch, bf, tp, dev, weights, a, args, n_total, steps, space=None):
