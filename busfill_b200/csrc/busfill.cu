@@ -275,17 +275,23 @@ struct DecodeSchedule {
   int nclusters = 1;  // clusters in the grid
 };
 
-// Pick the K split c (1..max_cluster) with the shortest estimated weight-streaming time:
-// each active CTA moves at most kSmGBs (one SM's TMA rate on 144-byte weight
-// rows, measured on B200) and all of them together at most kHbmGBs; a cluster
-// takes ceil(T / G) tiles of `segs` x ceil(S / c) units each (segs = 2 for
-// SwiGLU gate/up pairs). Ties go to the smaller c.
+// Pick the K split c (1..max_cluster) with the shortest estimated time. A
+// cluster takes R = ceil(T / G) tiles in turn, each `segs` x ceil(S / c)
+// units (segs = 2 for SwiGLU gate/up pairs), so a CTA runs U = R x segs x
+// ceil(S / c) units. The estimate, fitted to CUDA-event times of Q4_K GEMMs
+// on B200 (M = 1 and 32; N, K in {5120, 8192, 10240, 17408}; every c):
+//   t = 7.2 us + 0.51 us x U + 4 us x (R - 1)
+// A unit costs ~0.5 us once the dequant pipeline runs, whatever the K split;
+// a launch costs ~7 us (set-up, the first boxes, the last tile's reduction
+// and exit); every further round of tiles adds a drain and refill of the
+// pipeline and a cluster reduction (N = 10240, K = 5120, M = 32: 15.5 us as
+// 80 one-CTA tiles, 18.3 us as two rounds of 3-CTA clusters; a bandwidth-only
+// model preferred the latter). Ties go to the smaller c.
 template <WFmt FMT, int NB, typename OutT>
 DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count, int segs) {
-  constexpr double kSmGBs = 57.0;
-  constexpr double kHbmGBs = 6500.0;
+  constexpr double kLaunchUs = 7.2, kUnitUs = 0.51, kRoundUs = 4.0;
   DecodeSchedule best;
-  double best_ns = 1e300;
+  double best_us = 1e300;
   const int forced = g_force_ksplit.load();
   const int cmax = std::min(max_cluster<NB>(), S);
   for (int c = 1; c <= cmax; ++c) {
@@ -295,10 +301,9 @@ DecodeSchedule choose_schedule(int dev, int T, int S, int sm_count, int segs) {
     if (ncl < 1) continue;
     const long long rounds = (T + ncl - 1) / ncl;
     const long long units = rounds * segs * ((S + c - 1) / c);
-    const double rate = std::min(kSmGBs, kHbmGBs / (double)(ncl * c));
-    const double ns = (double)units * wstage_bytes<FMT>() / rate;
-    if (ns < best_ns * 0.999) {
-      best_ns = ns;
+    const double us = kLaunchUs + kUnitUs * (double)units + kRoundUs * (double)(rounds - 1);
+    if (us < best_us - 1e-9) {
+      best_us = us;
       best.csize = c;
       best.nclusters = ncl;
     }
