@@ -21,7 +21,7 @@ __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q5k", "gemm_q6k", "repack_q6k",
     "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
-    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "uses_prefill", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -135,6 +135,12 @@ def set_ksplit(csize: int) -> None:
 def uses_prefill(m: int, n: int, k: int) -> bool:
     """True if a GEMM of m batch rows, n output columns and depth k runs the prefill kernel."""
     return _lib().busfill_gemm_kernel_for(int(m), int(n), int(k)) == 1
+
+
+def set_exact_kquant(on: bool) -> None:
+    """Q4_K / Q5_K GEMMs build the exact fp16_rn(fp32 w) operand (the CPU
+    dequant's bits) instead of the faster two-rounding fp16 chain."""
+    _check(_lib().busfill_set_option(4, 1 if on else 0), "busfill_set_option")
 
 
 def set_prefill_min_m(m: int) -> None:

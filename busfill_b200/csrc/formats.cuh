@@ -17,6 +17,12 @@
 //   exponent byte 0x64: 1024 + q), hsub2 by 1056 is exact, hmul2 rounds. Two
 //   fp16 roundings per weight; the bit-exact fp16 dequant is
 //   busfill_dequant_q6k.
+//   Q4KX / Q5KX (the exact option): the Q4_K / Q5_K operand computed as the
+//   oracle and llama.cpp's CPU dequant do, fp16_rn(fp32(q * d*sc - dmin*m)):
+//   q exact in fp32 (the byte under the exponent byte 0x4B, minus 2^23),
+//   d*sc and dmin*m exact in fp32, one fma (the product is exact, so one
+//   rounding, as the oracle's multiply then subtract), one rounding to fp16.
+//   About twice the integer and float instructions of the fp16 chain.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -34,7 +40,11 @@ namespace busfill {
 // block bodies (ql, qh, scales) per row and a plane of the blocks' fp16 d,
 // block-major [K/256][N] (210-byte rows have no 16-byte row stride, which the
 // tensor-memory-access copies need, unless K is a multiple of 2048).
-enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3, Q6K = 4 };
+// Q4KX / Q5KX: the Q4_K / Q5_K layouts with the exact fp32 operand.
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3, Q6K = 4, Q4KX = 5, Q5KX = 6 };
+
+// The stored layout of a format (the exact variants share their format's).
+constexpr WFmt layout_of(WFmt f) { return f == WFmt::Q4KX ? WFmt::Q4K : f == WFmt::Q5KX ? WFmt::Q5K : f; }
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
 constexpr int kUnitK = 256;          // K per unit
@@ -52,7 +62,8 @@ constexpr bool aos_rows() { return F != WFmt::Q4_0; }
 // plane; Q6_K: its block body).
 template <WFmt F>
 constexpr int unit_row_bytes() {
-  return F == WFmt::Q5K ? kQ5KBlockBytes : F == WFmt::Q6K ? kQ6KBodyBytes : F == WFmt::Q4_0 ? 128 : kQ4KBlockBytes;
+  constexpr WFmt L = layout_of(F);
+  return L == WFmt::Q5K ? kQ5KBlockBytes : L == WFmt::Q6K ? kQ6KBodyBytes : L == WFmt::Q4_0 ? 128 : kQ4KBlockBytes;
 }
 // Bytes per row and unit of the format's second plane, which a weight stage
 // holds after the rows of the unit (Q4_0: 8 fp16 block scales; Q6_K: fp16 d).
@@ -220,6 +231,49 @@ __device__ __forceinline__ void dequant_q6k_chunk(const uint8_t* qlp, const uint
   }
 }
 
+// Exact operand pairs: `vals` holds four byte values q (0..63), elements
+// e .. e+3 of one sub-block; writes fp16_rn(fp32(q * d1 + nm1)) for them as
+// two fp16 pairs. q becomes exact in fp32 as 2^23 + q (the byte under the
+// exponent byte 0x4B) minus 2^23; q * d1 is exact in fp32 (d1 = d * sc has at
+// most 17 significant bits, q 6), so the fma rounds once, like the oracle's
+// product followed by a subtraction.
+__device__ __forceinline__ void exact_k_bytes(uint32_t vals, float d1, float nm1, uint32_t* out2) {
+  float f[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(prmt(vals, 0x4B000000u, 0x7550u + (uint32_t)i)) - 8388608.0f;
+  out2[0] = h2_as_u32(__floats2half2_rn(fmaf(f[0], d1, nm1), fmaf(f[1], d1, nm1)));
+  out2[1] = h2_as_u32(__floats2half2_rn(fmaf(f[2], d1, nm1), fmaf(f[3], d1, nm1)));
+}
+
+// Q4_K, exact: the chunk's 32 qs bytes as in dequant_q4k_chunk; d1 / nm1 =
+// fp32 d*sc and -dmin*m of sub-blocks 2cc (lo) and 2cc+1 (hi).
+__device__ __forceinline__ void dequant_q4k_chunk_exact(const uint4 q0, const uint4 q1, float d1_lo, float nm1_lo,
+                                                        float d1_hi, float nm1_hi, uint32_t* out) {
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    exact_k_bytes(w[i] & 0x0F0F0F0Fu, d1_lo, nm1_lo, out + 2 * i);
+    exact_k_bytes((w[i] >> 4) & 0x0F0F0F0Fu, d1_hi, nm1_hi, out + 16 + 2 * i);
+  }
+}
+
+// Q5_K, exact: as dequant_q5k_chunk (whole 5-bit bytes), then exact_k_bytes.
+template <int CC>
+__device__ __forceinline__ void dequant_q5k_chunk_exact(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1,
+                                                        float d1_lo, float nm1_lo, float d1_hi, float nm1_hi,
+                                                        uint32_t* out) {
+  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  constexpr int bl = 2 * CC, bh = 2 * CC + 1;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t fl = (bl <= 4 ? hw[i] << (4 - bl) : hw[i] >> (bl - 4)) & 0x10101010u;
+    const uint32_t fh = (bh <= 4 ? hw[i] << (4 - bh) : hw[i] >> (bh - 4)) & 0x10101010u;
+    exact_k_bytes(lop3_and_or(w[i], 0x0F0F0F0Fu, fl), d1_lo, nm1_lo, out + 2 * i);
+    exact_k_bytes(lop3_and_or(w[i] >> 4, 0x0F0F0F0Fu, fh), d1_hi, nm1_hi, out + 16 + 2 * i);
+  }
+}
+
 template <typename OutT>
 __device__ __forceinline__ OutT to_out(float v);
 template <>
@@ -240,7 +294,7 @@ template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
 __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* aux, int r,
                                                  uint32_t a_slot) {
   static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
-  if constexpr (FMT == WFmt::Q4K) {
+  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4KX) {
     constexpr int kRow = unit_row_bytes<FMT>();
     // this row's block header: d, dmin and the 6-bit scales/mins of its
     // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
@@ -259,22 +313,24 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
       const uint32_t mw = cc < 2 ? m_lo : m_hi;
       constexpr int sh = 16 * (cc & 1);
-      const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
-      const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
-      const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
-      const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
+      const float d1l = d * (float)((scw >> sh) & 0xFFu), nm1l = -dmin * (float)((mw >> sh) & 0xFFu);
+      const float d1h = d * (float)((scw >> (sh + 8)) & 0xFFu), nm1h = -dmin * (float)((mw >> (sh + 8)) & 0xFFu);
       uint32_t P[32];
       const uint8_t* qs = stage + r * kRow + 16 + cc * 32;
       const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
       const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-      dequant_q4k_chunk(q0, q1, dsl, dml, dsh, dmh, P);
+      if constexpr (FMT == WFmt::Q4KX)
+        dequant_q4k_chunk_exact(q0, q1, d1l, nm1l, d1h, nm1h, P);
+      else
+        dequant_q4k_chunk(q0, q1, __float2half2_rn(d1l), __float2half2_rn(nm1l), __float2half2_rn(d1h),
+                          __float2half2_rn(nm1h), P);
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     };
     if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
     if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
     if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
     if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
-  } else if constexpr (FMT == WFmt::Q5K) {
+  } else if constexpr (FMT == WFmt::Q5K || FMT == WFmt::Q5KX) {
     // header as Q4_K; qh at 16, qs at 48
     const uint8_t* row = stage + r * kQ5KBlockBytes;
     const uint4 hdr = *reinterpret_cast<const uint4*>(row);
@@ -289,16 +345,18 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
       const uint32_t mw = cc < 2 ? m_lo : m_hi;
       constexpr int sh = 16 * (cc & 1);
-      const __half2 dsl = __float2half2_rn(d * (float)((scw >> sh) & 0xFFu));
-      const __half2 dml = __float2half2_rn(-dmin * (float)((mw >> sh) & 0xFFu));
-      const __half2 dsh = __float2half2_rn(d * (float)((scw >> (sh + 8)) & 0xFFu));
-      const __half2 dmh = __float2half2_rn(-dmin * (float)((mw >> (sh + 8)) & 0xFFu));
+      const float d1l = d * (float)((scw >> sh) & 0xFFu), nm1l = -dmin * (float)((mw >> sh) & 0xFFu);
+      const float d1h = d * (float)((scw >> (sh + 8)) & 0xFFu), nm1h = -dmin * (float)((mw >> (sh + 8)) & 0xFFu);
       const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
       const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
       const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
       const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
       uint32_t P[32];
-      dequant_q5k_chunk<cc>(q0, q1, h0, h1, dsl, dml, dsh, dmh, P);
+      if constexpr (FMT == WFmt::Q5KX)
+        dequant_q5k_chunk_exact<cc>(q0, q1, h0, h1, d1l, nm1l, d1h, nm1h, P);
+      else
+        dequant_q5k_chunk<cc>(q0, q1, h0, h1, __float2half2_rn(d1l), __float2half2_rn(nm1l), __float2half2_rn(d1h),
+                              __float2half2_rn(nm1h), P);
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     };
     if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
@@ -354,8 +412,8 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
     const uint8_t* wrow = stage + r * 128;
     const uint32_t sw = (uint32_t)(r & 7);  // TMA 128-byte swizzle: 16-B chunk ^= row % 8
     const uint4 dd = *reinterpret_cast<const uint4*>(aux + r * 16);  // 8 block scales
-#pragma unroll 1
-    for (int cc = C0; cc < C1; ++cc) {
+    auto chunk = [&](auto cc_tag) {
+      constexpr int cc = decltype(cc_tag)::value;
       uint32_t P[32];
       const uint4 b0 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc)) ^ sw) << 4));
       const uint4 b1 = *reinterpret_cast<const uint4*>(wrow + ((((uint32_t)(2 * cc + 1)) ^ sw) << 4));
@@ -363,7 +421,11 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       dequant_q4_0_block(b0, __low2half2(d01), P);
       dequant_q4_0_block(b1, __high2half2(d01), P + 16);
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
-    }
+    };
+    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
+    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
+    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
+    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
   }
 }
 

@@ -285,10 +285,17 @@ BUSFILL_API int busfill_version(void);
  *     items of 256 weight rows x 128 batch rows for SwiGLU pairs and
  *     busfill_gemm_q4k_noalloc, which take whole items. A tuning and test
  *     knob; results agree within the accuracy gate.
+ *   BUSFILL_OPT_EXACT_KQUANT: 1 makes busfill_gemm_q4k and busfill_gemm_q5k
+ *     build their fp16 weight operand exactly as the CPU dequant
+ *     (fp16_rn(fp32(d*sc*q - dmin*m)), the bit-exact busfill_dequant_q4k /
+ *     _q5k) instead of the default fp16 chain (two fp16 roundings, ~3e-4
+ *     relative), at about twice the dequant instructions; 0 (default) off.
+ *     The SwiGLU, gathered and no-allocation entry points keep the chain.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
 #define BUSFILL_OPT_PREFILL_MIN_M 3
+#define BUSFILL_OPT_EXACT_KQUANT 4
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,
