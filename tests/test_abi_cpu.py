@@ -38,6 +38,8 @@ def test_set_option_rejects_unknown():
     lib = bf.load_library()
     assert lib.busfill_set_option(99, 1) == -1
     assert lib.busfill_set_option(1, 1) == 0
+    assert lib.busfill_set_option(4, 2) == -1          # the exact option is 0 or 1
+    assert lib.busfill_set_option(4, 1) == 0 and lib.busfill_set_option(4, 0) == 0
 
 
 def test_null_pointer_rejected_before_any_device_work():
