@@ -189,8 +189,10 @@ BUSFILL_API int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_
  * cudaMalloc would stall the device.  This entry point keeps its scratch
  * (the error word and the first failure record) in one 256-byte array
  * compiled into the library, which every GPU that loads the library holds
- * until the process exits.  The split-K partial sums live in shared memory,
- * so no problem size needs more scratch.  The caller still passes the inputs
+ * until the process exits.  The decode kernel's split-K partial sums live in
+ * shared memory, and large batches here take whole work items per SM (no
+ * stream-K workspace), so no problem size needs more scratch.  The caller
+ * still passes the inputs
  * and the output; arguments, layout and results are those of
  * busfill_gemm_q4k.
  *
