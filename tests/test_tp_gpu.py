@@ -1,5 +1,6 @@
 """Column split across GPUs through the C ABI and NCCL (busfill_b200/tp.py).
-Needs two or more GPUs; each rank is a spawned process on its own GPU."""
+Each rank is a spawned process on its own GPU; the multi-rank tests need two
+or more GPUs, the single-rank run of the gathered GEMMs one."""
 import os
 import socket
 
@@ -186,3 +187,25 @@ def test_gather_fused_into_epilogue(m):
         assert status == 0, (rank, status, runs)
         for errs in runs:
             assert all(e <= 1e-3 for e in errs), (rank, runs)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+@pytest.mark.parametrize("m", [8, 40])
+def test_gather_fused_single_rank(m):
+    """The gathered GEMMs in a process group of one: every peer store and
+    flag is the rank's own, and each consuming GEMM waits only on a GEMM
+    issued before it on the same stream (already resident when it starts),
+    so the whole epilogue-gather path, its tile counters, its call counting
+    and graph replays run on a single GPU."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_worker_gather, args=(0, 1, _free_port(), q, m))
+    p.start()
+    rank, status, runs = q.get(timeout=240)
+    p.join(timeout=60)
+    assert p.exitcode == 0
+    assert status == 0, (rank, status, runs)
+    for errs in runs:
+        assert all(e <= 1e-3 for e in errs), runs
