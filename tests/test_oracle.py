@@ -223,7 +223,7 @@ def test_gate_rejects_nan_and_large_error():
     assert not orc.gate_ok(far, cref)
 
 
-def test_algorithmic_bytes_matches_survey_figures():
+def test_algorithmic_bytes_match_hand_computed_figures():
     # 4.5-bit weights + fp16 A + fp16 C at K=N=5120
     assert orc.algorithmic_bytes(1, 5120, 5120) == 14_766_080
     assert orc.algorithmic_bytes(8, 5120, 5120) == 14_909_440
