@@ -204,6 +204,33 @@ __device__ __forceinline__ UnitInfo unit_info(int i, int len, int sb0, int g, in
   return r;
 }
 
+// Transposes, in each group of 8 lanes, the 8x8 blocks of the NB values the
+// lanes hold: before, lane j of a group holds batch rows 0..NB-1 of weight
+// row n0 + j; after, acc[8b + i] of lane j holds batch row 8b + j of weight
+// row n0 + i. Three butterfly stages (lane distance 4, 2, 1); in each, the
+// lanes of a pair swap the halves the other needs. All 32 lanes take part.
+template <int NB>
+__device__ __forceinline__ void transpose_8x8_blocks(float* acc, int lane) {
+  const int j = lane & 7;
+#pragma unroll
+  for (int b = 0; b < NB / 8; ++b) {
+    float* v = acc + 8 * b;
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i & m) continue;
+        const bool hi = (j & m) != 0;
+        const float y = __shfl_xor_sync(0xffffffffu, hi ? v[i] : v[i | m], m);
+        if (hi)
+          v[i] = y;
+        else
+          v[i | m] = y;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------
@@ -566,10 +593,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (t < p.M) Cq[(size_t)t * p.gather.ldc] = to_out<OutT>(acc[t]);
           }
         }
-      } else if (ok && n < p.N) {
+      } else if (ok) {
+        if (sizeof(OutT) == 2 && (p.N & 7) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0) {
+          // one 16-byte store of 8 consecutive outputs per batch row instead of
+          // NB 2-byte stores strided by N (the store tail shortens the launch)
+          transpose_8x8_blocks<NB>(acc, lane);
+          const int n0 = tile * kTileRows + (warp & 3) * 32 + (lane & ~7);   // the lane group's 8 rows
 #pragma unroll
-        for (int t = 0; t < NB; ++t)
-          if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
+          for (int b = 0; b < NB / 8; ++b) {
+            const int t = 8 * b + (lane & 7);
+            if (t < p.M && n0 < p.N) {   // N % 8 == 0: the group's 8 rows are all in range
+              uint4 v;
+              v.x = h2_as_u32(__floats2half2_rn(acc[8 * b], acc[8 * b + 1]));
+              v.y = h2_as_u32(__floats2half2_rn(acc[8 * b + 2], acc[8 * b + 3]));
+              v.z = h2_as_u32(__floats2half2_rn(acc[8 * b + 4], acc[8 * b + 5]));
+              v.w = h2_as_u32(__floats2half2_rn(acc[8 * b + 6], acc[8 * b + 7]));
+              *reinterpret_cast<uint4*>(C + (size_t)t * p.N + n0) = v;
+            }
+          }
+        } else if (n < p.N) {
+#pragma unroll
+          for (int t = 0; t < NB; ++t)
+            if (t < p.M) C[(size_t)t * p.N + n] = to_out<OutT>(acc[t]);
+        }
       }
     };
 

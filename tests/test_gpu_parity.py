@@ -293,6 +293,26 @@ def test_no_writes_outside_output():
     assert_gates(out, orc.gemm_ref(a, orc.dequant_q4k_f32(blocks, k)))
 
 
+@pytest.mark.parametrize("m,n,k,shift", [(20, 130, 512, 0), (32, 256, 1024, 1), (9, 640, 2048, 0)])
+def test_decode_output_store_paths(m, n, k, shift):
+    """The decode epilogue writes 8 consecutive outputs per 16-byte store when
+    N % 8 == 0 and C is 16-byte aligned, one output per store otherwise
+    (N = 130; C one element past an aligned address); every case against the
+    oracle, nothing written outside C."""
+    bf.set_prefill_min_m(10 ** 6)
+    try:
+        blocks = orc.gen_q4k(n, k, seed=m + n)
+        a = orc.gen_activations(m, k, seed=m + k)
+        big = torch.full((m * n + shift + 8,), -7.0, dtype=torch.float16, device=DEV)
+        out = big[shift:shift + m * n].view(m, n)
+        bf.gemm_q4k(cu(blocks), cu(a), out=out)
+        check_status()
+    finally:
+        bf.set_prefill_min_m(0)
+    assert torch.all(big[:shift] == -7.0) and torch.all(big[shift + m * n:] == -7.0)
+    assert_gates(out, orc.gemm_ref(a, orc.dequant_q4k_f32(blocks, k)))
+
+
 def test_deterministic_bitwise():
     m, n, k = 32, 640, 5120     # split-K tiles: fix-up order must be fixed
     blocks = cu(orc.gen_q4k(n, k, seed=51))
