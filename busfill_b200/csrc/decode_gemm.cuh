@@ -583,8 +583,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait_prerequisites();  // C may still be read by the previous kernel
       if (GA) {
-        // this rank's slice into every rank's full output (peer stores over NVLink)
-        if (ok && n < p.N) {
+        // this rank's slice into every rank's full output (peer stores over
+        // NVLink), 8 consecutive outputs per 16-byte store where every output
+        // row is 16-byte aligned (as for the local store below)
+        bool wide = sizeof(OutT) == 2 && ((p.gather.ldc | p.gather.col_off) & 7) == 0;
+        for (int q = 0; q < p.gather.npeers; ++q)
+          wide = wide && (reinterpret_cast<uintptr_t>(p.gather.out[q]) & 15) == 0;
+        if (ok && wide) {
+          transpose_8x8_blocks<NB>(acc, lane);
+          const int n0 = tile * kTileRows + (warp & 3) * 32 + (lane & ~7);   // the lane group's 8 rows
+          uint4 v[NB / 8];
+#pragma unroll
+          for (int b = 0; b < NB / 8; ++b) {
+            v[b].x = h2_as_u32(__floats2half2_rn(acc[8 * b], acc[8 * b + 1]));
+            v[b].y = h2_as_u32(__floats2half2_rn(acc[8 * b + 2], acc[8 * b + 3]));
+            v[b].z = h2_as_u32(__floats2half2_rn(acc[8 * b + 4], acc[8 * b + 5]));
+            v[b].w = h2_as_u32(__floats2half2_rn(acc[8 * b + 6], acc[8 * b + 7]));
+          }
+          if (n0 < p.N) {   // the local shard width is a multiple of 8 here (ldc and col_off are)
+#pragma unroll 1
+            for (int q = 0; q < p.gather.npeers; ++q) {
+              OutT* Cq = reinterpret_cast<OutT*>(p.gather.out[q]) + p.gather.col_off + n0;
+#pragma unroll
+              for (int b = 0; b < NB / 8; ++b) {
+                const int t = 8 * b + (lane & 7);
+                if (t < p.M) *reinterpret_cast<uint4*>(Cq + (size_t)t * p.gather.ldc) = v[b];
+              }
+            }
+          }
+        } else if (ok && n < p.N) {
 #pragma unroll 1
           for (int q = 0; q < p.gather.npeers; ++q) {
             OutT* Cq = reinterpret_cast<OutT*>(p.gather.out[q]) + p.gather.col_off + n;
