@@ -46,12 +46,11 @@
 //
 // Work split: a tile of 128 weight rows is split along K over the c CTAs of
 // a thread-block cluster (rank k takes units [k*S/c, (k+1)*S/c) of every
-// tile); cluster g of G takes tiles g, g+G, g+2G, ... The host picks c so
-// that the CTAs that stream weights have the most bandwidth each. At the end
-// of each tile the non-zero ranks push their fp32 partial sums into rank 0's
-// shared memory (st.async with complete_tx on rank 0's barrier), and rank 0
-// adds them in rank order (deterministic) and writes C. No global scratch, no
-// atomics.
+// tile); cluster g of G takes tiles g, g+G, g+2G, ... The host picks c from a
+// cost model of measured launches. At the end of each tile the non-zero ranks
+// move their fp32 partial sums into rank 0's shared memory (staged, then one
+// bulk copy each, completing rank 0's barrier), and rank 0 adds them in rank
+// order (deterministic) and writes C. No global scratch, no atomics.
 //
 // Every wait is bounded (ptx.cuh: kWaitTimeoutNs): a kernel that cannot make
 // progress records an error bit and winds down instead of hanging the GPU.
@@ -509,10 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float gate[SW ? NB : 1];  // SwiGLU: the reduced gate tile, held until its up tile
 
     // Finish tile `tile` (this CTA's segment `seg`). One CTA per tile: write C.
-    // Otherwise ranks k > 0 push their fp32 partial into rank 0's shared
-    // memory with st.async, whose bytes complete rank 0's bRedFull barrier (no
-    // fence, no separate signal: every release or remote round trip costs
-    // ~0.5 us on B200); rank 0 adds the partials in rank order and writes C.
+    // Otherwise ranks k > 0 stage their fp32 partial in their own shared
+    // memory and move it into rank 0's with one bulk copy, whose bytes
+    // complete rank 0's bRedFull barrier (no separate signal: every release
+    // or remote round trip costs ~0.5 us on B200); rank 0 adds the partials
+    // in rank order and writes C.
     // Receive layout: [rank-1][row][NB] fp32, 16-byte chunks swizzled by row.
     // After the last tile each CTA arrives on the cluster's teardown barrier
     // as soon as it is done with distributed shared memory (ranks k > 0 once
@@ -529,15 +529,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         cl_waited = true;
       }
       if (csize > 1 && crank != 0) {
-        // rank 0's buffer is free once it has read the previous segment
+        // rank 0's buffer, and this CTA's staging copy, are free once rank 0
+        // has read the previous segment
         if (seg > 0) warp_wait(BAR(L::bRedEmpty), (uint32_t)((seg - 1) & 1), true);
-        const uint32_t row = sbase + L::kRedOff + (uint32_t)((crank - 1) * L::kRedRankBytes + r * NB * 4);
-        const uint32_t dst = mapa_shared(row, 0);
-        const uint32_t dst_bar = mapa_shared(BAR(L::bRedFull), 0);
+        // Stage the partial in this CTA's own slot of the receive area (ranks
+        // k > 0 receive nothing), in the layout rank 0 reads, then move the
+        // whole slot with one bulk copy that completes rank 0's barrier: one
+        // transfer instead of a 16-byte remote store per thread and chunk.
+        const uint32_t slot = sbase + L::kRedOff + (uint32_t)((crank - 1) * L::kRedRankBytes);
+        const uint32_t row = slot + (uint32_t)(r * NB * 4);
 #pragma unroll
         for (int j = 0; j < kChunks; ++j)
-          st_async_f4(dst + (uint32_t)((j ^ swz) << 4), acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3],
-                      dst_bar);
+          st_shared_f4(row + (uint32_t)((j ^ swz) << 4), acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        fence_proxy_async_shared();
+        named_bar_sync(2, 128);   // the 4 epilogue warps have staged their rows
+        if (warp == kWarpEpilogue0 && lane == 0)
+          bulk_copy_to_cluster(mapa_shared(slot, 0), slot, (uint32_t)L::kRedRankBytes, mapa_shared(BAR(L::bRedFull), 0));
         if (seg == ntiles - 1) {
           __syncwarp();
           cluster_arrive();

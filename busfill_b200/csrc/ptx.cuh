@@ -163,6 +163,23 @@ __device__ __forceinline__ void st_async_f4(uint32_t cluster_addr, float a, floa
                "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
                : "memory");
 }
+// Bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from
+// this CTA's shared memory into another CTA's of the cluster (no multicast);
+// the bytes complete that CTA's mbarrier (complete_tx), which is also the only
+// completion: the source stays untouched until the receiver says it has read it.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, uint32_t src_cta, uint32_t bytes,
+                                                     uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster),
+               "r"(src_cta), "r"(bytes), "r"(bar_cluster)
+               : "memory");
+}
+// Make this thread's generic-proxy shared-memory writes visible to later
+// asynchronous-proxy operations (bulk copies) of the CTA.
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
 // all threads of all CTAs of the cluster (converged warps)
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
