@@ -426,14 +426,14 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
     cases = [("q4k", 1, 5120, 5120), ("q4k", 8, 5120, 5120), ("q4k", 32, 5120, 5120), ("q4k", 32, 17408, 5120),
              ("q4_0", 1, 5120, 5120), ("q4_0", 8, 5120, 5120), ("q4_0", 32, 5120, 5120),
              ("q4_0_ggml", 32, 5120, 5120), ("q5k", 32, 5120, 5120), ("q6k", 32, 5120, 5120),
-             ("q4k_swiglu", 32, 17408, 5120), ("q4k_exact", 32, 5120, 5120)]
+             ("q4k_swiglu", 32, 17408, 5120)]
     gen = torch.Generator(device=dev)
     gen.manual_seed(args.seed + 99)
     for fmt, m, n, k in cases:
         wbytes = n * k * {"q5k": 22, "q6k": 26.25}.get(fmt, 18) // 32 * (2 if fmt == "q4k_swiglu" else 1)
         wbytes = int(wbytes)
         R = max(2, math.ceil(2.2 * l2 / wbytes))
-        if fmt in ("q4k", "q4k_exact"):
+        if fmt == "q4k":
             w0 = make_q4k_weights(torch, n, k, gen, dev)
             ws = [w0] + [w0.clone() for _ in range(R - 1)]
         elif fmt == "q4k_swiglu":
@@ -455,11 +455,9 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
         c = torch.empty((m, n), dtype=torch.float16, device=dev)
         st = torch.cuda.Stream(device=dev)
 
-        bf.set_exact_kquant(fmt == "q4k_exact")
-
         def step():
             for w in ws:
-                if fmt in ("q4k", "q4k_exact"):
+                if fmt == "q4k":
                     bf.gemm_q4k(w, a, out=c, stream=st)
                 elif fmt == "q4k_swiglu":
                     bf.gemm_q4k_swiglu(w[0], w[1], a, out=c, stream=st)
@@ -482,7 +480,6 @@ def sweep(torch, bf, dev, l2, hbm_peak, args):
             for _ in range(nsteps):
                 step()
         ms = _time_on(torch, g, st)
-        bf.set_exact_kquant(False)
         assert bf.stream_status(st) == 0
         us = ms * 1e3 / (nsteps * R)
         gbs = (wbytes + 2 * m * k + 2 * m * n) / (us * 1e-6) / 1e9

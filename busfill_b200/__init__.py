@@ -138,8 +138,9 @@ def uses_prefill(m: int, n: int, k: int) -> bool:
 
 
 def set_exact_kquant(on: bool) -> None:
-    """Q4_K / Q5_K GEMMs build the exact fp16_rn(fp32 w) operand (the CPU
-    dequant's bits) instead of the faster two-rounding fp16 chain."""
+    """BUSFILL_OPT_EXACT_KQUANT, kept for callers that set it: every K-quant
+    GEMM operand is already fp16_rn(fp32 w), the CPU dequant's bits, so the
+    option changes nothing."""
     _check(_lib().busfill_set_option(4, 1 if on else 0), "busfill_set_option")
 
 

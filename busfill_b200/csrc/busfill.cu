@@ -54,8 +54,6 @@ std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 constexpr int kStreamKMinM = 64;
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
-// 1: busfill_gemm_q4k / _q5k build the exact fp16_rn(fp32 w) operand (WFmt::Q4KX / Q5KX)
-std::atomic<int> g_exact_kquant{0};
 
 bool use_prefill(int M, int N, int K, bool swiglu = false, bool stream_k = false) {
   const int forced = g_prefill_min_m.load();
@@ -711,9 +709,8 @@ int busfill_set_option(int option, int value) {
     return BUSFILL_OK;
   }
   if (option == BUSFILL_OPT_EXACT_KQUANT) {
-    if (value != 0 && value != 1) return BUSFILL_ERR_INVALID_ARG;
-    g_exact_kquant.store(value);
-    return BUSFILL_OK;
+    // accepted for compatibility: every K-quant operand is exact
+    return value == 0 || value == 1 ? BUSFILL_OK : BUSFILL_ERR_INVALID_ARG;
   }
   return BUSFILL_ERR_INVALID_ARG;
 }
@@ -724,8 +721,6 @@ int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const uint16_t* a, 
 }
 
 int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
-  if (g_exact_kquant.load())
-    return gemm_impl<WFmt::Q4KX, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
   return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -736,8 +731,6 @@ int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const ui
 }
 
 int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
-  if (g_exact_kquant.load())
-    return gemm_impl<WFmt::Q5KX, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
   return gemm_impl<WFmt::Q5K, __half>(blocks, nullptr, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
 

@@ -139,7 +139,7 @@ constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
 // (a group that skipped the other group's phase of a stage could see that
 // stale phase as complete: mbarrier waits only tell parities apart).
 template <int NB, WFmt FMT>
-constexpr int w_stages() { return layout_of(FMT) == WFmt::Q5K || FMT == WFmt::Q6K ? 4 : 6; }  // Q5_K / Q6_K: 22 / 26 KB
+constexpr int w_stages() { return FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 4 : 6; }  // Q5_K / Q6_K: 22 / 26 KB
 
 // Activation ring depth (one unit per stage), separate from the TMEM operand
 // slots so that a unit's activations are requested several units ahead: a

@@ -1,28 +1,26 @@
 // Weight formats of the quantized GEMMs and the per-row dequant of one unit
 // (128 weight rows x 256 K) into a tcgen05 A operand in tensor memory.
 //
-// Numerics (fp32 accumulation of fp16 products in every format):
-//   Q4_0: operand fp16_rn((q-8)*d), bit-identical to the reference dequant
-//   (kernels/busfill_v0.cu:74-81): the lop3 magic bias 0x6400 gives the exact
-//   fp16 1024+q, hsub2 by 1032 is exact, hmul2 by d rounds once.
+// Numerics (fp32 accumulation of fp16 products in every format). The fp16
+// operand of every format is bit-identical to the CPU dequant (the oracle):
+//   Q4_0: fp16_rn((q-8)*d), the reference dequant (kernels/busfill_v0.cu:
+//   74-81): the lop3 magic bias 0x6400 gives the exact fp16 1024+q, hsub2 by
+//   1032 is exact, hmul2 by d rounds once.
 //   Q4_0G (llama.cpp block_q4_0 rows): the same rule; high nibbles go
 //   through the bias 0x5400 (64 + q) and hsub2 by 72.
-//   Q4_K: operand q*ds - dm in one hfma2, with ds = fp16_rn(d*sc) and dm =
-//   fp16_rn(dmin*m) per 32-value sub-block and q exact (low nibbles via the
-//   bias 0x6400 = 1024 + q, high nibbles via 0x5400, whose mantissa step is
-//   1/16, = 64 + q). Two fp16 roundings per weight (~3e-4 relative rms); the
-//   bit-exact fp16 dequant is busfill_dequant_q4k.
-//   Q6_K: operand (q-32)*ds with ds = fp16_rn(d*sc) per 16-value group; q is
-//   exact above the bias (a byte-permute writes each 6-bit q under the fp16
-//   exponent byte 0x64: 1024 + q), hsub2 by 1056 is exact, hmul2 rounds. Two
-//   fp16 roundings per weight; the bit-exact fp16 dequant is
-//   busfill_dequant_q6k.
-//   Q4KX / Q5KX (the exact option): the Q4_K / Q5_K operand computed as the
-//   oracle and llama.cpp's CPU dequant do, fp16_rn(fp32(q * d*sc - dmin*m)):
-//   q exact in fp32 (the byte under the exponent byte 0x4B, minus 2^23),
-//   d*sc and dmin*m exact in fp32, one fma (the product is exact, so one
-//   rounding, as the oracle's multiply then subtract), one rounding to fp16.
-//   About twice the integer and float instructions of the fp16 chain.
+//   Q4_K / Q5_K: fp16_rn(w32) with w32 = fp32(d*sc*q - dmin*m), the
+//   llama.cpp CPU order (d1 = d*sc and m1 = dmin*m exact in fp32, d1*q exact,
+//   one rounding of the subtraction). Steps, all exact but the last two:
+//   the byte-permute / lop3 magic bias gives fp16 B + q (B = 1024, or 64 for
+//   high nibbles, whose mantissa step is 1/16); hfma2(B + q, sc, -B*sc) =
+//   q*sc, an integer below 2048 and so exact in fp16 (q <= 31, sc <= 63);
+//   the sm_100 mixed-precision fma.rn.f32.f16(q*sc, d, -m1) multiplies two
+//   fp16 values exactly and rounds q*sc*d - m1 once to fp32 (= w32, since
+//   q*sc*d = d1*q); cvt.rn.f16x2.f32 rounds the pair to fp16.
+//   Q6_K: fp16_rn(fp32(d*sc) * (q-32)). fma.rn.f32.f16(1024 + q, d, -1056*d)
+//   = (q-32)*d exactly (16 significant bits), times sc in fp32 is exact too
+//   (at most 23 bits, the oracle's product is exact as well), then one
+//   rounding to fp16.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -40,11 +38,7 @@ namespace busfill {
 // block bodies (ql, qh, scales) per row and a plane of the blocks' fp16 d,
 // block-major [K/256][N] (210-byte rows have no 16-byte row stride, which the
 // tensor-memory-access copies need, unless K is a multiple of 2048).
-// Q4KX / Q5KX: the Q4_K / Q5_K layouts with the exact fp32 operand.
-enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3, Q6K = 4, Q4KX = 5, Q5KX = 6 };
-
-// The stored layout of a format (the exact variants share their format's).
-constexpr WFmt layout_of(WFmt f) { return f == WFmt::Q4KX ? WFmt::Q4K : f == WFmt::Q5KX ? WFmt::Q5K : f; }
+enum class WFmt : int { Q4_0 = 0, Q4K = 1, Q4_0G = 2, Q5K = 3, Q6K = 4 };
 
 constexpr int kTileRows = 128;       // weight rows per tile = MMA M
 constexpr int kUnitK = 256;          // K per unit
@@ -62,8 +56,7 @@ constexpr bool aos_rows() { return F != WFmt::Q4_0; }
 // plane; Q6_K: its block body).
 template <WFmt F>
 constexpr int unit_row_bytes() {
-  constexpr WFmt L = layout_of(F);
-  return L == WFmt::Q5K ? kQ5KBlockBytes : L == WFmt::Q6K ? kQ6KBodyBytes : L == WFmt::Q4_0 ? 128 : kQ4KBlockBytes;
+  return F == WFmt::Q5K ? kQ5KBlockBytes : F == WFmt::Q6K ? kQ6KBodyBytes : F == WFmt::Q4_0 ? 128 : kQ4KBlockBytes;
 }
 // Bytes per row and unit of the format's second plane, which a weight stage
 // holds after the rows of the unit (Q4_0: 8 fp16 block scales; Q6_K: fp16 d).
@@ -97,15 +90,37 @@ __device__ __forceinline__ void dequant_q4_0_block(const uint4 b, const __half2 
   }
 }
 
+// Per-sub-block constants of the exact Q4_K / Q5_K operand: sc2 = {sc, sc}
+// and nbsc2 = {-B*sc, -B*sc} in fp16 (exact: sc <= 63, B*sc <= 64512) for the
+// magic bias B of the value words, nm1 = -fp32(dmin)*m (exact in fp32).
+struct KSub {
+  __half2 sc2, nbsc2;
+  float nm1;
+};
+__device__ __forceinline__ KSub ksub(uint32_t sc, uint32_t m, float dmin, float bias) {
+  KSub k;
+  k.sc2 = __float2half2_rn((float)sc);
+  k.nbsc2 = __float2half2_rn(-bias * (float)sc);
+  k.nm1 = -dmin * (float)m;
+  return k;
+}
+
+// One operand pair of an exact K-quant sub-block from the fp16 pair {B + q0,
+// B + q1}: hfma2 gives q*sc exactly (an integer below 2048), the mixed fma
+// rounds q*sc*d - m1 once to fp32 (= w32), the pack rounds to fp16.
+__device__ __forceinline__ uint32_t k_exact_pair(uint32_t biased, const KSub& k, uint16_t d16) {
+  const uint32_t qs = h2_as_u32(__hfma2(u32_as_h2(biased), k.sc2, k.nbsc2));
+  float lo, hi;
+  fma_f16x2_f32(qs, d16, k.nm1, lo, hi);
+  return h2_as_u32(__floats2half2_rn(lo, hi));
+}
+
 // Q4_K, one 64-value chunk of a super-block: 32 bytes; byte l holds element l
 // of sub-block 2c (low nibble) and of sub-block 2c+1 (high nibble). Writes
-// q*ds - dm in one hfma2 per pair: out[0..15] = sub-block 2c (ds_lo, ndm_lo),
-// out[16..31] = sub-block 2c+1 (ds_hi, ndm_hi); ndm = -dm.
-__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, const __half2 ds_lo,
-                                                  const __half2 ndm_lo, const __half2 ds_hi, const __half2 ndm_hi,
-                                                  uint32_t* out) {
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
-  const __half2 k64 = __halves2half2(__ushort_as_half(0x5400), __ushort_as_half(0x5400));
+// fp16_rn(w32): out[0..15] = sub-block 2c (lo: bias 1024), out[16..31] =
+// sub-block 2c+1 (hi: bias 64); d16 = the block's fp16 d bits.
+__device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1, uint16_t d16, const KSub& lo,
+                                                  const KSub& hi, uint32_t* out) {
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -115,10 +130,10 @@ __device__ __forceinline__ void dequant_q4k_chunk(const uint4 q0, const uint4 q1
     const uint32_t l23 = lop3_and_or(t1, 0x000F000Fu, 0x64006400u);
     const uint32_t h01 = lop3_and_or(t0, 0x00F000F0u, 0x54005400u);  // {64 + q}: mantissa step 1/16
     const uint32_t h23 = lop3_and_or(t1, 0x00F000F0u, 0x54005400u);
-    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
-    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
-    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k64), ds_hi, ndm_hi));
-    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k64), ds_hi, ndm_hi));
+    out[2 * i] = k_exact_pair(l01, lo, d16);
+    out[2 * i + 1] = k_exact_pair(l23, lo, d16);
+    out[16 + 2 * i] = k_exact_pair(h01, hi, d16);
+    out[16 + 2 * i + 1] = k_exact_pair(h23, hi, d16);
   }
 }
 
@@ -170,12 +185,11 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 // of sub-block 2cc+1), h0/h1 the 32 qh bytes (bit G of byte l: the fifth bit
 // of element l of sub-block G). Each byte of a word is first made the whole
 // 5-bit value (nibble | fifth bit << 4); a byte-permute then sets each value
-// under the fp16 exponent byte 0x64, giving the exact fp16 1024 + q.
+// under the fp16 exponent byte 0x64, giving the exact fp16 1024 + q, and
+// k_exact_pair makes fp16_rn(w32) of it (both sub-blocks with bias 1024).
 template <int CC>
 __device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1,
-                                                  const __half2 ds_lo, const __half2 ndm_lo, const __half2 ds_hi,
-                                                  const __half2 ndm_hi, uint32_t* out) {
-  const __half2 k1024 = __halves2half2(__ushort_as_half(0x6400), __ushort_as_half(0x6400));
+                                                  uint16_t d16, const KSub& lo, const KSub& hi, uint32_t* out) {
   const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
   const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
   constexpr int bl = 2 * CC, bh = 2 * CC + 1;   // the fifth bits' positions in the qh bytes
@@ -187,12 +201,10 @@ __device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1
     const uint32_t fh = (bh <= 4 ? hw[i] << (4 - bh) : hw[i] >> (bh - 4)) & 0x10101010u;
     const uint32_t ql = lop3_and_or(w[i], 0x0F0F0F0Fu, fl);        // four 5-bit values, sub-block 2cc
     const uint32_t qh = lop3_and_or(w[i] >> 4, 0x0F0F0F0Fu, fh);   // sub-block 2cc+1
-    const uint32_t l01 = prmt(ql, 0x64u, 0x4140u), l23 = prmt(ql, 0x64u, 0x4342u);  // {1024 + q}
-    const uint32_t h01 = prmt(qh, 0x64u, 0x4140u), h23 = prmt(qh, 0x64u, 0x4342u);
-    out[2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l01), k1024), ds_lo, ndm_lo));
-    out[2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(l23), k1024), ds_lo, ndm_lo));
-    out[16 + 2 * i] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h01), k1024), ds_hi, ndm_hi));
-    out[16 + 2 * i + 1] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(h23), k1024), ds_hi, ndm_hi));
+    out[2 * i] = k_exact_pair(prmt(ql, 0x64u, 0x4140u), lo, d16);   // {1024 + q}
+    out[2 * i + 1] = k_exact_pair(prmt(ql, 0x64u, 0x4342u), lo, d16);
+    out[16 + 2 * i] = k_exact_pair(prmt(qh, 0x64u, 0x4140u), hi, d16);
+    out[16 + 2 * i + 1] = k_exact_pair(prmt(qh, 0x64u, 0x4342u), hi, d16);
   }
 }
 
@@ -201,13 +213,13 @@ __device__ __forceinline__ void dequant_q5k_chunk(const uint4 q0, const uint4 q1
 // qh[0..7] are its 32 qh bytes. Element l
 // of group jj (elements 32 jj + l of the chunk) has its low 4 bits in ql byte
 // 32 jj + l (low nibble for even chunks, high nibble for odd ones) and its
-// top 2 bits at bit 4 odd + 2 jj of qh byte l. ds[t]: fp16 d*sc of the
-// chunk's 16-value group t. Writes (q-32)*ds: out[16 jj + i] = elements
-// 32 jj + 2i, +1.
+// top 2 bits at bit 4 odd + 2 jj of qh byte l. scf[t]: the int8 scale of the
+// chunk's 16-value group t as fp32; d16 / nd1056 = the block's fp16 d bits
+// and -1056*d (exact in fp32). Writes fp16_rn(fp32(d*sc) * (q-32)):
+// out[16 jj + i] = elements 32 jj + 2i, +1.
 template <int ODD>
-__device__ __forceinline__ void dequant_q6k_chunk(const uint8_t* qlp, const uint32_t* qh, const __half2* ds,
-                                                  uint32_t* out) {
-  const __half2 b1056 = __halves2half2(__ushort_as_half(0x6420), __ushort_as_half(0x6420));  // 1024 + 32
+__device__ __forceinline__ void dequant_q6k_chunk(const uint8_t* qlp, const uint32_t* qh, uint16_t d16,
+                                                  float nd1056, const float* scf, uint32_t* out) {
 #pragma unroll
   for (int jj = 0; jj < 2; ++jj) {
     constexpr int kLoSh = 4 * ODD;  // nibble of the ql bytes
@@ -222,55 +234,16 @@ __device__ __forceinline__ void dequant_q6k_chunk(const uint8_t* qlp, const uint
       const uint32_t hq = s <= 4 ? qh[i] << (4 - s) : qh[i] >> (s - 4);
       // four 6-bit values (bytes) of elements 4i .. 4i+3 of the group
       const uint32_t q4 = lop3_and_or(ql[i] >> kLoSh, 0x0F0F0F0Fu, hq & 0x30303030u);
-      const uint32_t v01 = prmt(q4, 0x64u, 0x4140u);  // {0x64 q0, 0x64 q1}: fp16 1024 + q
-      const uint32_t v23 = prmt(q4, 0x64u, 0x4342u);
-      const __half2 d = ds[2 * jj + (i >> 2)];
-      out[16 * jj + 2 * i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v01), b1056), d));
-      out[16 * jj + 2 * i + 1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(v23), b1056), d));
+      const float sc = scf[2 * jj + (i >> 2)];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        // {0x64 q, 0x64 q'}: fp16 1024 + q; (1024 + q) d - 1056 d = (q - 32) d exactly
+        float lo, hi;
+        fma_f16x2_f32(prmt(q4, 0x64u, h ? 0x4342u : 0x4140u), d16, nd1056, lo, hi);
+        mul_f32x2(lo, hi, sc);   // exact: at most 23 significant bits
+        out[16 * jj + 2 * i + h] = h2_as_u32(__floats2half2_rn(lo, hi));
+      }
     }
-  }
-}
-
-// Exact operand pairs: `vals` holds four byte values q (0..63), elements
-// e .. e+3 of one sub-block; writes fp16_rn(fp32(q * d1 + nm1)) for them as
-// two fp16 pairs. q becomes exact in fp32 as 2^23 + q (the byte under the
-// exponent byte 0x4B) minus 2^23; q * d1 is exact in fp32 (d1 = d * sc has at
-// most 17 significant bits, q 6), so the fma rounds once, like the oracle's
-// product followed by a subtraction.
-__device__ __forceinline__ void exact_k_bytes(uint32_t vals, float d1, float nm1, uint32_t* out2) {
-  float f[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) f[i] = __uint_as_float(prmt(vals, 0x4B000000u, 0x7550u + (uint32_t)i)) - 8388608.0f;
-  out2[0] = h2_as_u32(__floats2half2_rn(fmaf(f[0], d1, nm1), fmaf(f[1], d1, nm1)));
-  out2[1] = h2_as_u32(__floats2half2_rn(fmaf(f[2], d1, nm1), fmaf(f[3], d1, nm1)));
-}
-
-// Q4_K, exact: the chunk's 32 qs bytes as in dequant_q4k_chunk; d1 / nm1 =
-// fp32 d*sc and -dmin*m of sub-blocks 2cc (lo) and 2cc+1 (hi).
-__device__ __forceinline__ void dequant_q4k_chunk_exact(const uint4 q0, const uint4 q1, float d1_lo, float nm1_lo,
-                                                        float d1_hi, float nm1_hi, uint32_t* out) {
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    exact_k_bytes(w[i] & 0x0F0F0F0Fu, d1_lo, nm1_lo, out + 2 * i);
-    exact_k_bytes((w[i] >> 4) & 0x0F0F0F0Fu, d1_hi, nm1_hi, out + 16 + 2 * i);
-  }
-}
-
-// Q5_K, exact: as dequant_q5k_chunk (whole 5-bit bytes), then exact_k_bytes.
-template <int CC>
-__device__ __forceinline__ void dequant_q5k_chunk_exact(const uint4 q0, const uint4 q1, const uint4 h0, const uint4 h1,
-                                                        float d1_lo, float nm1_lo, float d1_hi, float nm1_hi,
-                                                        uint32_t* out) {
-  const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-  const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-  constexpr int bl = 2 * CC, bh = 2 * CC + 1;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t fl = (bl <= 4 ? hw[i] << (4 - bl) : hw[i] >> (bl - 4)) & 0x10101010u;
-    const uint32_t fh = (bh <= 4 ? hw[i] << (4 - bh) : hw[i] >> (bh - 4)) & 0x10101010u;
-    exact_k_bytes(lop3_and_or(w[i], 0x0F0F0F0Fu, fl), d1_lo, nm1_lo, out + 2 * i);
-    exact_k_bytes(lop3_and_or(w[i] >> 4, 0x0F0F0F0Fu, fh), d1_hi, nm1_hi, out + 16 + 2 * i);
   }
 }
 
@@ -294,13 +267,15 @@ template <WFmt FMT, int C0 = 0, int C1 = kChunksPerUnit>
 __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uint8_t* aux, int r,
                                                  uint32_t a_slot) {
   static_assert(0 <= C0 && C0 < C1 && C1 <= kChunksPerUnit, "chunk range");
-  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q4KX) {
-    constexpr int kRow = unit_row_bytes<FMT>();
+  if constexpr (FMT == WFmt::Q4K || FMT == WFmt::Q5K) {
     // this row's block header: d, dmin and the 6-bit scales/mins of its
     // sub-blocks (llama.cpp get_scale_min_k4 packing): *_lo holds
-    // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7
-    const uint4 hdr = *reinterpret_cast<const uint4*>(stage + r * kRow);
-    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
+    // sub-blocks 0-3 in bytes 0-3, *_hi sub-blocks 4-7. Q5_K: qh at 16,
+    // qs at 48; Q4_K: qs at 16.
+    constexpr int kRow = unit_row_bytes<FMT>();
+    const uint8_t* row = stage + r * kRow;
+    const uint4 hdr = *reinterpret_cast<const uint4*>(row);
+    const uint16_t d16 = (uint16_t)(hdr.x & 0xFFFFu);
     const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
     const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
     const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
@@ -313,50 +288,22 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
       const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
       const uint32_t mw = cc < 2 ? m_lo : m_hi;
       constexpr int sh = 16 * (cc & 1);
-      const float d1l = d * (float)((scw >> sh) & 0xFFu), nm1l = -dmin * (float)((mw >> sh) & 0xFFu);
-      const float d1h = d * (float)((scw >> (sh + 8)) & 0xFFu), nm1h = -dmin * (float)((mw >> (sh + 8)) & 0xFFu);
+      // value-word biases: Q4_K low nibbles 1024, high nibbles 64; Q5_K 1024
+      constexpr float kBiasHi = FMT == WFmt::Q4K ? 64.f : 1024.f;
+      const KSub lo = ksub((scw >> sh) & 0xFFu, (mw >> sh) & 0xFFu, dmin, 1024.f);
+      const KSub hi = ksub((scw >> (sh + 8)) & 0xFFu, (mw >> (sh + 8)) & 0xFFu, dmin, kBiasHi);
       uint32_t P[32];
-      const uint8_t* qs = stage + r * kRow + 16 + cc * 32;
-      const uint4 q0 = *reinterpret_cast<const uint4*>(qs);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(qs + 16);
-      if constexpr (FMT == WFmt::Q4KX)
-        dequant_q4k_chunk_exact(q0, q1, d1l, nm1l, d1h, nm1h, P);
-      else
-        dequant_q4k_chunk(q0, q1, __float2half2_rn(d1l), __float2half2_rn(nm1l), __float2half2_rn(d1h),
-                          __float2half2_rn(nm1h), P);
-      tmem_st_x32(a_slot + (cc - C0) * 32, P);
-    };
-    if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
-    if constexpr (C0 <= 1 && 1 < C1) chunk(std::integral_constant<int, 1>{});
-    if constexpr (C0 <= 2 && 2 < C1) chunk(std::integral_constant<int, 2>{});
-    if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
-  } else if constexpr (FMT == WFmt::Q5K || FMT == WFmt::Q5KX) {
-    // header as Q4_K; qh at 16, qs at 48
-    const uint8_t* row = stage + r * kQ5KBlockBytes;
-    const uint4 hdr = *reinterpret_cast<const uint4*>(row);
-    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-    const uint32_t sc_lo = hdr.y & 0x3F3F3F3Fu;
-    const uint32_t m_lo = hdr.z & 0x3F3F3F3Fu;
-    const uint32_t sc_hi = (hdr.w & 0x0F0F0F0Fu) | ((hdr.y >> 2) & 0x30303030u);
-    const uint32_t m_hi = ((hdr.w >> 4) & 0x0F0F0F0Fu) | ((hdr.z >> 2) & 0x30303030u);
-    auto chunk = [&](auto cc_tag) {
-      constexpr int cc = decltype(cc_tag)::value;
-      const uint32_t scw = cc < 2 ? sc_lo : sc_hi;
-      const uint32_t mw = cc < 2 ? m_lo : m_hi;
-      constexpr int sh = 16 * (cc & 1);
-      const float d1l = d * (float)((scw >> sh) & 0xFFu), nm1l = -dmin * (float)((mw >> sh) & 0xFFu);
-      const float d1h = d * (float)((scw >> (sh + 8)) & 0xFFu), nm1h = -dmin * (float)((mw >> (sh + 8)) & 0xFFu);
-      const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
-      const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
-      const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
-      const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
-      uint32_t P[32];
-      if constexpr (FMT == WFmt::Q5KX)
-        dequant_q5k_chunk_exact<cc>(q0, q1, h0, h1, d1l, nm1l, d1h, nm1h, P);
-      else
-        dequant_q5k_chunk<cc>(q0, q1, h0, h1, __float2half2_rn(d1l), __float2half2_rn(nm1l), __float2half2_rn(d1h),
-                              __float2half2_rn(nm1h), P);
+      if constexpr (FMT == WFmt::Q4K) {
+        const uint4 q0 = *reinterpret_cast<const uint4*>(row + 16 + cc * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(row + 32 + cc * 32);
+        dequant_q4k_chunk(q0, q1, d16, lo, hi, P);
+      } else {
+        const uint4 q0 = *reinterpret_cast<const uint4*>(row + 48 + cc * 32);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(row + 64 + cc * 32);
+        const uint4 h0 = *reinterpret_cast<const uint4*>(row + 16);
+        const uint4 h1 = *reinterpret_cast<const uint4*>(row + 32);
+        dequant_q5k_chunk<cc>(q0, q1, h0, h1, d16, lo, hi, P);
+      }
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     };
     if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});
@@ -365,7 +312,8 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
     if constexpr (C0 <= 3 && 3 < C1) chunk(std::integral_constant<int, 3>{});
   } else if constexpr (FMT == WFmt::Q6K) {
     const uint8_t* row = stage + r * kQ6KBodyBytes;   // ql at 0, qh at 128, int8 scales at 192
-    const float d = __half2float(*reinterpret_cast<const __half*>(aux + 2 * r));
+    const uint16_t d16 = *reinterpret_cast<const uint16_t*>(aux + 2 * r);
+    const float nd1056 = -1056.f * __half2float(__ushort_as_half(d16));
     const uint4 scv = *reinterpret_cast<const uint4*>(row + 192);
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
     auto chunk = [&](auto cc_tag) {
@@ -377,12 +325,11 @@ __device__ __forceinline__ void dequant_unit_row(const uint8_t* stage, const uin
         const uint4 x = *reinterpret_cast<const uint4*>(row + 128 + 32 * h + 16 * v);
         qh[4 * v] = x.x; qh[4 * v + 1] = x.y; qh[4 * v + 2] = x.z; qh[4 * v + 3] = x.w;
       }
-      __half2 ds[4];
+      float scf[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        ds[t] = __float2half2_rn(d * (float)(int)(int8_t)((scw[cc] >> (8 * t)) & 0xFFu));
+      for (int t = 0; t < 4; ++t) scf[t] = (float)(int)(int8_t)((scw[cc] >> (8 * t)) & 0xFFu);
       uint32_t P[32];
-      dequant_q6k_chunk<cc & 1>(row + 64 * h, qh, ds, P);
+      dequant_q6k_chunk<cc & 1>(row + 64 * h, qh, d16, nd1056, scf, P);
       tmem_st_x32(a_slot + (cc - C0) * 32, P);
     };
     if constexpr (C0 <= 0 && 0 < C1) chunk(std::integral_constant<int, 0>{});

@@ -79,7 +79,7 @@ static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
 template <WFmt FMT>
 struct Smem {
   static constexpr int kWStage = 2 * wstage_bytes<FMT>();
-  static constexpr int kWStages = layout_of(FMT) == WFmt::Q5K || FMT == WFmt::Q6K ? 2 : 3;   // Q5_K / Q6_K: 44 / 52.5 KB
+  static constexpr int kWStages = FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 2 : 3;   // Q5_K / Q6_K: 44 / 52.5 KB
   static constexpr int kWOff = 0;
   static constexpr int kXOff = kWOff + kWStages * kWStage;
   static constexpr int kBarOff = kXOff + kXStages * kXStage;

@@ -38,6 +38,29 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2*>(&u); }
 
+// lo = fp16(a2.lo) * fp16(b) + c and hi = fp16(a2.hi) * fp16(b) + c in fp32,
+// each with one rounding: the sm_100 mixed-precision fma.rn.f32.f16 forms
+// the product of two fp16 values exactly (at most 22 significant bits).
+__device__ __forceinline__ void fma_f16x2_f32(uint32_t a2, uint16_t b, float c, float& lo, float& hi) {
+  asm("{\n\t.reg .b16 l, h;\n\t"
+      "mov.b32 {l, h}, %2;\n\t"
+      "fma.rn.f32.f16 %0, l, %3, %4;\n\t"
+      "fma.rn.f32.f16 %1, h, %3, %4;\n\t}"
+      : "=f"(lo), "=f"(hi)
+      : "r"(a2), "h"(b), "f"(c));
+}
+
+// (a, b) *= s as one packed fp32 multiply (sm_100 mul.rn.f32x2).
+__device__ __forceinline__ void mul_f32x2(float& a, float& b, float s) {
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%0, %1};\n\t"
+      "mov.b64 y, {%2, %2};\n\t"
+      "mul.rn.f32x2 x, x, y;\n\t"
+      "mov.b64 {%0, %1}, x;\n\t}"
+      : "+f"(a), "+f"(b)
+      : "f"(s));
+}
+
 // One thread of the (converged) warp is elected; returns true in that thread.
 // Issuing tcgen05.mma / TMA from a converged warp through elect.sync keeps the
 // operands warp-uniform (measured on B200: ~21 cycles per N=32 MMA this way

@@ -62,6 +62,8 @@ BUSFILL_API int busfill_gemm_q4_0(const uint8_t* wq, const uint16_t* ws, const u
 /* Q4_K: llama.cpp block_q4_K rows, K/256 blocks of 144 bytes per weight row
  * (fp16 d, fp16 dmin, 12 bytes of packed 6-bit sub-block scales and mins,
  * 128 nibble bytes); value = d*sc*q - dmin*m.  a [M, K] fp16, c [M, N] fp16.
+ * The fp16 weight operand is fp16_rn(fp32(d*sc)*q - fp32(dmin*m)), bit for
+ * bit the CPU dequant of busfill_dequant_q4k (llama.cpp's order).
  * Requires K % 256 == 0; blocks and a 16-byte aligned.
  * The reference has no Q4_K kernel; this is the Q4_K counterpart of
  * busfill_q4 (kernels/busfill_v1a.cu:41-46) that its docstring announces
@@ -157,8 +159,8 @@ BUSFILL_API int busfill_gemm_q4_0_ggml(const uint8_t* blocks, const uint16_t* a,
  * each value's fifth bit, 128 nibble bytes); value = d*sc*q - dmin*m with q
  * in 0..31.  a [M, K] fp16, c [M, N] fp16.  Requires K % 256 == 0; blocks and
  * a 16-byte aligned.  No reference counterpart: one of the K-quant formats
- * that Q4_K_M models mix in (the BASELINE "next" formats); same kernels and
- * numerics as busfill_gemm_q4k (two fp16 roundings of the weight operand). */
+ * that Q4_K_M models mix in; same kernels as busfill_gemm_q4k, and the same
+ * exact operand fp16_rn(fp32(d*sc)*q - fp32(dmin*m)). */
 BUSFILL_API int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream);
 
 /* Q6_K weights (llama.cpp block_q6_K: 128 B ql, 64 B qh, 16 int8 scales,
@@ -168,7 +170,7 @@ BUSFILL_API int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint1
  * A 210-byte block row has a 16-byte row stride (which the kernels'
  * tensor-memory-access copies need) only when K % 2048 == 0, so the blocks
  * are split once at load time; the bytes per weight stay 6.5625 bits.
- * Operand (q-32)*fp16_rn(d*sc), two fp16 roundings (as Q4_K); N % 8 == 0
+ * Operand fp16_rn(fp32(d*sc)*(q-32)), the CPU dequant's bits; N % 8 == 0
  * (d's row stride), K % 256 == 0, body/d/a 16-byte aligned.  No reference
  * counterpart: the other K-quant format that Q4_K_M models mix in. */
 BUSFILL_API int busfill_gemm_q6k(const uint8_t* body, const uint16_t* d, const uint16_t* a, uint16_t* c, int M, int N,
@@ -287,12 +289,9 @@ BUSFILL_API int busfill_version(void);
  *     items of 256 weight rows x 128 batch rows for SwiGLU pairs and
  *     busfill_gemm_q4k_noalloc, which take whole items. A tuning and test
  *     knob; results agree within the accuracy gate.
- *   BUSFILL_OPT_EXACT_KQUANT: 1 makes busfill_gemm_q4k and busfill_gemm_q5k
- *     build their fp16 weight operand exactly as the CPU dequant
- *     (fp16_rn(fp32(d*sc*q - dmin*m)), the bit-exact busfill_dequant_q4k /
- *     _q5k) instead of the default fp16 chain (two fp16 roundings, ~3e-4
- *     relative), at about twice the dequant instructions; 0 (default) off.
- *     The SwiGLU, gathered and no-allocation entry points keep the chain.
+ *   BUSFILL_OPT_EXACT_KQUANT: accepted (0 or 1) and ignored: every K-quant
+ *     GEMM builds the exact operand fp16_rn(fp32 w). Kept so that callers
+ *     which set it keep working.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2

@@ -1,11 +1,13 @@
 """CPU-side checks of the C ABI and of the kernels' host/bit-level logic.
 
 No GPU: the library is loaded and its exports and status strings checked; the
-dequant instruction chains of busfill_b200/csrc/decode_gemm.cuh are emulated
-bit for bit in numpy and compared with the oracle; the cluster K split
+dequant instruction chains of busfill_b200/csrc/formats.cuh are emulated
+bit for bit in numpy and compared with the oracle (the K formats' exact
+chains against the gguf-py golden vectors too); the cluster K split
 and tile assignment are checked to cover every unit exactly once.
 """
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -142,29 +144,84 @@ def test_q4k_nibble_bias_is_exact():
         assert float(np.float16(float(hi) - 64)) == byte >> 4
 
 
-def q4k_operand_chain(d16, dmin16, sc, m, q):
-    """Bit-level model of the GEMM's Q4_K operand: hfma2(q, ds, -dm) with
-    ds = fp16_rn(fp32(d)*sc), dm = fp16_rn(fp32(dmin)*m) (decode_gemm.cuh)."""
-    ds = (np.float32(d16) * np.float32(sc)).astype(np.float16)
-    ndm = (-(np.float32(dmin16) * np.float32(m))).astype(np.float16)
-    return hfma(np.float16(q), ds, ndm)
+def fma_f16_f32(a16, b16, c32):
+    """fma.rn.f32.f16: fp16 a times fp16 b plus fp32 c, rounded once to fp32.
+    The product is exact in float64 (at most 22 significant bits); the sum is
+    checked to be exact in float64 too (TwoSum error 0), so rounding it to
+    float32 once models the device instruction exactly."""
+    p = np.asarray(a16, np.float16).astype(np.float64) * np.asarray(b16, np.float16).astype(np.float64)
+    c = np.asarray(c32, np.float32).astype(np.float64)
+    s = p + c
+    bb = s - p
+    err = (p - (s - bb)) + (c - bb)
+    assert np.all(err == 0)
+    return s.astype(np.float32)
 
 
-def test_q4k_operand_chain_is_within_two_roundings_of_oracle():
-    rng = np.random.default_rng(7)
-    blocks = orc.gen_q4k(64, 2048, seed=7)
-    d16, dmin16, sc, m, q = orc.split_q4k_blocks(blocks, 2048)
+def k_exact_operand(d16, dmin16, sc, m, q, bias):
+    """Bit-level model of k_exact_pair (formats.cuh): the fp16 word bias + q
+    (exact), hfma2(bias + q, sc, -bias*sc) = q*sc (checked exact), the mixed
+    fma q*sc*d - m1 rounded once to fp32, then fp16_rn."""
+    q = np.asarray(q, np.int64)
+    sc = np.asarray(sc, np.int64)
+    biased = (bias + q).astype(np.float16)
+    assert np.all(biased.astype(np.int64) == bias + q)
+    nbsc = (-bias * sc).astype(np.float16)
+    assert np.all(nbsc.astype(np.int64) == -bias * sc)
+    qs = hfma(biased, sc.astype(np.float16), nbsc)
+    assert np.all(qs.astype(np.int64) == q * sc)
+    nm1 = -(np.asarray(dmin16, np.float16).astype(np.float32) * np.asarray(m, np.float32))
+    return fma_f16_f32(qs, d16, nm1).astype(np.float16)
+
+
+def q4k_model(blocks, k):
+    d16, dmin16, sc, m, q = orc.split_q4k_blocks(blocks, k)
     n, s = d16.shape
     qf = q.reshape(n, s, 8, 32)
-    got = q4k_operand_chain(d16[:, :, None, None], dmin16[:, :, None, None], sc[:, :, :, None], m[:, :, :, None], qf)
-    w32 = orc.dequant_q4k_f32(blocks, 2048).reshape(n, s, 8, 32).astype(np.float64)
-    # |err| <= ulp(ds)/2 * q + ulp(dm)/2 + ulp(w)/2, each ulp <= 2^-10 * |value|
-    ds = np.abs(d16.astype(np.float64)[:, :, None, None] * sc[:, :, :, None])
-    dm = np.abs(dmin16.astype(np.float64)[:, :, None, None] * m[:, :, :, None])
-    bound = 2.0 ** -11 * (ds * qf + dm + np.abs(w32)) + 1e-7
-    assert np.all(np.abs(got.astype(np.float64) - w32) <= bound)
-    rel = np.linalg.norm(got.astype(np.float64) - w32) / np.linalg.norm(w32)
-    assert rel < 5e-4, rel
+    # sub-blocks 2c (low nibbles, bias 1024) and 2c+1 (high nibbles, bias 64)
+    bias = np.where(np.arange(8) % 2 == 0, 1024, 64)[None, None, :, None]
+    w = k_exact_operand(d16[:, :, None, None], dmin16[:, :, None, None], sc[:, :, :, None], m[:, :, :, None], qf,
+                        bias)
+    return w.reshape(n, k)
+
+
+def canon16(w):
+    b = np.asarray(w, np.float16).view(np.uint16).copy()
+    b[b == 0x8000] = 0
+    return b
+
+
+def test_q4k_exact_chain_steps_are_exact_for_every_nibble_and_scale():
+    # every (q, sc) of both nibble positions: bias + q and q*sc exact in fp16
+    q = np.arange(16)[:, None]
+    sc = np.arange(64)[None, :]
+    for bias in (1024, 64):
+        k_exact_operand(np.float16(1.0), np.float16(0.0), sc, np.zeros_like(sc), q, bias)
+    # Q5_K: 5-bit values under the bias 1024
+    k_exact_operand(np.float16(1.0), np.float16(0.0), sc, np.zeros_like(sc), np.arange(32)[:, None], 1024)
+
+
+def test_q4k_exact_chain_is_the_oracle():
+    blocks = orc.gen_q4k(64, 2048, seed=7)
+    assert np.array_equal(canon16(q4k_model(blocks, 2048)), canon16(orc.dequant_q4k(blocks, 2048)))
+
+
+def test_q4k_exact_chain_on_golden_random_blocks(golden_dir):
+    g = np.load(os.path.join(golden_dir, "q4k_gguf.npz"))
+    for case in ("a", "b"):
+        blocks, w32, k = g[f"{case}_blocks"], g[f"{case}_w32"], int(g[f"{case}_k"])
+        assert np.array_equal(canon16(q4k_model(blocks, k)), canon16(w32.astype(np.float16)))
+
+
+def test_q5k_exact_chain_on_golden_random_blocks(golden_dir):
+    g = np.load(os.path.join(golden_dir, "q5k_gguf.npz"))
+    for case in ("a", "b"):
+        blocks, w32, k = g[f"{case}_blocks"], g[f"{case}_w32"], int(g[f"{case}_k"])
+        d16, dmin16, sc, m, q = orc.split_q5k_blocks(blocks, k)
+        n, s = d16.shape
+        w = k_exact_operand(d16[:, :, None, None], dmin16[:, :, None, None], sc[:, :, :, None], m[:, :, :, None],
+                            q.reshape(n, s, 8, 32), 1024)
+        assert np.array_equal(canon16(w.reshape(n, k)), canon16(w32.astype(np.float16)))
 
 
 def test_q6k_shape_and_alignment_checked_before_any_device_work():
@@ -209,12 +266,15 @@ def test_q5k_chunk_chain_values_and_order():
 def q6k_chunk_chain(body, d16, cc):
     """Bit-level model of dequant_q6k_chunk<cc % 2> (formats.cuh) on one
     208-byte block body: returns the chunk's 64 exact integers q - 32 (from
-    the biased fp16 words) and its 64 fp16 operands, in column order."""
+    the biased fp16 words) and its 64 fp16 operands, in column order. The
+    mixed fma (1024 + q) d - 1056 d gives (q - 32) d exactly; the product
+    with the group's int8 scale is exact in fp32 (checked); one rounding to
+    fp16 follows."""
     h, odd = cc >> 1, cc & 1
     ql = body[64 * h: 64 * h + 64].copy().view(np.uint32)
     qh = body[128 + 32 * h: 128 + 32 * h + 32].copy().view(np.uint32)
     sc = body[192 + 4 * cc: 196 + 4 * cc].copy().view(np.int8)
-    ds = [(np.float32(d16) * np.float32(sc[t])).astype(np.float16) for t in range(4)]
+    nd1056 = np.float32(-1056.0) * np.float32(d16)
     ints, vals = [], []
     for jj in range(2):
         s = 4 * odd + 2 * jj
@@ -224,17 +284,21 @@ def q6k_chunk_chain(body, d16, cc):
             q4 = ((int(ql[8 * jj + i]) >> (4 * odd)) & 0x0F0F0F0F) | (hq & 0x30303030)
             for sel in (0x4140, 0x4342):
                 for half in h2(prmt(q4, 0x64, sel)):
-                    qm = np.float16(np.float64(half) - 1056.0)     # hsub2 by 1056: exact
-                    ints.append(float(qm))
-                    vals.append(rn16(np.float64(qm) * np.float64(ds[2 * jj + i // 4])))
+                    t = fma_f16_f32(half, d16, nd1056)                 # (q - 32) d, exact
+                    ints.append(float(half) - 1056.0)
+                    assert float(t) == ints[-1] * float(d16)
+                    scale = np.float32(sc[2 * jj + i // 4])
+                    v = np.float32(t) * scale
+                    assert float(v) == float(t) * float(scale)        # exact: <= 23 significant bits
+                    vals.append(np.float16(v))
     return ints, np.array(vals, dtype=np.float16)
 
 
-def test_q6k_chunk_chain_order_exactness_and_rounding():
+def test_q6k_chunk_chain_order_and_exactness():
     blocks = orc.gen_q6k(6, 512, seed=11)
     d16, sc, q = orc.split_q6k_blocks(blocks, 512)
     body, dplane = orc.repack_q6k(blocks, 512)
-    w32 = orc.dequant_q6k_f32(blocks, 512)
+    want16 = orc.dequant_q6k(blocks, 512)
     for r in range(6):
         for b in range(2):
             blk = body[r, 208 * b: 208 * (b + 1)]
@@ -242,12 +306,21 @@ def test_q6k_chunk_chain_order_exactness_and_rounding():
                 ints, vals = q6k_chunk_chain(blk, dplane[b, r], cc)
                 e0 = 256 * b + 64 * cc
                 assert ints == [float(v) - 32 for v in q[r, e0: e0 + 64]]
-                want = w32[r, e0: e0 + 64].astype(np.float64)
-                dsa = np.abs(np.float64(d16[r, b]) * np.repeat(sc[r, b, 4 * cc: 4 * cc + 4], 16).astype(np.float64))
-                qa = np.abs(np.array(ints))
-                # |err| <= ulp(ds)/2 * |q-32| + ulp(w)/2, ulps <= 2^-10 of the value
-                bound = 2.0 ** -11 * (dsa * qa + np.abs(want)) + 1e-9
-                assert np.all(np.abs(vals.astype(np.float64) - want) <= bound)
+                assert np.array_equal(canon16(vals), canon16(want16[r, e0: e0 + 64]))
+
+
+def test_q6k_chunk_chain_on_golden_random_blocks(golden_dir):
+    g = np.load(os.path.join(golden_dir, "q6k_gguf.npz"))
+    blocks, w32, k = g["b_blocks"], g["b_w32"], int(g["b_k"])
+    body, dplane = orc.repack_q6k(blocks, k)
+    want16 = w32.astype(np.float16)
+    for r in range(0, blocks.shape[0], 5):
+        for b in range(k // 256):
+            blk = body[r, 208 * b: 208 * (b + 1)]
+            for cc in range(4):
+                _, vals = q6k_chunk_chain(blk, dplane[b, r], cc)
+                e0 = 256 * b + 64 * cc
+                assert np.array_equal(canon16(vals), canon16(want16[r, e0: e0 + 64]))
 
 
 def test_q4k_chunk_extraction_and_order():
