@@ -77,9 +77,12 @@ def alg_bytes(m, n, k):
     return n * k * 18 // 32 + 2 * m * k + 2 * m * n
 
 
-def profiled_traffic(workload):
-    """dram bytes per launch from a committed ncu summary, if one exists."""
-    path = os.path.join(ROOT, "profiles", f"{workload}.md")
+def profiled_traffic(workload, world=1):
+    """dram bytes per launch from a committed ncu summary of this exact
+    per-rank workload (profiles/<workload>.md for one GPU,
+    profiles/<workload>_tp<world>.md for a column split), else None."""
+    name = workload if world == 1 else f"{workload}_tp{world}"
+    path = os.path.join(ROOT, "profiles", f"{name}.md")
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):
@@ -204,6 +207,84 @@ def make_q4_0_weights(torch, n, k, gen, dev):
 
 
 # ---------------------------------------------------------------------------
+# parity of the timed path (device reference, outside the timed region)
+# ---------------------------------------------------------------------------
+GATE_MAX_ABS = 0.6      # the reference's gate, kernels/q4k_batched.py:102
+GATE_REL_L2 = 1e-3
+
+
+def _errors(torch, c, ref):
+    d = (c.double() - ref.double())
+    finite = bool(torch.isfinite(c).all())
+    return (float(d.abs().max()) if finite else float("inf"),
+            float(d.norm() / ref.double().norm()), finite)
+
+
+def parity_check(torch, bf, tp, dev, world, rank, args, space=None):
+    """One call of the timed path on seeded inputs, checked on every rank
+    against fp32 matmuls (torch, on the device) of the weights dequantized by
+    busfill_dequant_q4k / _q4_0 (bit-exact to the CPU dequant in the test
+    suite): the plain GEMM on one GPU; over several GPUs the gathered GEMM
+    of one call site and a second site that consumes it (its wait on the
+    first site's tile counters included), every rank's full gathered output
+    against the all-gathered reference columns. Gates: max abs <= 0.6,
+    rel-L2 <= 1e-3; the worst rank is reported."""
+    import torch.distributed as dist
+    torch.backends.cuda.matmul.allow_tf32 = False     # the reference is a true fp32 product
+    M, N, K = args.m, args.n, args.k
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(args.seed + 7 + rank)
+    r0, r1 = tp.shard_rows(N, world, rank)
+    a = torch.randn((M, K), device=dev, generator=gen).half()
+    if world > 1:
+        dist.broadcast(a, 0)
+    errs = []
+    if args.fmt == "q4k":
+        w1 = make_q4k_weights(torch, r1 - r0, K, gen, dev)
+        ref1 = a.float() @ bf.dequant_q4k(w1, K).float().t()
+    else:
+        wq, ws = make_q4_0_weights(torch, r1 - r0, K, gen, dev)
+        ref1 = a.float() @ bf.dequant_q4_0(wq, ws).float().t()
+    if world == 1:
+        c = bf.gemm_q4k(w1, a) if args.fmt == "q4k" else bf.gemm_q4_0(wq, ws, a)
+        errs.append(_errors(torch, c.float(), ref1))
+    elif space is None:
+        c = tp.gemm_q4_0_tp(wq, ws, a, N)
+        errs.append(_errors(torch, c.float(), tp.gather_columns(ref1.contiguous(), N)))
+    else:
+        # site 0: x -> [M, N]; site 1 (K' = N): its activations are site 0's
+        # gathered output, read after the device-side wait on site 0's counters
+        w2 = make_q4k_weights(torch, r1 - r0, N, gen, dev)
+        st = torch.cuda.current_stream()
+        c1 = tp.gemm_q4k_gather(w1, a, space, 0, stream=st)
+        c2 = tp.gemm_q4k_gather(w2, c1, space, 1, wait_site=0, stream=st)
+        space.wait(1, stream=st)
+        assert bf.stream_status(st) == 0
+        ref1_full = tp.gather_columns(ref1.contiguous(), N)
+        ref2 = c1.float() @ bf.dequant_q4k(w2, N).float().t()
+        ref2_full = tp.gather_columns(ref2.contiguous(), N)
+        errs.append(_errors(torch, c1.float(), ref1_full))
+        errs.append(_errors(torch, c2.float(), ref2_full))
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    max_abs = max(e[0] for e in errs)
+    rel = max(e[1] for e in errs)
+    finite = all(e[2] for e in errs)
+    if world > 1:
+        t = torch.tensor([max_abs, rel, 0.0 if finite else 1.0], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        max_abs, rel, finite = float(t[0]), float(t[1]), t[2].item() == 0.0
+    ok = finite and max_abs <= GATE_MAX_ABS and rel <= GATE_REL_L2
+    what = ("plain GEMM" if world == 1 else
+            "gathered GEMM and a consuming gathered GEMM (2 call sites)" if space is not None else
+            "GEMM + NCCL all-gather")
+    return {"ok": ok, "max_abs": round(max_abs, 6), "rel_l2": float(f"{rel:.4g}"), "finite": finite,
+            "checked": f"{what}, M={M}, N={N}, K={K}, worst rank of {world}",
+            "reference": "fp32 torch matmul on the device of busfill_dequant_* weights (bit-exact dequant)",
+            "gates": {"max_abs": GATE_MAX_ABS, "rel_l2": GATE_REL_L2}}
+
+
+# ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
 def run_busfill(args):
@@ -249,6 +330,18 @@ def run_busfill(args):
     # stores into every rank's output, one call site per weight copy);
     # Q4_0: NCCL all-gather after the GEMM
     space = tp.GatherSpace([(M, N)] * R) if (world > 1 and args.fmt == "q4k") else None
+    pspace = tp.GatherSpace([(M, N), (M, N)]) if (world > 1 and args.fmt == "q4k") else None
+    parity = parity_check(torch, bf, tp, dev, world, rank, args, pspace)
+    if pspace is not None:
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        pspace.close()
+    if not parity["ok"]:
+        if rank == 0:
+            print(json.dumps({"error": "parity check failed", "parity": parity}))
+        if world > 1:
+            dist.destroy_process_group()
+        raise SystemExit(3)
 
     def gemm(w, stream, i=0):
         if world == 1:
@@ -324,6 +417,9 @@ def run_busfill(args):
     tok_s = M * launches / (ms / 1e3)
     b_launch = alg_bytes(M, n_loc, K)
     achieved = b_launch / (us_per_gemm * 1e-6) / 1e9
+    # over several GPUs each rank also stores its [M, n_loc] slice into the
+    # other ranks' outputs (NVLink)
+    peer_bytes = 2 * M * n_loc * (world - 1) if space is not None else 0
     workload = f"{args.fmt}_gemm_m{M}_k{K}_n{N}"
     # this library's kernels per GEMM call (the gathered path is the decode kernel)
     try:
@@ -360,8 +456,15 @@ def run_busfill(args):
         "roofline": {
             "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
             "frac": round(achieved / hbm_peak, 4), "peak_source": peak_src,
-            "alg_bytes_per_launch": b_launch, "traffic": profiled_traffic(workload),
+            "alg_bytes_per_launch": b_launch, "traffic": profiled_traffic(workload, world),
+            "traffic_source": (f"ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of this per-rank "
+                               f"workload (profiles/)" if profiled_traffic(workload, world) is not None
+                               else "no ncu capture of this per-rank workload"),
+            **({"peer_store_bytes_per_launch": peer_bytes,
+                "achieved_with_peer_stores": round((b_launch + peer_bytes) / (us_per_gemm * 1e-6) / 1e9, 1)}
+               if world > 1 else {}),
         },
+        "parity": parity,
         "clocks": sampler.summary(),
     }
 
@@ -856,8 +959,13 @@ def cpu_baseline(args, reps=5):
             "dequant_s": round(deq, 4), "matmul_s": round(mm, 4)}
 
 
-def run_reference(args):
-    """The reference's CPU dequantize-then-matmul path, timed on the host cores."""
+def run_reference(args, budget_s=90.0):
+    """The reference's CPU dequantize-then-matmul path, timed on the host
+    cores: each step is one full GEMM (M x N x K) through the same code and
+    chunking as cpu_baseline (the oracle's dequant in 4 x cores row chunks on
+    a thread pool, then one torch fp32 matmul), so the two CPU numbers measure
+    the same thing. Up to --steps steps, stopping early once `budget_s` of
+    timed work has run (the count timed is reported)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -869,28 +977,32 @@ def run_reference(args):
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     m, n, k = args.m, args.n, args.k
-    rows = max(128, n // 8)            # each step: a bounded row slice of the weight matrix
-    w = orc.gen_q4k(rows, k, seed=args.seed) if args.fmt == "q4k" else orc.gen_q4_0(rows, k, seed=args.seed)
+    w = orc.gen_q4k(n, k, seed=args.seed) if args.fmt == "q4k" else orc.gen_q4_0(n, k, seed=args.seed)
     a = orc.gen_activations(m, k, seed=args.seed + 1)
+    times = []
     with ThreadPoolExecutor(cores) as pool:
         for _ in range(max(args.warmup, 1)):
             _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
-        t0 = time.perf_counter()
+        t_start = time.perf_counter()
         for _ in range(args.steps):
-            _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
-        el = time.perf_counter() - t0
-    t_full = el / args.steps * (n / rows)      # extrapolate the slice to all N rows
-    value = m / t_full
+            d, mm, _c = _cpu_dequant_gemm(orc, args.fmt, w, a, k, pool, 4 * cores)
+            times.append(d + mm)
+            if time.perf_counter() - t_start > budget_s:
+                break
+    el = sum(times)
+    value = m * len(times) / el
     out = {"metric": metric_name(args.fmt, k, n),
            "value": round(value, 2), "unit": "tokens/s", "impl": "reference", "n_gpus": args.gpus,
-           "steps": args.steps, "warmup": max(args.warmup, 1), "ms_per_step": round(el / args.steps * 1e3, 3),
+           "steps": len(times), "steps_requested": args.steps, "warmup": max(args.warmup, 1),
+           "ms_per_step": round(el / len(times) * 1e3, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
            "data": "synthetic (seeded numpy RNG, BASELINE config distributions)",
            "config": {"workload": f"{args.fmt}_gemm_m{m}_k{k}_n{n}", "format": args.fmt, "M": m, "N": n, "K": k,
                       "parallelism": "host CPU"},
            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": f"each step: {rows} of {n} weight rows (dequant + fp32 matmul, "
-                                      f"{cores} threads), extrapolated to N={n}"},
+                            "sample": f"{len(times)} full GEMMs (M={m}, K={k}, N={n}): oracle dequant (numpy, "
+                                      f"{cores} threads, {4 * cores} row chunks) + torch fp32 matmul ({cores} "
+                                      f"threads), the cpu_baseline code path"},
            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out))
 

@@ -19,9 +19,9 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q5k", "gemm_q6k", "repack_q6k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q4k_noalloc", "gemm_q5k", "gemm_q6k", "repack_q6k",
     "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
-    "stream_status", "stream_status_bits", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "noalloc_status", "internal_allocations", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -69,6 +69,8 @@ _SIGS = {
     "busfill_repack_q6k": [_P, _P, _P, _I, _I, _P],
     "busfill_dequant_q6k": [_P, _P, _P, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_noalloc_status": [_P, ctypes.POINTER(ctypes.c_uint)],
+    "busfill_internal_allocations": [],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q4_0": [_P, _P, _P, _I, _I, _P],
     "busfill_dequant_q4_0_ggml": [_P, _P, _I, _I, _P],
@@ -105,7 +107,8 @@ def load_library(path: str | None = None):
         fn = getattr(lib, name)
         fn.argtypes = args
         fn.restype = (ctypes.c_char_p if name == "busfill_status_string"
-                      else ctypes.c_uint if name == "busfill_last_failure_detail" else ctypes.c_int)
+                      else ctypes.c_uint if name in ("busfill_last_failure_detail", "busfill_internal_allocations")
+                      else ctypes.c_int)
     if path is None:
         _LIB = lib
     return lib
@@ -372,6 +375,19 @@ def dequant_q6k(body, d, k, out=None, stream=None):
         out = torch.empty((n, k), dtype=torch.float16, device=body.device)
     _check(_lib().busfill_dequant_q6k(_ptr(body), _ptr(d), _ptr(out), n, k, _stream(stream)), "busfill_dequant_q6k")
     return out
+
+
+def noalloc_status(stream=None):
+    """(status, error_bits) of the no-allocation GEMMs' static error word
+    (busfill_noalloc_status): synchronizes the stream, reads and clears it."""
+    bits = ctypes.c_uint(0)
+    st = _lib().busfill_noalloc_status(_stream(stream), ctypes.byref(bits))
+    return st, bits.value
+
+
+def internal_allocations() -> int:
+    """Device allocations the library has made on its own so far."""
+    return _lib().busfill_internal_allocations()
 
 
 def stream_status(stream=None) -> int:

@@ -151,16 +151,34 @@ bool make_tmap_act3d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t K
 constexpr size_t kErrorWordsBytes = 256;
 
 std::map<std::pair<int, cudaStream_t>, unsigned*> g_err;
+// device allocations this library made on its own (error words, stream-K
+// workspaces; not busfill_ipc_alloc), for busfill_internal_allocations
+std::atomic<unsigned> g_internal_allocs{0};
+
+// true if `s` is capturing a graph (or the query failed): no allocation then,
+// since a cudaMalloc would invalidate the capture
+bool capturing(cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) {
+    cudaGetLastError();
+    return true;
+  }
+  return cs != cudaStreamCaptureStatusNone;
+}
 
 int get_error_words(int dev, cudaStream_t s, unsigned** out) {
   // caller holds g_mu
   unsigned*& w = g_err[{dev, s}];
   if (!w) {
+    // the first call on a stream makes its words; inside a graph capture that
+    // would end the capture, so it fails cleanly instead
+    if (capturing(s)) return BUSFILL_ERR_ALLOC;
     if (cudaMalloc(&w, kErrorWordsBytes) != cudaSuccess) {
       cudaGetLastError();
       w = nullptr;
       return BUSFILL_ERR_ALLOC;
     }
+    ++g_internal_allocs;
     if (cudaMemsetAsync(w, 0, kErrorWordsBytes, s) != cudaSuccess) return BUSFILL_ERR_CUDA;
   }
   *out = w;
@@ -178,14 +196,12 @@ float* prefill_workspace(int dev, cudaStream_t s, int sm_count) {
   std::lock_guard<std::mutex> lk(g_mu);
   float*& w = g_part[{dev, s}];
   if (!w) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-      cudaGetLastError();
-      return nullptr;
-    }
+    if (capturing(s)) return nullptr;
     if (cudaMalloc(&w, (size_t)2 * sm_count * prefill::kPartElems * sizeof(float)) != cudaSuccess) {
       cudaGetLastError();
       w = nullptr;
+    } else {
+      ++g_internal_allocs;
     }
   }
   return w;
@@ -609,9 +625,11 @@ int grid_for(long long work, int sm_count) {
 struct WaitTiles {
   int n[kMaxPeers];
 };
+// One CTA: it is every call's last arrival, so only the call count
+// (wait_gen[0]) moves; wait_gen[1] stays 0.
 __global__ void __launch_bounds__(32, 1) gather_wait_kernel(const unsigned* wait, unsigned* wait_gen, int nwait,
                                                             WaitTiles tiles, unsigned* error) {
-  const unsigned calls = *reinterpret_cast<volatile unsigned*>(wait_gen);  // one CTA: one per call
+  const unsigned calls = *reinterpret_cast<volatile unsigned*>(wait_gen);
   bool got = true;
   if ((int)threadIdx.x < nwait) got = wait_flag_sys(wait + threadIdx.x, (calls + 1u) * (unsigned)tiles.n[threadIdx.x]);
   got = __all_sync(0xffffffffu, got);
@@ -841,6 +859,37 @@ int busfill_gemm_q4k_noalloc(const uint8_t* blocks, const uint16_t* a, uint16_t*
                              void* stream) {
   return gemm_q4k_static(blocks, a, c, M, N, K, reinterpret_cast<cudaStream_t>(stream));
 }
+
+int busfill_noalloc_status(void* stream, unsigned* bits) {
+  if (bits) *bits = 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (cudaStreamSynchronize(s) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  uint8_t* scratch = nullptr;
+  const int st = static_scratch(dev, &scratch);
+  if (st != BUSFILL_OK) return st;
+  unsigned err2[2] = {0, 0};
+  if (cudaMemcpy(err2, scratch, sizeof(err2), cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  if (bits) {
+    bits[0] = err2[0];
+    g_last_detail = err2[1];
+  }
+  if (err2[0] == 0) return BUSFILL_OK;
+  if (cudaMemset(scratch, 0, kStaticScratchBytes) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_CUDA;
+  }
+  return BUSFILL_ERR_DEVICE_TIMEOUT;
+}
+
+unsigned busfill_internal_allocations(void) { return g_internal_allocs.load(); }
 
 int busfill_q4(const uint16_t* A, const uint8_t* Wq, const uint16_t* Ws, float* C, int Bsz, int K, int N,
                void* stream) {

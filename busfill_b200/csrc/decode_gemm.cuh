@@ -101,7 +101,7 @@ struct GatherArgs {
   void* out[kMaxPeers];       // each rank's full output [rows, ldc], at this launch's first row
   unsigned* flag[kMaxPeers];  // per rank: this rank's tile counter in that rank's memory
   const unsigned* wait;       // nwait local counter words (one per source rank); may be null
-  unsigned* wait_gen;         // each waiting CTA adds 1 after its wait: value / grid = calls so far
+  unsigned* wait_gen;         // two words: [0] completed calls of the site, [1] CTAs of the current call through
   int nwait;
   int wait_tiles[kMaxPeers];  // tiles each source rank writes per call
 };
@@ -364,10 +364,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
     if (GA && p.gather.nwait > 0) {
       // activations gathered by an earlier GEMM on every rank: wait for each
-      // rank's flag, then let this thread's TMA copies see what it acquired
-      // calls completed so far: every earlier call's CTAs each added 1; this
-      // call's CTAs that already got through add less than one grid's worth
-      const unsigned calls = *reinterpret_cast<volatile unsigned*>(p.gather.wait_gen) / gridDim.x;
+      // rank's flag, then let this thread's TMA copies see what it acquired.
+      // wait_gen[0] counts this site's completed calls and wait_gen[1] the
+      // CTAs of the current call that got through: every CTA reads [0] before
+      // it arrives on [1], and the last to arrive resets [1] and advances [0],
+      // so the count holds whatever grid each call had. The previous call
+      // of the site completed before this one started (the stream order, and
+      // griddepcontrol.wait above), so [1] starts at 0.
+      unsigned calls = 0;
+      if (lane == 0) calls = ld_acquire_gpu(p.gather.wait_gen);
+      calls = __shfl_sync(0xffffffffu, calls, 0);
       bool got = true;
       if (lane < p.gather.nwait)
         got = wait_flag_sys(p.gather.wait + lane, (calls + 1u) * (unsigned)p.gather.wait_tiles[lane]);
@@ -376,7 +382,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         atomicCAS(p.error + 1, 0u, 0x80000000u | ((unsigned)warp << 24) | 0xFFFu << 12);
       }
       fence_proxy_async_global();
-      if (lane == 0) atomicAdd(p.gather.wait_gen, 1u);
+      if (lane == 0 && atom_add_acq_rel_gpu(p.gather.wait_gen + 1, 1u) == gridDim.x - 1) {
+        st_relaxed_gpu(p.gather.wait_gen + 1, 0u);
+        red_release_gpu_add(p.gather.wait_gen, 1u);
+      }
     }
     if (lane < x_early) issue_x_thread(lane);
     __syncwarp();
@@ -701,12 +710,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (csize > 1) cluster_wait();
   // Gathered output: a CTA that wrote tiles (rank 0 of its cluster) adds
   // their number to this rank's counter in every rank's memory. The CTA
-  // barrier above orders the epilogue warps' peer stores before thread 0, and
-  // the reduction's system-scope release makes them visible to a consumer
-  // that acquires the counter (a data-then-flag protocol over NVLink).
-  if (GA && p.gather.signal && crank == 0 && threadIdx.x == 0) {
-    const unsigned tiles = (unsigned)(ntiles >> kSw);
-    for (int q = 0; q < p.gather.npeers; ++q) red_release_sys_add(p.gather.flag[q], tiles);
+  // barrier above orders the epilogue warps' peer stores before warp 0; lane
+  // q then makes them visible at system scope (one fence for the warp) and
+  // adds to peer q's counter with a relaxed reduction, all peers at once, so
+  // a consumer that acquires the counter sees the data (a data-then-flag
+  // protocol over NVLink). One release reduction per peer in turn instead
+  // made every reduction wait for the previous one to be performed.
+  if (GA && p.gather.signal && crank == 0 && warp == 0 && lane < p.gather.npeers) {
+    fence_acq_rel_sys();
+    red_relaxed_sys_add(p.gather.flag[lane], (unsigned)(ntiles >> kSw));
   }
 }
 

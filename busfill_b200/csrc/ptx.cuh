@@ -216,14 +216,29 @@ __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.w
 // ----------------------------------------------------------------------------
 // flags between GPUs (peer memory mapped over NVLink)
 // ----------------------------------------------------------------------------
-// store that releases this thread's prior writes at system scope
-__device__ __forceinline__ void st_release_sys(unsigned* addr, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+// add to a (possibly peer) word without a result, relaxed at system scope; a
+// fence_acq_rel_sys before it in the same thread makes the pair a release of
+// this thread's prior writes (and those ordered before them)
+__device__ __forceinline__ void red_relaxed_sys_add(unsigned* addr, unsigned v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
-// add to a (possibly peer) word without a result, releasing this thread's
-// prior writes (and those ordered before them) at system scope
-__device__ __forceinline__ void red_release_sys_add(unsigned* addr, unsigned v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+// returns the old value; acquire and release at GPU scope
+__device__ __forceinline__ unsigned atom_add_acq_rel_gpu(unsigned* addr, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void st_relaxed_gpu(unsigned* addr, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_gpu_add(unsigned* addr, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* addr) {
   unsigned v;

@@ -145,10 +145,15 @@ class GatherSpace:
 
     Site i owns, in every rank's allocation, a full output [rows_i, cols_i]
     fp16, one tile-counter word per source rank (rank r adds to word r), and
-    two local words that count this site's waits (as a GEMM consumer and
-    through `wait`). A site's output is written by every rank's GEMM for that site and
-    read by later sites; a separate buffer per call site keeps a rank from
-    overwriting data another rank has not read yet.
+    four local words that count this site's waits (two as a GEMM consumer,
+    two through `wait`). A site's output is written by every rank's GEMM for
+    that site and read by later sites. Within one pass over the sites, the
+    separate buffer per site keeps a rank from overwriting data that another
+    rank has not read yet. Across passes it does not: a site must not be
+    called again until every rank's consumers of its previous output have
+    finished, e.g. because a later site's wait already orders the ranks, or
+    because the caller puts a barrier between passes (as the tests and the
+    benchmark do between graph replays).
     """
 
     _ALIGN = 256
@@ -219,7 +224,7 @@ class GatherSpace:
             g.flag[q] = self.bases[q] + o_flag + 4 * self.rank
         if wait_site is not None:
             g.wait = self._base + self._off[wait_site][1]
-            g.wait_gen = self._base + o_cnt          # this site's count of waits on wait_site's counters
+            g.wait_gen = self._base + o_cnt          # this site's 2 words counting its waits on wait_site
             g.nwait = self.world
             for r in range(self.world):
                 g.wait_tiles[r] = self._tiles(wait_site, r)
@@ -240,7 +245,7 @@ class GatherSpace:
         if g is None:
             g = Gather()
             g.wait = self._base + self._off[site][1]
-            g.wait_gen = self._base + self._off[site][2] + 4    # this site's standalone wait count
+            g.wait_gen = self._base + self._off[site][2] + 8    # this site's standalone wait count (2 words)
             g.nwait = self.world
             for r in range(self.world):
                 g.wait_tiles[r] = self._tiles(site, r)

@@ -95,13 +95,18 @@ BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_
  * memory that only this rank adds to; a running total over the call site's
  * calls). A later GEMM whose activations are that gathered output passes the
  * nwait local words it must wait on (`wait`, one per source rank), the tiles
- * each source rank writes per call (`wait_tiles`) and `wait_gen`, a zeroed
- * local word for its own call site; its kernel waits (acquire, bounded by
+ * each source rank writes per call (`wait_tiles`) and `wait_gen`, two zeroed
+ * local words for its own call site; its kernel waits (acquire, bounded by
  * 1 s, else BUSFILL_ERR_DEVICE_TIMEOUT) until word r reaches (calls so far +
- * 1) x wait_tiles[r], counting its calls in *wait_gen. All state lives in
+ * 1) x wait_tiles[r], counting its calls in wait_gen[0] (wait_gen[1] counts
+ * the CTAs of the call in progress, so M and the launch shape may change from
+ * call to call). All state lives in
  * device memory, so the calls can be captured in a CUDA graph and replayed.
  * No NCCL call, no host round trip. Every rank must make the same calls in
- * the same order. The reference is
+ * the same order. A call site's output buffer is overwritten by the peers'
+ * next call of that site: do not call a site again until every rank's
+ * consumers of its previous output have finished (a later site's wait that
+ * orders the ranks, or a barrier between passes). The reference is
  * single-GPU (no counterpart); this is BASELINE's N-split with its
  * all-gather moved into the GEMM.
  * ------------------------------------------------------------------------- */
@@ -113,7 +118,7 @@ typedef struct busfill_gather {
   uint16_t* out[BUSFILL_MAX_PEERS];  /* each rank's full output [M, ldc] fp16 (device pointers) */
   uint32_t* flag[BUSFILL_MAX_PEERS]; /* per rank q: this rank's tile counter in rank q's memory */
   const uint32_t* wait;              /* optional: nwait local counter words to wait on before reading a */
-  uint32_t* wait_gen;                /* with wait: zeroed local word of this call site */
+  uint32_t* wait_gen;                /* with wait: two zeroed local words of this call site */
   int nwait;                         /* source ranks waited on, <= 8 */
   int wait_tiles[BUSFILL_MAX_PEERS]; /* with wait: 128-row tiles source rank r writes per call */
 } busfill_gather;
@@ -127,8 +132,9 @@ BUSFILL_API int busfill_gemm_q4k_swiglu_gather(const uint8_t* w_gate, const uint
                                                int N, int K, const busfill_gather* g, void* stream);
 
 /* Make `stream` wait until a gathered output is complete on this rank: one
- * small kernel waits (acquire, bounded by 1 s) until every word of g->wait
- * reaches *g->wait_gen + 1 and then advances *g->wait_gen, as a consuming
+ * small kernel waits (acquire, bounded by 1 s) until word r of g->wait
+ * reaches (g->wait_gen[0] + 1) x g->wait_tiles[r] and then advances
+ * g->wait_gen[0] (two zeroed words of its own, not a GEMM's), as a consuming
  * GEMM would. For consumers that are not busfill GEMMs (a copy to the host,
  * another library's kernel). Only the wait fields of `g` are read. */
 BUSFILL_API int busfill_gather_wait(const busfill_gather* g, void* stream);
@@ -206,10 +212,19 @@ BUSFILL_API int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_
  *     kernels overlap on the GPU (other streams, other host threads) race on
  *     the array: a failure of one can be cleared or misattributed by another.
  *   - A device-side wait that expires is recorded in the array, not in the
- *     per-stream word that busfill_stream_status reads, so it is not reported
- *     there; the output of such a call is undefined. */
+ *     per-stream word that busfill_stream_status reads: busfill_noalloc_status
+ *     reports it. The output of such a call is undefined. */
 BUSFILL_API int busfill_gemm_q4k_noalloc(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K,
                                          void* stream);
+
+/* Synchronizes `stream`, then reports (and clears) the error word that
+ * busfill_gemm_q4k_noalloc calls keep in the library's static array: BUSFILL_OK,
+ * BUSFILL_ERR_DEVICE_TIMEOUT or BUSFILL_ERR_CUDA; *bits (if not NULL) gets the
+ * role bits as in busfill_stream_status_ex. Allocates nothing. The array is
+ * shared by every no-allocation call on the device, so with calls in flight
+ * on other streams the word may belong to any of them. No reference
+ * counterpart. */
+BUSFILL_API int busfill_noalloc_status(void* stream, unsigned* bits);
 
 /* Reference-compatible surface: the arguments and fp32 output of
  * busfill_q4(A, Wq, Ws, C, Bsz, K, N) (kernels/busfill_v1a.cu:41-46) plus a
@@ -265,6 +280,12 @@ BUSFILL_API int busfill_stream_status_ex(void* stream, unsigned* bits);
  * the warp index, bits 12-23 the unit index within that CTA's range, bits
  * 1-11 the barrier slot, bit 0 the awaited phase parity. For diagnostics. */
 BUSFILL_API unsigned busfill_last_failure_detail(void);
+
+/* Number of device allocations this library has made on its own so far in
+ * the process (per-stream error words and stream-K workspaces; not the
+ * buffers of busfill_ipc_alloc). Diagnostic: lets a caller check that a
+ * path allocates nothing. No reference counterpart. */
+BUSFILL_API unsigned busfill_internal_allocations(void);
 
 /* Human-readable text for a busfill_status value. */
 BUSFILL_API const char* busfill_status_string(int status);
