@@ -252,17 +252,26 @@ def parity_check(torch, bf, tp, dev, world, rank, args, space=None):
         c = tp.gemm_q4_0_tp(wq, ws, a, N)
         errs.append(_errors(torch, c.float(), tp.gather_columns(ref1.contiguous(), N)))
     else:
-        # site 0: x -> [M, N]; site 1 (K' = N): its activations are site 0's
-        # gathered output, read after the device-side wait on site 0's counters
+        # site 0: the timed call's shape on the config-scale activations;
+        # site 1 on the activations scaled by 2^-12 (exact), whose output
+        # site 2 (K' = N) consumes after its device-side wait on site 1's
+        # counters (the scaling keeps the chained product near the
+        # magnitudes the absolute gate is for)
         w2 = make_q4k_weights(torch, r1 - r0, N, gen, dev)
+        a_small = (a.float() / 4096).half()
         st = torch.cuda.current_stream()
-        c1 = tp.gemm_q4k_gather(w1, a, space, 0, stream=st)
-        c2 = tp.gemm_q4k_gather(w2, c1, space, 1, wait_site=0, stream=st)
-        space.wait(1, stream=st)
+        c0 = tp.gemm_q4k_gather(w1, a, space, 0, stream=st)
+        c1 = tp.gemm_q4k_gather(w1, a_small, space, 1, stream=st)
+        c2 = tp.gemm_q4k_gather(w2, c1, space, 2, wait_site=1, stream=st)
+        space.wait(0, stream=st)
+        space.wait(2, stream=st)
         assert bf.stream_status(st) == 0
-        ref1_full = tp.gather_columns(ref1.contiguous(), N)
+        ref0_full = tp.gather_columns(ref1.contiguous(), N)
+        ref1s = a_small.float() @ bf.dequant_q4k(w1, K).float().t()
+        ref1_full = tp.gather_columns(ref1s.contiguous(), N)
         ref2 = c1.float() @ bf.dequant_q4k(w2, N).float().t()
         ref2_full = tp.gather_columns(ref2.contiguous(), N)
+        errs.append(_errors(torch, c0.float(), ref0_full))
         errs.append(_errors(torch, c1.float(), ref1_full))
         errs.append(_errors(torch, c2.float(), ref2_full))
         dist.barrier()
@@ -276,7 +285,7 @@ def parity_check(torch, bf, tp, dev, world, rank, args, space=None):
         max_abs, rel, finite = float(t[0]), float(t[1]), t[2].item() == 0.0
     ok = finite and max_abs <= GATE_MAX_ABS and rel <= GATE_REL_L2
     what = ("plain GEMM" if world == 1 else
-            "gathered GEMM and a consuming gathered GEMM (2 call sites)" if space is not None else
+            "gathered GEMMs at 3 call sites, one consuming another's output" if space is not None else
             "GEMM + NCCL all-gather")
     return {"ok": ok, "max_abs": round(max_abs, 6), "rel_l2": float(f"{rel:.4g}"), "finite": finite,
             "checked": f"{what}, M={M}, N={N}, K={K}, worst rank of {world}",
@@ -330,7 +339,7 @@ def run_busfill(args):
     # stores into every rank's output, one call site per weight copy);
     # Q4_0: NCCL all-gather after the GEMM
     space = tp.GatherSpace([(M, N)] * R) if (world > 1 and args.fmt == "q4k") else None
-    pspace = tp.GatherSpace([(M, N), (M, N)]) if (world > 1 and args.fmt == "q4k") else None
+    pspace = tp.GatherSpace([(M, N)] * 3) if (world > 1 and args.fmt == "q4k") else None
     parity = parity_check(torch, bf, tp, dev, world, rank, args, pspace)
     if pspace is not None:
         torch.cuda.synchronize(dev)

@@ -20,7 +20,7 @@ import re
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q4k_noalloc", "gemm_q5k", "gemm_q6k", "repack_q6k",
-    "busfill_q4", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
+    "busfill_q4", "repack_q4k_planar", "gemm_q4k_planar", "Tensor", "tensor_desc", "mul_mat", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
     "stream_status", "stream_status_bits", "noalloc_status", "internal_allocations", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "probe_umma", "version",
 ]
 
@@ -69,6 +69,9 @@ _SIGS = {
     "busfill_repack_q6k": [_P, _P, _P, _I, _I, _P],
     "busfill_dequant_q6k": [_P, _P, _P, _I, _I, _P],
     "busfill_gemm_q4k_noalloc": [_P, _P, _P, _I, _I, _I, _P],
+    "busfill_repack_q4k_planar": [_P, _P, _P, _P, _P, _I, _I, _P],
+    "busfill_gemm_q4k_planar": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_mul_mat": [_P, _P, _P, _P],
     "busfill_noalloc_status": [_P, ctypes.POINTER(ctypes.c_uint)],
     "busfill_internal_allocations": [],
     "busfill_q4": [_P, _P, _P, _P, _I, _I, _I, _P],
@@ -266,6 +269,75 @@ def gemm_q4k_noalloc(blocks, a, out, stream=None):
     _check(_lib().busfill_gemm_q4k_noalloc(_ptr(blocks), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
            "busfill_gemm_q4k_noalloc")
     return out
+
+
+def repack_q4k_planar(qs, d, dmin, scales12, stream=None):
+    """Q4_K planes (qs u8 [N, K/2], d / dmin fp16 [N, K/256], scales12 u8
+    [N, K/256*12]) -> llama.cpp block_q4_K rows u8 [N, K/256*144]."""
+    torch = _torch()
+    _need(qs, torch.uint8, "qs"); _need(d, torch.float16, "d"); _need(dmin, torch.float16, "dmin")
+    _need(scales12, torch.uint8, "scales12")
+    n, k = qs.shape[0], qs.shape[1] * 2
+    blocks = torch.empty((n, k // 256 * 144), dtype=torch.uint8, device=qs.device)
+    _check(_lib().busfill_repack_q4k_planar(_ptr(qs), _ptr(d), _ptr(dmin), _ptr(scales12), _ptr(blocks), n, k,
+                                            _stream(stream)), "busfill_repack_q4k_planar")
+    return blocks
+
+
+def gemm_q4k_planar(qs, d, dmin, scales12, a, out=None, stream=None):
+    """C[M, N] = A @ deq(W)^T with the Q4_K weight given as planes (see
+    repack_q4k_planar); the library repacks per call into its own buffer."""
+    torch = _torch()
+    _need(qs, torch.uint8, "qs"); _need(d, torch.float16, "d"); _need(dmin, torch.float16, "dmin")
+    _need(scales12, torch.uint8, "scales12"); _need(a, torch.float16, "a")
+    m, k = a.shape
+    n = qs.shape[0]
+    if qs.shape[1] * 2 != k or d.shape != (n, k // 256) or dmin.shape != (n, k // 256) or \
+            scales12.shape != (n, k // 256 * 12):
+        raise ValueError("shape mismatch between the Q4_K planes and a")
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.float16, device=a.device)
+    _need(out, torch.float16, "out")
+    _check(_lib().busfill_gemm_q4k_planar(_ptr(qs), _ptr(d), _ptr(dmin), _ptr(scales12), _ptr(a), _ptr(out), m, n,
+                                          k, _stream(stream)), "busfill_gemm_q4k_planar")
+    return out
+
+
+class Tensor(ctypes.Structure):
+    """ctypes mirror of busfill_tensor (a ggml-style tensor description)."""
+    _fields_ = [("type", ctypes.c_int32), ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4),
+                ("data", ctypes.c_void_p)]
+
+
+TYPE_F16, TYPE_Q4_0, TYPE_Q4_K, TYPE_Q5_K = 1, 2, 12, 13
+_BLOCK = {TYPE_Q4_0: (32, 18), TYPE_Q4_K: (256, 144), TYPE_Q5_K: (256, 176)}
+
+
+def tensor_desc(t, ggml_type, ne):
+    """busfill_tensor of a CUDA tensor holding a packed ggml tensor of type
+    `ggml_type` with ggml shape `ne` (innermost first); strides as ggml
+    computes them for a contiguous tensor."""
+    ne = list(ne) + [1] * (4 - len(ne))
+    if ggml_type == TYPE_F16:
+        nb0, row = 2, 2 * ne[0]
+    else:
+        qk, bs = _BLOCK[ggml_type]
+        nb0, row = bs, ne[0] // qk * bs
+    d = Tensor()
+    d.type = ggml_type
+    for i in range(4):
+        d.ne[i] = ne[i]
+    d.nb[0], d.nb[1] = nb0, row
+    d.nb[2] = row * ne[1]
+    d.nb[3] = d.nb[2] * ne[2]
+    d.data = t.data_ptr()
+    return d
+
+
+def mul_mat(src0, src1, dst, stream=None):
+    """busfill_mul_mat on three busfill_tensor descriptions (ggml_mul_mat)."""
+    _check(_lib().busfill_mul_mat(ctypes.byref(src0), ctypes.byref(src1), ctypes.byref(dst), _stream(stream)),
+           "busfill_mul_mat")
 
 
 def busfill_q4(A, Wq, Ws, C, Bsz, K, N, stream=None):

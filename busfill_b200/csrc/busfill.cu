@@ -683,6 +683,53 @@ int gemm_q4k_static(const uint8_t* w, const uint16_t* a, uint16_t* c, int M, int
                                      nullptr, false);
 }
 
+// ---------------------------------------------------------------------------
+// planar Q4_K: block rows rebuilt per call in a per-(device, stream) buffer
+// ---------------------------------------------------------------------------
+struct PlanarBuf {
+  uint8_t* p = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, PlanarBuf> g_planar;
+
+int planar_buffer(int dev, cudaStream_t s, size_t bytes, uint8_t** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  PlanarBuf& b = g_planar[{dev, s}];
+  if (b.bytes < bytes) {
+    if (capturing(s)) return BUSFILL_ERR_ALLOC;
+    if (b.p) {
+      cudaFree(b.p);   // synchronizes the device: no kernel still reads the old rows
+      b.p = nullptr;
+      b.bytes = 0;
+    }
+    if (cudaMalloc(&b.p, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      b.p = nullptr;
+      return BUSFILL_ERR_ALLOC;
+    }
+    ++g_internal_allocs;
+    b.bytes = bytes;
+  }
+  *out = b.p;
+  return BUSFILL_OK;
+}
+
+int repack_q4k_planar_impl(const uint8_t* qs, const uint16_t* d, const uint16_t* dmin, const uint8_t* sc12,
+                           uint8_t* blocks, int N, int K, cudaStream_t s) {
+  if (!qs || !d || !dmin || !sc12 || !blocks) return BUSFILL_ERR_INVALID_ARG;
+  if (N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  if (!aligned16(qs) || !aligned16(blocks) || (reinterpret_cast<uintptr_t>(d) & 1u) ||
+      (reinterpret_cast<uintptr_t>(dmin) & 1u) || (reinterpret_cast<uintptr_t>(sc12) & 3u))
+    return BUSFILL_ERR_ALIGNMENT;
+  DeviceInfo di;
+  int dev;
+  const int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  const long long nb = (long long)N * (K / kUnitK);
+  repack_q4k_planar_kernel<<<grid_for(nb * 9, di.sm_count), 256, 0, s>>>(qs, d, dmin, sc12, blocks, nb);
+  return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -769,6 +816,68 @@ int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_t* d, int N,
   repack_q6k_kernel<<<grid_for(words, di.sm_count), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<const uint16_t*>(blocks), reinterpret_cast<uint16_t*>(body), d, N, K / 256);
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
+}
+
+int busfill_repack_q4k_planar(const uint8_t* qs, const uint16_t* d, const uint16_t* dmin, const uint8_t* scales12,
+                              uint8_t* blocks, int N, int K, void* stream) {
+  return repack_q4k_planar_impl(qs, d, dmin, scales12, blocks, N, K, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int busfill_gemm_q4k_planar(const uint8_t* qs, const uint16_t* d, const uint16_t* dmin, const uint8_t* scales12,
+                            const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
+  if (!qs || !d || !dmin || !scales12 || !a || !c) return BUSFILL_ERR_INVALID_ARG;
+  if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  DeviceInfo di;
+  int dev = 0;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  uint8_t* blocks = nullptr;
+  st = planar_buffer(dev, s, (size_t)N * (K / kUnitK) * kQ4KBlockBytes, &blocks);
+  if (st != BUSFILL_OK) return st;
+  st = repack_q4k_planar_impl(qs, d, dmin, scales12, blocks, N, K, s);
+  if (st != BUSFILL_OK) return st;
+  return gemm_impl<WFmt::Q4K, __half>(blocks, nullptr, a, c, M, N, K, s);
+}
+
+int busfill_mul_mat(const busfill_tensor* src0, const busfill_tensor* src1, busfill_tensor* dst, void* stream) {
+  if (!src0 || !src1 || !dst || !src0->data || !src1->data || !dst->data) return BUSFILL_ERR_INVALID_ARG;
+  if (src1->type != BUSFILL_TYPE_F16 || dst->type != BUSFILL_TYPE_F16) return BUSFILL_ERR_INVALID_ARG;
+  int qk = 0, bs = 0;
+  switch (src0->type) {
+    case BUSFILL_TYPE_Q4_0: qk = 32; bs = 18; break;
+    case BUSFILL_TYPE_Q4_K: qk = 256; bs = kQ4KBlockBytes; break;
+    case BUSFILL_TYPE_Q5_K: qk = 256; bs = kQ5KBlockBytes; break;
+    default: return BUSFILL_ERR_INVALID_ARG;
+  }
+  const int64_t K = src0->ne[0], N = src0->ne[1], M = src1->ne[1];
+  for (int i = 0; i < 4; ++i)
+    if (src0->ne[i] < 1 || src1->ne[i] < 1 || dst->ne[i] < 1) return BUSFILL_ERR_SHAPE;
+  if (src1->ne[0] != K || dst->ne[0] != N || dst->ne[1] != M) return BUSFILL_ERR_SHAPE;
+  if (dst->ne[2] != src1->ne[2] || dst->ne[3] != src1->ne[3]) return BUSFILL_ERR_SHAPE;
+  if (src1->ne[2] % src0->ne[2] != 0 || src1->ne[3] % src0->ne[3] != 0) return BUSFILL_ERR_SHAPE;
+  if (K % kUnitK != 0 || K > (1 << 30) || N > (1 << 30) || M > (1 << 30)) return BUSFILL_ERR_SHAPE;
+  // rows must be packed: one GEMM runs per batch slice over [rows, K] blocks
+  if (src0->nb[0] != (size_t)bs || src0->nb[1] != (size_t)(K / qk) * bs) return BUSFILL_ERR_SHAPE;
+  if (src1->nb[0] != 2 || src1->nb[1] != (size_t)K * 2 || dst->nb[0] != 2 || dst->nb[1] != (size_t)N * 2)
+    return BUSFILL_ERR_SHAPE;
+  const int64_t r2 = src1->ne[2] / src0->ne[2], r3 = src1->ne[3] / src0->ne[3];
+  for (int64_t i3 = 0; i3 < src1->ne[3]; ++i3)
+    for (int64_t i2 = 0; i2 < src1->ne[2]; ++i2) {
+      const uint8_t* w = static_cast<const uint8_t*>(src0->data) + (i2 / r2) * src0->nb[2] + (i3 / r3) * src0->nb[3];
+      const uint16_t* a = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(src1->data) +
+                                                            i2 * src1->nb[2] + i3 * src1->nb[3]);
+      uint16_t* c = reinterpret_cast<uint16_t*>(static_cast<uint8_t*>(dst->data) + i2 * dst->nb[2] + i3 * dst->nb[3]);
+      int st;
+      if (src0->type == BUSFILL_TYPE_Q4_0)
+        st = busfill_gemm_q4_0_ggml(w, a, c, (int)M, (int)N, (int)K, stream);
+      else if (src0->type == BUSFILL_TYPE_Q4_K)
+        st = busfill_gemm_q4k(w, a, c, (int)M, (int)N, (int)K, stream);
+      else
+        st = busfill_gemm_q5k(w, a, c, (int)M, (int)N, (int)K, stream);
+      if (st != BUSFILL_OK) return st;
+    }
+  return BUSFILL_OK;
 }
 
 int busfill_gemm_q4k_gather(const uint8_t* blocks, const uint16_t* a, int M, int N, int K, const busfill_gather* g,

@@ -267,4 +267,30 @@ __global__ void dequant_q6k_kernel(const uint8_t* __restrict__ body, const __hal
   }
 }
 
+// Q4_K planes -> llama.cpp block_q4_K rows: one thread per 16-byte word of
+// an output block (9 per 144-byte block). Word 0 is the header (fp16 d,
+// fp16 dmin, the 12 packed scale/min bytes), words 1..8 the block's 128
+// nibble bytes. Planes: qs [N][S][128], d and dmin [N][S] fp16, scales
+// [N][S][12]; the bytes are moved, never changed.
+__global__ void repack_q4k_planar_kernel(const uint8_t* __restrict__ qs, const uint16_t* __restrict__ d,
+                                         const uint16_t* __restrict__ dmin, const uint8_t* __restrict__ sc12,
+                                         uint8_t* __restrict__ blocks, long long nblocks) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < nblocks * 9;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long b = i / 9;
+    const int w = (int)(i - b * 9);
+    uint4 v;
+    if (w == 0) {
+      const uint32_t* s4 = reinterpret_cast<const uint32_t*>(sc12 + b * 12);   // 4-byte aligned
+      v.x = (uint32_t)d[b] | ((uint32_t)dmin[b] << 16);
+      v.y = s4[0];
+      v.z = s4[1];
+      v.w = s4[2];
+    } else {
+      v = reinterpret_cast<const uint4*>(qs + b * 128)[w - 1];
+    }
+    reinterpret_cast<uint4*>(blocks + b * 144)[w] = v;
+  }
+}
+
 }  // namespace busfill

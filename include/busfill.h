@@ -186,6 +186,60 @@ BUSFILL_API int busfill_gemm_q6k(const uint8_t* body, const uint16_t* d, const u
  * Asynchronous on `stream`; `blocks` and the outputs must not overlap. */
 BUSFILL_API int busfill_repack_q6k(const uint8_t* blocks, uint8_t* body, uint16_t* d, int N, int K, void* stream);
 
+/* Q4_K as separate planes, the split-pointer form of the Q4_K weight:
+ *   qs       [N, K/2] u8        each 256-value super-block's 128 nibble bytes
+ *                               in block_q4_K order (32-byte chunk c: low
+ *                               nibbles sub-block 2c, high nibbles 2c+1);
+ *   d, dmin  [N, K/256] fp16    the super-blocks' scale and min scale;
+ *   scales12 [N, K/256, 12] u8  the packed 6-bit sub-block scales and mins.
+ * busfill_repack_q4k_planar moves these bytes into block_q4_K rows [N,
+ * K/256 x 144 B] for busfill_gemm_q4k (do it once, when the weights are
+ * loaded). busfill_gemm_q4k_planar repacks into a per-stream buffer that the
+ * library allocates on first use (and grows; never during a graph capture:
+ * BUSFILL_ERR_ALLOC), then runs busfill_gemm_q4k on it, so every call moves
+ * the weights three times (read, write, read): prefer the one-time repack.
+ * qs, blocks, a 16-byte aligned; d, dmin 2-byte; scales12 4-byte. The
+ * reference has no Q4_K code; this is the planar signature of the Q4_K
+ * entry its docstring announces (kernels/q4k_batched.py:7-8). */
+BUSFILL_API int busfill_repack_q4k_planar(const uint8_t* qs, const uint16_t* d, const uint16_t* dmin,
+                                          const uint8_t* scales12, uint8_t* blocks, int N, int K, void* stream);
+BUSFILL_API int busfill_gemm_q4k_planar(const uint8_t* qs, const uint16_t* d, const uint16_t* dmin,
+                                        const uint8_t* scales12, const uint16_t* a, uint16_t* c, int M, int N, int K,
+                                        void* stream);
+
+/* ---------------------------------------------------------------------------
+ * ggml mul_mat call site
+ *
+ * A tensor as ggml describes one: element type (ggml_type numbering), ne[]
+ * elements and nb[] byte strides per dimension (index 0 innermost), and its
+ * device data. busfill_mul_mat(src0, src1, dst) computes what
+ * ggml_mul_mat(ctx, src0, src1) defines: src0 the quantized weight
+ * [ne0 = K, ne1 = N, ne2, ne3] (Q4_0 in block_q4_0, Q4_K in block_q4_K, Q5_K
+ * in block_q5_K rows), src1 the activations [K, M, ne12, ne13] fp16, dst
+ * [N, M, ne12, ne13] fp16 (row m of dst holds the N outputs of activation row
+ * m: C[M, N]); src0 is broadcast over src1's batch dimensions (ne12 % ne02
+ * == 0, ne13 % ne03 == 0). Rows must be packed (nb[1] = the row's bytes);
+ * batch strides nb[2], nb[3] are free. One busfill_gemm_* call per batch
+ * slice. Other types (Q6_K, whose rows need busfill_repack_q6k first; fp32
+ * activations) return BUSFILL_ERR_INVALID_ARG. No reference counterpart:
+ * the reference's next step is wiring its dequant into llama.cpp's batched
+ * GEMM (RESULTS.md:235-237), which is reached through this call site.
+ * ------------------------------------------------------------------------- */
+#define BUSFILL_TYPE_F32 0
+#define BUSFILL_TYPE_F16 1
+#define BUSFILL_TYPE_Q4_0 2
+#define BUSFILL_TYPE_Q4_K 12
+#define BUSFILL_TYPE_Q5_K 13
+#define BUSFILL_TYPE_Q6_K 14
+typedef struct busfill_tensor {
+  int32_t type;  /* BUSFILL_TYPE_*: the ggml_type numbering */
+  int64_t ne[4]; /* elements per dimension, ne[0] innermost */
+  size_t nb[4];  /* bytes per step along each dimension */
+  void* data;    /* device pointer */
+} busfill_tensor;
+BUSFILL_API int busfill_mul_mat(const busfill_tensor* src0, const busfill_tensor* src1, busfill_tensor* dst,
+                                void* stream);
+
 /* busfill_gemm_q4k that allocates no device memory.  It has no counterpart
  * in the reference.
  *

@@ -483,3 +483,62 @@ def test_stream_k_partition_covers_every_unit_once(items, s, g):
     assert set(owned) == split_items
     for it, sl in owned.items():
         assert sorted(sl) == sorted(v for (c, i), v in slots.items() if i == it)
+
+
+# ---------------------------------------------------------------------------
+# planar Q4_K and the ggml mul_mat call site (host-side checks)
+# ---------------------------------------------------------------------------
+def test_ggml_type_numbering_matches_gguf():
+    gguf = pytest.importorskip("gguf")
+    t = gguf.GGMLQuantizationType
+    assert (int(t.F32), int(t.F16), int(t.Q4_0), int(t.Q4_K), int(t.Q5_K), int(t.Q6_K)) == (0, 1, 2, 12, 13, 14)
+    assert (bf.TYPE_F16, bf.TYPE_Q4_0, bf.TYPE_Q4_K, bf.TYPE_Q5_K) == (1, 2, 12, 13)
+
+
+class _FakeDev:
+    """Stand-in for a device tensor: only its (never dereferenced) address."""
+
+    def __init__(self, ptr):
+        self.ptr = ptr
+
+    def data_ptr(self):
+        return self.ptr
+
+
+def test_mul_mat_checks_before_any_device_work():
+    lib = bf.load_library()
+    fake = 0x10000
+    w = bf.tensor_desc(_FakeDev(fake), bf.TYPE_Q4_K, [512, 256])
+    x = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [512, 8])
+    y = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [256, 8])
+    call = lambda a, b, c: lib.busfill_mul_mat(ctypes.byref(a), ctypes.byref(b), ctypes.byref(c), None)  # noqa: E731
+    assert lib.busfill_mul_mat(None, None, None, None) == -1
+    q6 = bf.tensor_desc(_FakeDev(fake), bf.TYPE_Q4_K, [512, 256])
+    q6.type = 14                                     # Q6_K rows need busfill_repack_q6k first
+    assert call(q6, x, y) == -1
+    x32 = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [512, 8])
+    x32.type = 0                                     # fp32 activations are not taken
+    assert call(w, x32, y) == -1
+    bad_k = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [256, 8])
+    assert call(w, bad_k, y) == -2                   # K mismatch
+    bad_n = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [128, 8])
+    assert call(w, x, bad_n) == -2                   # N mismatch
+    strided = bf.tensor_desc(_FakeDev(fake), bf.TYPE_Q4_K, [512, 256])
+    strided.nb[1] += 16                              # padded rows are not taken
+    assert call(strided, x, y) == -2
+    wb = bf.tensor_desc(_FakeDev(fake), bf.TYPE_Q4_K, [512, 256, 2])
+    xb = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [512, 8, 3])
+    yb = bf.tensor_desc(_FakeDev(fake), bf.TYPE_F16, [256, 8, 3])
+    assert call(wb, xb, yb) == -2                    # 3 batches do not broadcast over 2
+
+
+def test_planar_q4k_checks_before_any_device_work():
+    lib = bf.load_library()
+    fake = 0x10000
+    assert lib.busfill_repack_q4k_planar(None, None, None, None, None, 4, 256, None) == -1
+    assert lib.busfill_repack_q4k_planar(fake, fake, fake, fake, fake, 4, 300, None) == -2
+    assert lib.busfill_repack_q4k_planar(fake + 8, fake, fake, fake, fake, 4, 256, None) == -3
+    assert lib.busfill_repack_q4k_planar(fake, fake + 1, fake, fake, fake, 4, 256, None) == -3
+    assert lib.busfill_repack_q4k_planar(fake, fake, fake, fake + 2, fake, 4, 256, None) == -3
+    assert lib.busfill_gemm_q4k_planar(fake, fake, fake, fake, None, fake, 8, 4, 256, None) == -1
+    assert lib.busfill_gemm_q4k_planar(fake, fake, fake, fake, fake, fake, 0, 4, 256, None) == -2
