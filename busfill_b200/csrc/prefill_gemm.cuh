@@ -28,6 +28,13 @@
 // Measured on B200: a 128x128x16 TS MMA (A in TMEM) takes ~74 cycles back to
 // back, 92% of the dense fp16 rate; a unit (32 MMAs) ~2400 cycles.
 //
+// Handoffs: a dequant warp group publishes a half slot with a named-barrier
+// arrive that the MMA warp syncs on (no mbarrier round trip on the path of
+// every 8 MMAs); the slot comes back through the commit barrier of its MMAs.
+// Named barriers have no timeout, so every group arrives, and the MMA warp
+// syncs, for every half slot of every unit whatever happens (work is skipped
+// after a failed wait, the arrivals are not).
+//
 // Warp roles (16 warps, one CTA per SM, persistent over work items):
 //   0      weight TMA producer (3-stage ring of 36 KB)
 //   1      activation TMA producer (3-stage ring of 32 KB); TMEM allocator
@@ -72,6 +79,8 @@ constexpr int kSlotCols = 64;                   // half a unit
 constexpr int kSlot0 = 2 * kAccCols;
 constexpr int kTmemCols = 512;
 static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
+constexpr uint32_t kBarSlot0 = 1;          // named barrier of half slot s: kBarSlot0 + s
+constexpr uint32_t kSlotBarThreads = 160;  // the tile's 4 dequant warps + the MMA warp
 
 // shared memory map (the weight stage holds both tiles' unit: 256 rows, then
 // the rows' second plane: Q4_0 32 KB of nibbles and 4 KB of scales; Q6_K
@@ -85,8 +94,7 @@ struct Smem {
   static constexpr int kBarOff = kXOff + kXStages * kXStage;
   static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
   static constexpr int bXFull = bWEmpty + kWStages, bXEmpty = bXFull + kXStages;
-  static constexpr int bReady = bXEmpty + kXStages;   // half slot s = 2t + h filled (4 dequant warps of tile t)
-  static constexpr int bSDone = bReady + 4;           // half slot s read by its MMAs (commit)
+  static constexpr int bSDone = bXEmpty + kXStages;  // half slot s = 2t + h read by its MMAs (commit)
   static constexpr int bAccFull = bSDone + 4, bAccEmpty = bAccFull + 1, bFinal = bAccEmpty + 1;
   static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
@@ -126,7 +134,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   constexpr int kWStage = SM::kWStage, kWStages = SM::kWStages, kWOff = SM::kWOff, kXOff = SM::kXOff;
   constexpr int kBarOff = SM::kBarOff, kMiscOff = SM::kMiscOff, kNumBars = SM::kNumBars;
   constexpr int bWFull = SM::bWFull, bWEmpty = SM::bWEmpty, bXFull = SM::bXFull, bXEmpty = SM::bXEmpty;
-  constexpr int bReady = SM::bReady, bSDone = SM::bSDone, bAccFull = SM::bAccFull, bAccEmpty = SM::bAccEmpty;
+  constexpr int bSDone = SM::bSDone, bAccFull = SM::bAccFull, bAccEmpty = SM::bAccEmpty;
   constexpr int bFinal = SM::bFinal;
   constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, kBatchTile);
   constexpr bool kRows144 = aos_rows<FMT>();
@@ -180,7 +188,6 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   };
   auto bar_count = [&](int b) -> uint32_t {
     if (b >= bWEmpty && b < bWEmpty + kWStages) return 8;  // both tiles' dequant warps
-    if (b >= bReady && b < bReady + 4) return 4;           // the tile's dequant warps
     if (b == bAccEmpty) return 4;                          // the epilogue warps
     return 1;                                              // TMA expect_tx arrivals, MMA commits
   };
@@ -289,19 +296,18 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
       unit_at(u, it, k);
       const bool first = u == 0 || k == 0, last = u == nunits - 1 || k == S - 1;
       // the accumulators are free once the epilogue has read piece j - 1
-      if (first && j >= 1 && !warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1))) break;
-      bool good = true;
+      if (first && j >= 1) warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1));
 #pragma unroll 1
-      for (int h = 0; h < 2 && good; ++h) {
+      for (int h = 0; h < 2; ++h) {
         const int v = 2 * u + h;
-        if (!warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1)) { good = false; break; }
+        warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1);
         const uint64_t bx = bdesc0 + (uint64_t)(((v % kXStages) * kXStage) >> 4);
 #pragma unroll 1
         for (int t = 0; t < 2; ++t) {
           const int sl = 2 * t + h;
-          if (!warp_wait(BAR(bReady + sl), (uint32_t)(u & 1))) { good = false; break; }
+          named_bar_sync(kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // the tile's group published the half
           tc_fence_after();
-          if (elect_one()) {
+          if (ok && elect_one()) {
             const uint32_t d_acc = tmem + (uint32_t)(t * kAccCols);
             const uint32_t a_t = tmem + (uint32_t)(kSlot0 + sl * kSlotCols);
 #pragma unroll
@@ -314,11 +320,10 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
           }
           __syncwarp();
         }
-        if (good && elect_one()) tc_commit(BAR(bXEmpty + v % kXStages));  // activation stage free
+        if (ok && elect_one()) tc_commit(BAR(bXEmpty + v % kXStages));  // activation stage free
         __syncwarp();
       }
-      if (!good) break;
-      if (elect_one() && last) tc_commit(BAR(bAccFull));  // piece's accumulators complete
+      if (ok && elect_one() && last) tc_commit(BAR(bAccFull));  // piece's accumulators complete
       __syncwarp();
       if (last) ++j;
     }
@@ -335,26 +340,26 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     for (int u = 0; u < nunits; ++u) {
       diag_unit = u;
       const int ws = u % kWStages;
-      if (!warp_wait(BAR(bWFull + ws), (u / kWStages) & 1)) break;
+      warp_wait(BAR(bWFull + ws), (u / kWStages) & 1);
       const uint8_t* stage = smem + kWOff + ws * kWStage;
-      bool good = true;
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
         const int sl = 2 * t + h;
         // half slot sl is free once the MMAs of the previous unit read it
-        if (u >= 1 && !warp_wait(BAR(bSDone + sl), (uint32_t)((u - 1) & 1))) { good = false; break; }
+        if (u >= 1) warp_wait(BAR(bSDone + sl), (uint32_t)((u - 1) & 1));
         tc_fence_after();
-        const uint32_t a_col = tmem + lane_off + (uint32_t)(kSlot0 + sl * kSlotCols);
-        if (h == 0)
-          dequant_unit_row<FMT, 0, 2>(stage, stage + kAuxOff, row, a_col);
-        else
-          dequant_unit_row<FMT, 2, 4>(stage, stage + kAuxOff, row, a_col);
-        tc_wait_st();
+        if (ok) {
+          const uint32_t a_col = tmem + lane_off + (uint32_t)(kSlot0 + sl * kSlotCols);
+          if (h == 0)
+            dequant_unit_row<FMT, 0, 2>(stage, stage + kAuxOff, row, a_col);
+          else
+            dequant_unit_row<FMT, 2, 4>(stage, stage + kAuxOff, row, a_col);
+          tc_wait_st();
+        }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(BAR(bReady + sl));
+        named_bar_arrive(kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // always: the MMA warp syncs on every half
       }
-      if (!good) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(bWEmpty + ws));
     }
