@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
 #pragma unroll 1
         for (int t = 0; t < 2; ++t) {
           const int sl = 2 * t + h;
-          named_bar_sync(kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // the tile's group published the half
+          named_bar_sync(prefill::kBarSlot0 + (uint32_t)sl, prefill::kSlotBarThreads);   // the tile's group published the half
           tc_fence_after();
           if (ok && elect_one()) {
             const uint32_t d_acc = tmem + (uint32_t)(t * kAccCols);
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        named_bar_arrive(kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // always: the MMA warp syncs on every half
+        named_bar_arrive(prefill::kBarSlot0 + (uint32_t)sl, prefill::kSlotBarThreads);   // always: the MMA warp syncs on every half
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(BAR(bWEmpty + ws));
