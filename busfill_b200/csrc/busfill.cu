@@ -572,12 +572,18 @@ int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws
 template <WFmt FMT>
 int gemm_gather_impl(const uint8_t* w, const uint8_t* w_up, bool swiglu, const uint16_t* a, int M, int N, int K,
                      const busfill_gather* g, cudaStream_t s) {
-  if (!g || (swiglu && !w_up)) return BUSFILL_ERR_INVALID_ARG;
-  if (g->npeers < 1 || g->npeers > kMaxPeers || g->col_off < 0 || g->ldc < g->col_off + N) return BUSFILL_ERR_SHAPE;
+  if (!g) return BUSFILL_ERR_INVALID_ARG;
+  if (g->npeers < 1 || g->npeers > kMaxPeers || g->col_off < 0 || N < 0 || g->ldc < g->col_off + N)
+    return BUSFILL_ERR_SHAPE;
   if (g->nwait < 0 || g->nwait > kMaxPeers || (g->nwait > 0 && (!g->wait || !g->wait_gen)))
     return BUSFILL_ERR_INVALID_ARG;
   for (int q = 0; q < g->npeers; ++q)
     if (!g->out[q] || !g->flag[q]) return BUSFILL_ERR_INVALID_ARG;
+  // A rank that owns no rows of this weight (fewer 128-row tiles than ranks)
+  // computes and stores nothing and writes 0 tiles a call, which is what the
+  // other ranks' consumers wait for from it: the call is a no-op.
+  if (N == 0) return BUSFILL_OK;
+  if (swiglu && !w_up) return BUSFILL_ERR_INVALID_ARG;
   int st = check_gemm_args<FMT>(w, nullptr, a, g->out[0], M, N, K);
   if (st != BUSFILL_OK) return st;
   if (w_up && !aligned16(w_up)) return BUSFILL_ERR_ALIGNMENT;

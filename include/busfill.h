@@ -103,7 +103,9 @@ BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_
  * call to call). All state lives in
  * device memory, so the calls can be captured in a CUDA graph and replayed.
  * No NCCL call, no host round trip. Every rank must make the same calls in
- * the same order. A call site's output buffer is overwritten by the peers'
+ * the same order; a rank that owns no rows of a weight (N = 0: fewer 128-row
+ * tiles than ranks) makes the call too, and it does nothing (its weight
+ * pointers may be NULL; it writes 0 tiles a call). A call site's output buffer is overwritten by the peers'
  * next call of that site: do not call a site again until every rank's
  * consumers of its previous output have finished (a later site's wait that
  * orders the ranks, or a barrier between passes). The reference is

@@ -542,3 +542,20 @@ def test_planar_q4k_checks_before_any_device_work():
     assert lib.busfill_repack_q4k_planar(fake, fake, fake, fake + 2, fake, 4, 256, None) == -3
     assert lib.busfill_gemm_q4k_planar(fake, fake, fake, fake, None, fake, 8, 4, 256, None) == -1
     assert lib.busfill_gemm_q4k_planar(fake, fake, fake, fake, fake, fake, 0, 4, 256, None) == -2
+
+
+def test_gathered_call_of_a_rank_without_rows_is_a_no_op():
+    """A rank that owns no rows of a weight (fewer 128-row tiles than ranks)
+    still makes the gathered call; it launches nothing, whatever its weight
+    pointers, and so needs no device."""
+    from busfill_b200 import tp
+    lib = bf.load_library()
+    fake = 0x10000
+    g = tp.Gather()
+    g.npeers, g.col_off, g.ldc = 4, 0, 384
+    for q in range(4):
+        g.out[q] = fake
+        g.flag[q] = fake
+    assert lib.busfill_gemm_q4k_gather(None, fake, 8, 0, 1280, ctypes.byref(g), None) == 0
+    assert lib.busfill_gemm_q4k_swiglu_gather(None, None, fake, 8, 0, 1280, ctypes.byref(g), None) == 0
+    assert lib.busfill_gemm_q4k_gather(None, fake, 8, -1, 1280, ctypes.byref(g), None) == -2
