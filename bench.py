@@ -92,20 +92,6 @@ def profiled_traffic(workload, world=1):
     return None
 
 
-def kernels_per_gemm(bf, m, n, k, sm_count):
-    """Kernel launches of one plain busfill_gemm_* call, mirroring the
-    library's dispatch: one decode launch per 32 batch rows, or the prefill
-    kernel plus its fix-up kernel when the stream-K ranges (G = min(units,
-    SMs) CTAs over the items' units) split an item between CTAs."""
-    if not bf.uses_prefill(m, n, k):
-        return (m + 31) // 32
-    items = ((n + 255) // 256) * ((m + 127) // 128)
-    s = k // 256
-    t = items * s
-    g = min(t, sm_count, 201)
-    return 2 if any((t * c // g) % s for c in range(1, g)) else 1
-
-
 class ClockSampler:
     """Samples SM clock and throttle reasons with NVML while the timed region runs."""
 
@@ -431,11 +417,8 @@ def run_busfill(args):
     peer_bytes = 2 * M * n_loc * (world - 1) if space is not None else 0
     workload = f"{args.fmt}_gemm_m{M}_k{K}_n{N}"
     # this library's kernels per GEMM call (the gathered path is the decode kernel)
-    try:
-        k_per_gemm = ((M + 31) // 32 if space is not None else
-                      kernels_per_gemm(bf, M, n_loc, K, props.multi_processor_count))
-    except Exception:
-        k_per_gemm = 1
+    k_per_gemm = ((M + 31) // 32 if space is not None else
+                  bf.gemm_launches(M, n_loc, K, props.multi_processor_count))
     out = {
         "metric": metric_name(args.fmt, K, N),
         "value": round(tok_s, 1),

@@ -21,7 +21,7 @@ __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
     "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q4k_noalloc", "gemm_q5k", "gemm_q6k", "repack_q6k",
     "busfill_q4", "repack_q4k_planar", "gemm_q4k_planar", "Tensor", "tensor_desc", "mul_mat", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
-    "stream_status", "stream_status_bits", "noalloc_status", "internal_allocations", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "probe_umma", "version",
+    "stream_status", "stream_status_bits", "noalloc_status", "internal_allocations", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "gemm_launches", "probe_umma", "version",
 ]
 
 _PKG = os.path.dirname(os.path.abspath(__file__))
@@ -86,6 +86,7 @@ _SIGS = {
     "busfill_set_option": [_I, _I],
     "busfill_probe_umma": [_P, _P, _P, _I, _P],
     "busfill_gemm_kernel_for": [_I, _I, _I],
+    "busfill_gemm_launches": [_I, _I, _I, _I],
     "busfill_gemm_q4k_gather": [_P, _P, _I, _I, _I, _P, _P],
     "busfill_gemm_q4k_swiglu_gather": [_P, _P, _P, _I, _I, _I, _P, _P],
     "busfill_gather_wait": [_P, _P],
@@ -141,6 +142,13 @@ def set_ksplit(csize: int) -> None:
 def uses_prefill(m: int, n: int, k: int) -> bool:
     """True if a GEMM of m batch rows, n output columns and depth k runs the prefill kernel."""
     return _lib().busfill_gemm_kernel_for(int(m), int(n), int(k)) == 1
+
+
+def gemm_launches(m: int, n: int, k: int, sm_count: int = 0) -> int:
+    """Kernel launches of one plain GEMM call of that shape (busfill_gemm_launches)."""
+    v = _lib().busfill_gemm_launches(int(m), int(n), int(k), int(sm_count))
+    _check(min(v, 0), "busfill_gemm_launches")
+    return v
 
 
 def set_exact_kquant(on: bool) -> None:

@@ -749,6 +749,27 @@ unsigned busfill_last_failure_detail(void) { return g_last_detail.load(); }
 
 int busfill_gemm_kernel_for(int M, int N, int K) { return use_prefill(M, N, K, false, true) ? 1 : 0; }
 
+int busfill_gemm_launches(int M, int N, int K, int sm_count) {
+  if (M < 1 || N < 1 || K < kUnitK || K % kUnitK != 0) return BUSFILL_ERR_SHAPE;
+  if (sm_count <= 0) {
+    DeviceInfo di;
+    int dev = 0;
+    const int st = current_device(&di, &dev);
+    if (st != BUSFILL_OK) return st;
+    sm_count = di.sm_count;
+  }
+  if (!use_prefill(M, N, K, false, true)) return (M + 31) / 32;   // the decode kernel, 32 rows a launch
+  // the stream-K prefill launch, and the fix-up launch if it splits an item
+  const int S = K / kUnitK;
+  const long long items = (long long)((N + prefill::kPairRows - 1) / prefill::kPairRows) *
+                          ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
+  const long long units = items * S;
+  const int grid = (int)std::min<long long>(std::min<long long>(units, sm_count), prefill::kMaxSplitItems + 1);
+  prefill::SplitItems si;
+  split_items(units, S, grid, &si);
+  return si.n > 0 ? 2 : 1;
+}
+
 const char* busfill_status_string(int status) {
   switch (status) {
     case BUSFILL_OK: return "ok";

@@ -383,6 +383,15 @@ BUSFILL_API int busfill_set_option(int option, int value);
  * no reference counterpart. */
 BUSFILL_API int busfill_gemm_kernel_for(int M, int N, int K);
 
+/* Kernel launches one plain GEMM call of that shape makes on a device with
+ * sm_count SMs (sm_count <= 0: the current device): one decode launch per 32
+ * batch rows, or the prefill kernel and, when its stream-K ranges split a
+ * work item between CTAs, the fix-up kernel (with the per-stream workspace in
+ * place; a first call inside a graph capture takes whole items instead, one
+ * launch). A negative busfill_status for a bad shape. Diagnostic; no
+ * reference counterpart. */
+BUSFILL_API int busfill_gemm_launches(int M, int N, int K, int sm_count);
+
 /* Known-answer probe of the tcgen05 operand layouts the GEMM relies on, in the
  * spirit of kernels/frag_probe.cu:1-48: d[128, nb] = a[128, 64] * b[nb, 64]^T
  * with a in tensor memory and b in 128-byte-swizzled shared memory.
