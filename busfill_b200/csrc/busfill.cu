@@ -395,11 +395,15 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
       return BUSFILL_ERR_CUDA;
   }
 
-  for (int m0 = 0; m0 < M; m0 += 32) {
-    const int mc = std::min(32, M - m0);
-    const int nb = mc <= 16 ? 16 : 32;
-    const DecodeSchedule sch = nb == 16 ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count, 1 + swiglu)
-                                        : choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count, 1 + swiglu);
+  // plain GEMMs take up to 64 batch rows a launch (one pass over the weights
+  // for M <= 64); the fused SwiGLU and gathered GEMMs 32
+  const int step = (swiglu || gather) ? 32 : 64;
+  for (int m0 = 0; m0 < M; m0 += step) {
+    const int mc = std::min(step, M - m0);
+    const int nb = mc <= 16 ? 16 : mc <= 32 ? 32 : 64;
+    const DecodeSchedule sch = nb == 16   ? choose_schedule<FMT, 16, OutT>(dev, T, S, di.sm_count, 1 + swiglu)
+                               : nb == 32 ? choose_schedule<FMT, 32, OutT>(dev, T, S, di.sm_count, 1 + swiglu)
+                                          : choose_schedule<FMT, 64, OutT>(dev, T, S, di.sm_count, 1);
     const uint16_t* a_chunk = a + (size_t)m0 * K;
     if (!make_tmap_act3d(&ta, a_chunk, (uint64_t)mc, (uint64_t)K, (uint32_t)nb, kChunksPerUnit))
       return BUSFILL_ERR_CUDA;
@@ -415,7 +419,7 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
         p.gather.out[q] = reinterpret_cast<OutT*>(gather->out[q]) + (size_t)m0 * gather->ldc;
         p.gather.flag[q] = gather->flag[q];
       }
-      p.gather.signal = (m0 + 32 >= M) ? 1 : 0;
+      p.gather.signal = (m0 + step >= M) ? 1 : 0;
       if (m0 == 0 && gather->wait && gather->nwait > 0) {
         p.gather.wait = gather->wait;
         p.gather.wait_gen = gather->wait_gen;
@@ -446,8 +450,9 @@ int run_decode(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* 
                       : launch_decode_nb<FMT, 32, OutT, false, true>(di, tw, tws, ta, p, s);
     }
     if (!swiglu && !gather)
-      st = nb == 16 ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
-                    : launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s);
+      st = nb == 16   ? launch_decode_nb<FMT, 16, OutT>(di, tw, tws, ta, p, s)
+           : nb == 32 ? launch_decode_nb<FMT, 32, OutT>(di, tw, tws, ta, p, s)
+                      : launch_decode_nb<FMT, 64, OutT>(di, tw, tws, ta, p, s);
     if (st != BUSFILL_OK) return st;
   }
   return BUSFILL_OK;
@@ -758,7 +763,7 @@ int busfill_gemm_launches(int M, int N, int K, int sm_count) {
     if (st != BUSFILL_OK) return st;
     sm_count = di.sm_count;
   }
-  if (!use_prefill(M, N, K, false, true)) return (M + 31) / 32;   // the decode kernel, 32 rows a launch
+  if (!use_prefill(M, N, K, false, true)) return (M + 63) / 64;   // the decode kernel, 64 rows a launch
   // the stream-K prefill launch, and the fix-up launch if it splits an item
   const int S = K / kUnitK;
   const long long items = (long long)((N + prefill::kPairRows - 1) / prefill::kPairRows) *

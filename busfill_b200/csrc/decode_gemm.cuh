@@ -1,5 +1,6 @@
-// Batched dequant-fused 4-bit-weight GEMM for small batches (M <= 32 per
-// launch) on sm_100a:  C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 in, fp32
+// Batched dequant-fused 4-bit-weight GEMM for small batches (M <= 64 per
+// launch for plain GEMMs, 32 for the fused SwiGLU and gathered ones) on
+// sm_100a:  C[M, N] = A[M, K] * deq(W)[N, K]^T, fp16 in, fp32
 // accumulate.
 //
 // Replaces the reference kernel `busfill_q4` (kernels/busfill_v1a.cu:41-104,
@@ -131,7 +132,7 @@ struct DecodeTmem {
 // Largest cluster (K split) for a batch tile of NB rows: rank 0 receives the
 // other ranks' [128][NB] fp32 partials in shared memory.
 template <int NB>
-constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
+constexpr int max_cluster() { return NB == 64 ? 2 : NB == 32 ? 4 : 8; }
 
 // Weight ring depth: what shared memory leaves next to the activation slots
 // and rank 0's receive buffer. Even, so that stage s is always filled with
@@ -139,14 +140,17 @@ constexpr int max_cluster() { return NB == 32 ? 4 : 8; }
 // (a group that skipped the other group's phase of a stage could see that
 // stale phase as complete: mbarrier waits only tell parities apart).
 template <int NB, WFmt FMT>
-constexpr int w_stages() { return FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 4 : 6; }  // Q5_K / Q6_K: 22 / 26 KB
+constexpr int w_stages() {
+  // Q5_K / Q6_K stages are 22 / 26 KB; 64-row batches take 32 KB activation stages
+  return NB == 64 ? (FMT == WFmt::Q6K ? 2 : 4) : FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 4 : 6;
+}
 
 // Activation ring depth (one unit per stage), separate from the TMEM operand
 // slots so that a unit's activations are requested several units ahead: a
 // box waits behind the weight boxes in its SM's TMA queue (~1.2 us from issue
 // to landing under load on B200), longer than the three-slot operand cycle.
 template <int NB>
-constexpr int x_stages() { return NB == 32 ? 4 : 6; }
+constexpr int x_stages() { return NB == 64 ? 3 : NB == 32 ? 4 : 6; }
 
 template <int NB, WFmt FMT>
 struct DecodeSmem {
@@ -158,8 +162,7 @@ struct DecodeSmem {
   static_assert(kWStages % 2 == 0, "each weight stage must belong to one dequant group");
   static constexpr int kXStages = x_stages<NB>();
   static_assert(kXStages >= kSlots, "an activation stage per operand slot at least");
-  static constexpr int kXOff = kWOff + kWStages * kWStage;
-  static_assert(kXOff % 1024 == 0, "swizzled activation stages need 1 KB alignment");
+  static constexpr int kXOff = (kWOff + kWStages * kWStage + 1023) / 1024 * 1024;   // swizzled stages: 1 KB aligned
   static constexpr int kRedOff = kXOff + kXStages * kXSlotBytes;      // rank 0: [rank-1][128][NB] fp32 partials
   static constexpr int kRedRankBytes = kTileRows * NB * 4;
   static constexpr int kBarOff = kRedOff + (max_cluster<NB>() - 1) * kRedRankBytes;
@@ -244,7 +247,8 @@ template <WFmt FMT, int NB, typename OutT, bool SW = false, bool GA = false>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                        const __grid_constant__ CUtensorMap tmap_a, const DecodeParams p) {
-  static_assert(NB == 16 || NB == 32, "batch tile");
+  static_assert(NB == 16 || NB == 32 || NB == 64, "batch tile");
+  static_assert(NB != 64 || (!SW && !GA), "64-row batches: plain GEMMs (the epilogue's registers)");
   using L = DecodeSmem<NB, FMT>;
   using TM = DecodeTmem<NB>;
   constexpr bool kRows144 = aos_rows<FMT>();  // whole block rows per unit (block_q4_K / q5_K, 8 x block_q4_0)

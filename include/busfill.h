@@ -358,7 +358,8 @@ BUSFILL_API int busfill_version(void);
  *     1..8 forces that split where K/256 allows it (a tuning and test knob).
  *   BUSFILL_OPT_PREFILL_MIN_M: GEMMs with M >= value rows run the large-batch
  *     (prefill) kernel, one pass over the weights for all rows, instead of
- *     the decode kernel's launches of 32 rows; 0 (default) chooses by shape:
+ *     the decode kernel's launches of 64 rows (32 for the SwiGLU pairs and
+ *     the gathered GEMMs); 0 (default) chooses by shape:
  *     M > 64, or M > 32 when N <= K, for the plain GEMMs, whose prefill
  *     kernel splits the units of work evenly over all SMs (stream-K, with a
  *     per-stream workspace of 2 x SMs x 128 KB allocated on first use, never
@@ -378,13 +379,13 @@ BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,
  * N output columns and depth K runs with the current options: 0 = decode
- * kernel (launches of 32 rows), 1 = prefill kernel (one pass over the
+ * kernel (launches of 64 rows), 1 = prefill kernel (one pass over the
  * weights; by default for M > 64, and for M > 32 when N <= K). Diagnostic;
  * no reference counterpart. */
 BUSFILL_API int busfill_gemm_kernel_for(int M, int N, int K);
 
 /* Kernel launches one plain GEMM call of that shape makes on a device with
- * sm_count SMs (sm_count <= 0: the current device): one decode launch per 32
+ * sm_count SMs (sm_count <= 0: the current device): one decode launch per 64
  * batch rows, or the prefill kernel and, when its stream-K ranges split a
  * work item between CTAs, the fix-up kernel (with the per-stream workspace in
  * place; a first call inside a graph capture takes whole items instead, one

@@ -562,12 +562,12 @@ def test_gathered_call_of_a_rank_without_rows_is_a_no_op():
 
 
 def test_gemm_launch_count_by_shape():
-    """busfill_gemm_launches mirrors the dispatch: one decode launch per 32
+    """busfill_gemm_launches mirrors the dispatch: one decode launch per 64
     batch rows; the prefill kernel, plus its fix-up when the stream-K ranges
     over 148 SMs split a work item."""
     assert bf.gemm_launches(32, 5120, 5120, 148) == 1
     assert bf.gemm_launches(8, 5120, 5120, 148) == 1
-    assert bf.gemm_launches(64, 17408, 5120, 148) == 2          # N > K: two decode launches
+    assert bf.gemm_launches(64, 17408, 5120, 148) == 1          # N > K: one 64-row decode launch
     # M = 128, N = K = 5120: 20 pairs x 1 batch tile x 20 units over 148 CTAs splits items
     assert bf.gemm_launches(128, 5120, 5120, 148) == 2
     # 40 items x 20 units = 800 units over 40 CTAs: every range boundary on an item edge

@@ -135,6 +135,7 @@ SHAPES = [
     (8, 256, 8192),
     (5, 3840, 5120),   # 30 tiles: clusters of 3-4, ~5-7 units per CTA
     (2, 1024, 40960),  # 8 tiles x 160 units: 20 units per CTA, deep operand-slot reuse
+    (40, 1024, 512), (64, 2560, 1024), (57, 520, 256),   # N > K, 33-64 rows: one 64-row decode launch
 ]
 
 
@@ -207,6 +208,8 @@ KSPLIT_CASES = [
     (5, 3, 2560, 5120),
     (8, 5, 3072, 2048),    # 24 tiles over <= 18 clusters
     (8, 1, 128, 2048),     # one unit per rank
+    (2, 64, 2048, 1024),   # 64-row batch tile, split over a cluster of 2
+    (2, 48, 5120, 512),    # 64-row batch tile, 40 tiles, two tiles per cluster for some
 ]
 
 

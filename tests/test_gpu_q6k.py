@@ -75,7 +75,7 @@ def check(c, a, w32):
 
 
 @pytest.mark.parametrize("m,n,k", [(1, 128, 256), (8, 640, 1024), (17, 200, 2048), (32, 1280, 5120), (33, 384, 768),
-                                   (5, 3840, 5120), (2, 512, 16384)])
+                                   (5, 3840, 5120), (2, 512, 16384), (48, 1024, 512), (64, 2048, 1024)])
 def test_gemm_q6k_decode(m, n, k):
     blocks = orc.gen_q6k(n, k, seed=m + n + k)
     a = orc.gen_activations(m, k, seed=m * 3 + k)
