@@ -37,28 +37,27 @@ std::atomic<unsigned> g_last_detail{0};
 std::atomic<int> g_use_pdl{1};
 std::atomic<int> g_force_ksplit{0};  // 0 = automatic
 // Batch size from which GEMMs take the prefill kernel (one pass over the
-// weights for all rows) instead of the decode kernel (32 rows a launch).
+// weights for all rows) instead of the decode kernel (64 rows a launch).
 // 0 = automatic:
 //  * with the stream-K workspace (plain GEMMs): M > kStreamKMinM, or M > 32
-//    when N <= K. Every SM gets an equal share of the units however few work
-//    items there are. Measured on B200 (Q4_K, us, decode vs prefill): three
-//    or more decode launches lose on every config-4 shape (M = 96: 31 vs 18
-//    at K = N = 5120, 59 vs 33 at N = 5120, K = 17408, 48 vs 37 at N = 17408,
-//    K = 5120); two lose where N <= K (M = 33: 19.8 vs 15.5, 38.6 vs 32.3) and
-//    win where the decode kernel has many tiles (N = 17408, K = 5120, M = 33:
-//    32.3 vs 38.0).
+//    when N <= K and K >= kPrefillMinK. Measured on B200 (Q4_K, us, decode vs
+//    prefill, M = 33 / 64): K = N = 5120 14.2 / 14.5 vs 15.1 / 15.8; N = 5120,
+//    K = 8192 18.8 / 19.2 vs 19.7 / 20.1; N = 5120, K = 17408 32.1 / 32.5 vs
+//    29.9 / 30.3; N = 10240, K = 5120 19.1 / 19.7 vs 23.0 / 24.1; at M = 96
+//    the prefill kernel wins on every shape (17.5 vs 25.0 at 5120^2).
 //  * without it (SwiGLU pairs, the no-allocation entry point, a first call
 //    inside a graph capture): M >= 128 and at least kPrefillMinItems work
 //    items, since whole items go one per SM (measured: M = 128, N = 5120,
 //    K = 17408 takes 157 us as 20 items, 93 us as four decode launches).
 constexpr int kStreamKMinM = 64;
+constexpr int kPrefillMinK = 12288;
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
 
 bool use_prefill(int M, int N, int K, bool swiglu = false, bool stream_k = false) {
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
-  if (stream_k && !swiglu) return M > kStreamKMinM || (M > 32 && N <= K);
+  if (stream_k && !swiglu) return M > kStreamKMinM || (M > 32 && N <= K && K >= kPrefillMinK);
   const int pair_rows = swiglu ? kTileRows : prefill::kPairRows;  // SwiGLU items: gate tile j + up tile j
   const long long items = (long long)((N + pair_rows - 1) / pair_rows) *
                           ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);

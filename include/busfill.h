@@ -360,7 +360,8 @@ BUSFILL_API int busfill_version(void);
  *     (prefill) kernel, one pass over the weights for all rows, instead of
  *     the decode kernel's launches of 64 rows (32 for the SwiGLU pairs and
  *     the gathered GEMMs); 0 (default) chooses by shape:
- *     M > 64, or M > 32 when N <= K, for the plain GEMMs, whose prefill
+ *     M > 64, or M > 32 when N <= K and K >= 12288, for the plain GEMMs,
+ *     whose prefill
  *     kernel splits the units of work evenly over all SMs (stream-K, with a
  *     per-stream workspace of 2 x SMs x 128 KB allocated on first use, never
  *     during a graph capture); M >= 128 and at least 64 work
@@ -380,7 +381,8 @@ BUSFILL_API int busfill_set_option(int option, int value);
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,
  * N output columns and depth K runs with the current options: 0 = decode
  * kernel (launches of 64 rows), 1 = prefill kernel (one pass over the
- * weights; by default for M > 64, and for M > 32 when N <= K). Diagnostic;
+ * weights; by default for M > 64, and for M > 32 when N <= K and
+ * K >= 12288). Diagnostic;
  * no reference counterpart. */
 BUSFILL_API int busfill_gemm_kernel_for(int M, int N, int K);
 

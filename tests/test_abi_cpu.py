@@ -415,12 +415,14 @@ def test_ksplit_option_values():
 
 def test_kernel_choice_by_shape():
     """Default dispatch of the plain GEMMs: the stream-K prefill kernel for
-    M > 64, and for M > 32 when N <= K; the decode kernel otherwise. The option
-    forces a plain M threshold and 0 restores the default."""
+    M > 64, and for M > 32 when N <= K and K >= 12288; the decode kernel
+    otherwise. The option forces a plain M threshold and 0 restores the
+    default."""
     bf.load_library()
     assert not bf.uses_prefill(32, 5120, 5120)
-    assert not bf.uses_prefill(64, 17408, 5120)   # many decode tiles: two decode launches win
-    assert bf.uses_prefill(33, 5120, 5120) and bf.uses_prefill(64, 5120, 17408)   # N <= K: stream-K wins
+    assert not bf.uses_prefill(64, 17408, 5120)   # many decode tiles: one 64-row launch wins
+    assert not bf.uses_prefill(33, 5120, 5120) and not bf.uses_prefill(64, 5120, 8192)
+    assert bf.uses_prefill(33, 5120, 17408) and bf.uses_prefill(64, 5120, 17408)   # long K: stream-K wins
     assert bf.uses_prefill(65, 17408, 5120)       # from three decode launches on
     assert bf.uses_prefill(128, 5120, 17408) and bf.uses_prefill(128, 17408, 5120)
     assert bf.uses_prefill(512, 5120, 5120) and bf.uses_prefill(2048, 5120, 17408)
@@ -568,6 +570,7 @@ def test_gemm_launch_count_by_shape():
     assert bf.gemm_launches(32, 5120, 5120, 148) == 1
     assert bf.gemm_launches(8, 5120, 5120, 148) == 1
     assert bf.gemm_launches(64, 17408, 5120, 148) == 1          # N > K: one 64-row decode launch
+    assert bf.gemm_launches(48, 5120, 5120, 148) == 1           # K < 12288: one 64-row decode launch
     # M = 128, N = K = 5120: 20 pairs x 1 batch tile x 20 units over 148 CTAs splits items
     assert bf.gemm_launches(128, 5120, 5120, 148) == 2
     # 40 items x 20 units = 800 units over 40 CTAs: every range boundary on an item edge
