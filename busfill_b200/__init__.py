@@ -164,6 +164,12 @@ def set_prefill_min_m(m: int) -> None:
     _check(_lib().busfill_set_option(3, int(m)), "busfill_set_option")
 
 
+def set_prefill_batch_tile(bt: int) -> None:
+    """Batch rows per work item of the prefill kernel: 128 (two weight tiles)
+    or 256 (one weight tile, MMA N = 256); 0 restores the choice by M."""
+    _check(_lib().busfill_set_option(5, int(bt)), "busfill_set_option")
+
+
 # ---------------------------------------------------------------------------
 # torch-tensor wrappers
 # ---------------------------------------------------------------------------

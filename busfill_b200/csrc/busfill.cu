@@ -54,14 +54,32 @@ constexpr int kPrefillMinK = 12288;
 constexpr int kPrefillMinItems = 64;
 std::atomic<int> g_prefill_min_m{0};
 
+// Batch rows per prefill work item (prefill_gemm.cuh, Geo): 256 (one weight
+// tile, MMA N = 256, half the dequant per flop) from kWideMinM rows, else 128
+// (two weight tiles); SwiGLU pairs always 128 (gate and up accumulators).
+// BUSFILL_OPT_PREFILL_BATCH_TILE forces 128 or 256.
+constexpr int kWideMinM = 256;
+std::atomic<int> g_prefill_bt{0};
+
+int prefill_bt(int M, bool swiglu) {
+  if (swiglu) return 128;
+  const int forced = g_prefill_bt.load();
+  if (forced) return forced;
+  return M >= kWideMinM ? 256 : 128;
+}
+
+// work items of a prefill launch: weight-row groups x batch tiles
+long long prefill_items(int M, int N, bool swiglu) {
+  const int bt = prefill_bt(M, swiglu);
+  const int item_rows = swiglu ? kTileRows : bt == 128 ? 2 * kTileRows : kTileRows;  // SwiGLU: gate tile j + up tile j
+  return (long long)((N + item_rows - 1) / item_rows) * ((M + bt - 1) / bt);
+}
+
 bool use_prefill(int M, int N, int K, bool swiglu = false, bool stream_k = false) {
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
   if (stream_k && !swiglu) return M > kStreamKMinM || (M > 32 && N <= K && K >= kPrefillMinK);
-  const int pair_rows = swiglu ? kTileRows : prefill::kPairRows;  // SwiGLU items: gate tile j + up tile j
-  const long long items = (long long)((N + pair_rows - 1) / pair_rows) *
-                          ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
-  return M >= 128 && items >= kPrefillMinItems;
+  return M >= 128 && prefill_items(M, N, swiglu) >= kPrefillMinItems;
 }
 
 // ---------------------------------------------------------------------------
@@ -184,8 +202,8 @@ int get_error_words(int dev, cudaStream_t s, unsigned** out) {
   return BUSFILL_OK;
 }
 
-// The prefill kernel's stream-K partial tiles: two fp32 tiles of 128 batch
-// rows x 256 weight rows per CTA, one workspace per (device, stream) so that
+// The prefill kernel's stream-K partial tiles: two fp32 tiles of 32768
+// values (batch tile x item rows) per CTA, one workspace per (device, stream) so that
 // GEMMs on different streams never share one. Allocated on first use; never
 // while the stream is capturing a graph (an allocation would end the
 // capture), in which case the kernel runs without stream-K.
@@ -477,20 +495,21 @@ void split_items(long long t, int s, int g, prefill::SplitItems* out) {
 }
 
 // `part`: the stream's partial-tile workspace (stream-K), or nullptr for whole
-// items round-robin; SwiGLU pairs always take whole items.
-template <WFmt FMT, typename OutT>
-int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-                int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr,
-                float* part = nullptr) {
+// items round-robin; SwiGLU pairs always take whole items. BT: batch tile.
+template <WFmt FMT, typename OutT, int BT>
+int run_prefill_bt(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
+                   int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up, float* part) {
+  constexpr int kItemRows = prefill::Geo<BT>::kItemRows;
   const int S = K / kUnitK;
   const int swiglu = w_up ? 1 : 0;
+  if (swiglu && BT != 128) return BUSFILL_ERR_INVALID_ARG;
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
   if constexpr (aos_rows<FMT>()) {
-    // one 256-row box per unit, or with SwiGLU one 128-row box from each matrix
+    // one box of the item's rows per unit, or with SwiGLU one 128-row box from each matrix
     constexpr int ub = unit_row_bytes<FMT>();
     const uint64_t row = (uint64_t)S * ub;
-    const uint32_t box_rows = swiglu ? kTileRows : prefill::kPairRows;
+    const uint32_t box_rows = swiglu ? kTileRows : kItemRows;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, ub, box_rows,
                       CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
@@ -499,25 +518,26 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
                                 box_rows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
     if (FMT == WFmt::Q6K && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)N, (uint64_t)S,
-                                          (uint64_t)N * 2, prefill::kPairRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+                                          (uint64_t)N * 2, kItemRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   } else {
     if (swiglu) return BUSFILL_ERR_INVALID_ARG;
     if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
-                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_128B))
+                      kItemRows, CU_TENSOR_MAP_SWIZZLE_128B))
       return BUSFILL_ERR_CUDA;
     if (!make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)K / 32, (uint64_t)N, (uint64_t)K / 16, 8,
-                      prefill::kPairRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+                      kItemRows, CU_TENSOR_MAP_SWIZZLE_NONE))
       return BUSFILL_ERR_CUDA;
   }
-  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, prefill::kBatchTile, 2)) return BUSFILL_ERR_CUDA;
+  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, BT, prefill::Geo<BT>::kXChunks)) return BUSFILL_ERR_CUDA;
 
-  const void* kern = reinterpret_cast<const void*>(prefill_gemm_kernel<FMT, OutT>);
+  const void* kern = reinterpret_cast<const void*>(prefill_gemm_kernel<FMT, OutT, BT>);
   {
     static std::once_flag once[64];
     static cudaError_t err[64];
     std::call_once(once[dev & 63], [&] {
-      err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::Smem<FMT>::kAlloc);
+      err[dev & 63] =
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, prefill::Smem<FMT, BT>::kAlloc);
     });
     if (err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
   }
@@ -527,18 +547,19 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
   p.M = M;
   p.N = N;
   p.K = K;
-  p.pairs = swiglu ? (N + kTileRows - 1) / kTileRows : (N + prefill::kPairRows - 1) / prefill::kPairRows;
+  p.pairs = swiglu ? (N + kTileRows - 1) / kTileRows : (N + kItemRows - 1) / kItemRows;
   p.swiglu = swiglu;
-  p.btiles = (M + prefill::kBatchTile - 1) / prefill::kBatchTile;
+  p.btiles = (M + BT - 1) / BT;
   p.units = S;
   const long long items = (long long)p.pairs * p.btiles;
   const long long units = items * S;
+  if (units > INT32_MAX) return BUSFILL_ERR_SHAPE;   // the kernel counts units in an int
   p.part = swiglu ? nullptr : part;
   const int grid = p.part ? (int)std::min<long long>(std::min<long long>(units, di.sm_count), prefill::kMaxSplitItems + 1)
                            : (int)std::min<long long>(items, di.sm_count);
   void* args[] = {&tw, &tws, &ta, &p};
-  if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::Smem<FMT>::kAlloc, s, args, g_use_pdl.load() != 0) !=
-      cudaSuccess) {
+  if (launch(kern, dim3(grid), dim3(prefill::kThreads), prefill::Smem<FMT, BT>::kAlloc, s, args,
+             g_use_pdl.load() != 0) != cudaSuccess) {
     cudaGetLastError();
     return BUSFILL_ERR_LAUNCH;
   }
@@ -550,14 +571,25 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
     OutT* cc = reinterpret_cast<OutT*>(c);
     int m = M, n = N, bts = p.btiles;
     void* rargs[] = {&cpart, &cc, &m, &n, &bts, &si};
-    const int rows = std::min(M, prefill::kBatchTile);
-    if (launch(reinterpret_cast<const void*>(prefill_reduce_kernel<OutT>), dim3(si.n, (rows + 3) / 4),
-               dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
+    const int rows = std::min(M, BT);
+    constexpr int kRowsPerBlock = 256 / (kItemRows / 4);
+    if (launch(reinterpret_cast<const void*>(prefill_reduce_kernel<OutT, BT>),
+               dim3(si.n, (rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(256), 0, s, rargs,
+               g_use_pdl.load() != 0) != cudaSuccess) {
       cudaGetLastError();
       return BUSFILL_ERR_LAUNCH;
     }
   }
   return BUSFILL_OK;
+}
+
+template <WFmt FMT, typename OutT>
+int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
+                int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr,
+                float* part = nullptr) {
+  if (prefill_bt(M, w_up != nullptr) == 256)
+    return run_prefill_bt<FMT, OutT, 256>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
+  return run_prefill_bt<FMT, OutT, 128>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
 }
 
 // Decode (M < prefill threshold) or prefill kernel for one GEMM.
@@ -765,9 +797,7 @@ int busfill_gemm_launches(int M, int N, int K, int sm_count) {
   if (!use_prefill(M, N, K, false, true)) return (M + 63) / 64;   // the decode kernel, 64 rows a launch
   // the stream-K prefill launch, and the fix-up launch if it splits an item
   const int S = K / kUnitK;
-  const long long items = (long long)((N + prefill::kPairRows - 1) / prefill::kPairRows) *
-                          ((M + prefill::kBatchTile - 1) / prefill::kBatchTile);
-  const long long units = items * S;
+  const long long units = prefill_items(M, N, false) * S;
   const int grid = (int)std::min<long long>(std::min<long long>(units, sm_count), prefill::kMaxSplitItems + 1);
   prefill::SplitItems si;
   split_items(units, S, grid, &si);
@@ -807,6 +837,11 @@ int busfill_set_option(int option, int value) {
   if (option == BUSFILL_OPT_EXACT_KQUANT) {
     // accepted for compatibility: every K-quant operand is exact
     return value == 0 || value == 1 ? BUSFILL_OK : BUSFILL_ERR_INVALID_ARG;
+  }
+  if (option == BUSFILL_OPT_PREFILL_BATCH_TILE) {
+    if (value != 0 && value != 128 && value != 256) return BUSFILL_ERR_INVALID_ARG;
+    g_prefill_bt.store(value);
+    return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;
 }

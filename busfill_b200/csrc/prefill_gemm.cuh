@@ -7,26 +7,30 @@
 // The reference has no such path (its kernel computes batch rows < 32 only,
 // kernels/busfill_v1a.cu:41-104); the shapes are BASELINE config 4.
 //
-// Shape of the computation. A work item is two 128-row weight tiles (256
-// weight rows) x 128 batch rows, looped over K in units of 256. The weights
-// of a unit are dequantized into tensor memory (the MMA's A operand, one
-// 128-lane tile per weight tile) and each tile's accumulator [128 weight rows
-// x 128 batch rows] fp32 lives in TMEM next to them:
-//   columns   0..127  accumulator of weight tile 0
-//   columns 128..255  accumulator of weight tile 1
-//   columns 256..511  four half-unit operand slots (t, h) of 64 columns:
-//                     tile t, K half h (chunks 2h, 2h+1) of the current unit.
-// The MMAs of a unit run (t0,h0) (t1,h0) (t0,h1) (t1,h1), 8 MMAs of
-// 128x128x16 each, so a half slot is refilled while the three other MMA
-// blocks run. Activations come as one 3-D TMA box per K half (2 chunks x 128
-// rows x 64 values, 32 KB) and weights as one box per unit for both tiles
-// (256 rows, 36 KB): an SM's TMA unit takes a roughly fixed time per box
-// (~0.5 us with every SM loading, measured on B200), so few large boxes. The
-// weight ring is three units deep: a weight box lands ~1.7 us after issue
-// under load, longer than a unit's MMAs (~1.3 us).
+// Shape of the computation. A work item is BT batch rows x the weight rows
+// of one or two 128-row tiles (Geo below), looped over K in units of 256.
+// The weights of a unit are dequantized into tensor memory (the MMA's A
+// operand) and the fp32 accumulators live in TMEM next to them:
+//   columns   0..255  accumulators: BT = 128, tile 0 then tile 1 [128 weight
+//                     rows x 128 batch rows] each; BT = 256, the one tile
+//                     [128 weight rows x 256 batch rows]
+//   columns 256..511  four half-unit operand slots of 64 columns (one K half,
+//                     chunks 2h and 2h+1, of one tile)
+// BT = 256 (from M = 256) halves the dequant work per flop and lets two
+// units sit in TMEM at once; BT = 128 serves M < 256 and the SwiGLU pairs
+// (gate and up accumulators of the same rows). Activations come as 3-D TMA
+// boxes of 32 KB (BT = 128: a K half, 2 chunks x 128 rows; BT = 256: one
+// chunk x 256 rows, released as soon as its four MMAs complete) and weights
+// as one box per unit of the item's rows.
 //
 // Measured on B200: a 128x128x16 TS MMA (A in TMEM) takes ~74 cycles back to
-// back, 92% of the dense fp16 rate; a unit (32 MMAs) ~2400 cycles.
+// back, 92% of the dense fp16 rate; a unit (2 x 128 x 256 x 256 MACs) ~2400
+// cycles. A per-unit clock64 trace at M = 512, N = 17408, K = 5120 (BT = 256)
+// puts a unit at ~2900-3100 cycles of the MMA warp: ~1600 issuing MMAs (the
+// tensor pipe's back-pressure), ~800 waiting for activation boxes (L2 to SM
+// traffic: 128 KB of activations per unit) and ~500 of loop overhead. The
+// loops step their (item, unit) cursor instead of dividing: a 64-bit
+// division per unit had cost each producer and the MMA warp ~400-600 cycles.
 //
 // Handoffs: a dequant warp group publishes a half slot with a named-barrier
 // arrive that the MMA warp syncs on (no mbarrier round trip on the path of
@@ -36,12 +40,12 @@
 // after a failed wait, the arrivals are not).
 //
 // Warp roles (16 warps, one CTA per SM, persistent over work items):
-//   0      weight TMA producer (3-stage ring of 36 KB)
-//   1      activation TMA producer (3-stage ring of 32 KB); TMEM allocator
+//   0      weight TMA producer (ring of 2-3 units)
+//   1      activation TMA producer (ring of 32 KB stages); TMEM allocator
 //   3      MMA issuer (converged warp, one elected thread issues)
-//   4-7    dequant of weight tile 0, 8-11 of weight tile 1: thread (warp%4,
-//          lane) owns tile row 32*(warp%4)+lane, both K halves of each unit
-//   12-15  epilogue: reads both accumulators once per item, writes C
+//   4-11   dequant, two groups of four warps (see Geo): thread (warp%4, lane)
+//          owns row 32*(warp%4)+lane of its weight tile
+//   12-15  epilogue: reads the accumulators once per item, writes C
 //   2      idle
 //
 // Work order: item = pair * B + batch_tile. With a partial-tile workspace
@@ -69,29 +73,53 @@ namespace busfill {
 namespace prefill {
 
 constexpr int kThreads = 512;
-constexpr int kBatchTile = 128;                 // batch rows per item = MMA N
-constexpr int kPairRows = 2 * kTileRows;        // weight rows per item
-constexpr int kXStages = 3;                     // half units (2 chunks each)
-constexpr int kXChunk = kBatchTile * 128;       // 64 values x 128 rows, 16 KB
-constexpr int kXStage = 2 * kXChunk;            // one K half of a unit, 32 KB
-constexpr int kAccCols = kBatchTile;            // per weight tile
-constexpr int kSlotCols = 64;                   // half a unit
-constexpr int kSlot0 = 2 * kAccCols;
+constexpr int kDequantWarp0 = 4, kEpilogueWarp0 = 12;
+constexpr int kSlotCols = 64;                   // half a unit of one weight tile
+constexpr int kSlot0 = 256;                     // after the accumulators
 constexpr int kTmemCols = 512;
 static_assert(kSlot0 + 4 * kSlotCols == kTmemCols, "TMEM map");
 constexpr uint32_t kBarSlot0 = 1;          // named barrier of half slot s: kBarSlot0 + s
-constexpr uint32_t kSlotBarThreads = 160;  // the tile's 4 dequant warps + the MMA warp
+constexpr uint32_t kSlotBarThreads = 160;  // the slot's 4 dequant warps + the MMA warp
+constexpr int kXStageBytes = 32768;        // one activation stage
 
-// shared memory map (the weight stage holds both tiles' unit: 256 rows, then
-// the rows' second plane: Q4_0 32 KB of nibbles and 4 KB of scales; Q6_K
-// 52 KB of block bodies and 512 B of d)
-template <WFmt FMT>
+// Item geometry by batch tile BT (= the MMA's N):
+//   BT = 128: two 128-row weight tiles x 128 batch rows; an activation stage
+//             is a K half of a unit (2 chunks x 128 rows); half slot s = 2t + h
+//             holds tile t's K half h of the current unit.
+//   BT = 256: one weight tile x 256 batch rows (MMAs of 128x256x16); a stage
+//             is one chunk x 256 rows; half slot s = 2 (u % 2) + h holds K half
+//             h of unit u, so two units are in TMEM at once. Every dequantized
+//             weight feeds twice the batch rows: half the dequant per flop.
+// Dequant warp group g (four warps, one per TMEM lane quarter) writes, of
+// every unit, BT = 128: both K halves of tile g (half slots 2g, 2g + 1);
+// BT = 256: K half g, into half slot 2 (u % 2) + g. Every dequant warp takes
+// every unit, so each waits on every phase of the barriers it uses (a warp
+// that skipped units could see a barrier two phases back as complete).
+template <int BT>
+struct Geo {
+  static_assert(BT == 128 || BT == 256, "batch tile");
+  static constexpr int kTiles = BT == 128 ? 2 : 1;          // weight tiles per item
+  static constexpr int kItemRows = kTiles * kTileRows;      // weight rows per item
+  static constexpr int kXChunks = BT == 128 ? 2 : 1;        // 64-value chunks per activation stage
+  static constexpr int kXPerUnit = kChunksPerUnit / kXChunks;
+  static constexpr int kXChunkBytes = BT * 128;             // 64 values x BT rows
+  static_assert(kXChunks * kXChunkBytes == kXStageBytes, "activation stage");
+  static_assert(kTiles * BT == kSlot0, "accumulators: 256 columns");
+};
+constexpr int kPartElems = 256 * 128;   // one partial tile, fp32: BT batch rows x item rows
+
+// shared memory map: weight stages of one unit of the item's rows (then the
+// rows' second plane: Q4_0 scales, Q6_K d), activation stages, barriers
+template <WFmt FMT, int BT>
 struct Smem {
-  static constexpr int kWStage = 2 * wstage_bytes<FMT>();
-  static constexpr int kWStages = FMT == WFmt::Q5K || FMT == WFmt::Q6K ? 2 : 3;   // Q5_K / Q6_K: 44 / 52.5 KB
+  using GE = Geo<BT>;
+  static constexpr int kWStage = GE::kTiles * wstage_bytes<FMT>();
+  static constexpr int kXStages = BT == 128 ? 3 : 5;
+  static constexpr int kWStages =
+      kXStages * kXStageBytes + 3 * kWStage + 3072 <= 232448 ? 3 : 2;   // Q5_K / Q6_K: 2
   static constexpr int kWOff = 0;
-  static constexpr int kXOff = kWOff + kWStages * kWStage;
-  static constexpr int kBarOff = kXOff + kXStages * kXStage;
+  static constexpr int kXOff = (kWOff + kWStages * kWStage + 1023) / 1024 * 1024;
+  static constexpr int kBarOff = kXOff + kXStages * kXStageBytes;
   static constexpr int bWFull = 0, bWEmpty = bWFull + kWStages;
   static constexpr int bXFull = bWEmpty + kWStages, bXEmpty = bXFull + kXStages;
   static constexpr int bSDone = bXEmpty + kXStages;  // half slot s = 2t + h read by its MMAs (commit)
@@ -100,7 +128,7 @@ struct Smem {
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
   static constexpr int kBytes = kMiscOff + 64;
   static constexpr int kAlloc = kBytes + 1024;
-  static_assert(kXOff % 1024 == 0 && kXStage % 1024 == 0, "swizzled operands need 1 KB alignment");
+  static_assert(kXOff % 1024 == 0, "swizzled operands need 1 KB alignment");
   static_assert(kAlloc <= 232448, "dynamic shared memory per block on sm_100");
 };
 
@@ -108,11 +136,11 @@ struct Params {
   void* c;            // [M, N] row-major, OutT
   unsigned* error;    // device error word (+1: first failure record)
   int M, N, K;
-  int pairs;          // P = ceil(N / 256); SwiGLU: ceil(N / 128) (gate tile j, up tile j)
-  int btiles;         // B = ceil(M / 128)
+  int pairs;          // P = ceil(N / item rows); SwiGLU: ceil(N / 128) (gate tile j, up tile j)
+  int btiles;         // B = ceil(M / BT)
   int units;          // S = K / 256
   int swiglu;         // 1: C = silu(A Wg^T) * (A Wu^T); tmap_w gate, tmap_ws up (128-row boxes)
-  float* part;        // stream-K partial tiles [2 G][128 batch rows][256 weight rows], or nullptr
+  float* part;        // stream-K partial tiles [2 G][BT batch rows][item rows], or nullptr
 };
 
 // Stream-K range of CTA c of g over t units: [first_unit(c), first_unit(c + 1)).
@@ -121,25 +149,26 @@ __host__ __device__ __forceinline__ long long first_unit(long long t, int c, int
 __host__ __device__ __forceinline__ int cta_of_unit(long long t, long long x, int g) {
   return (int)(((x + 1) * g - 1) / t);
 }
-constexpr int kPartElems = kPairRows * kBatchTile;   // one partial tile, fp32
-
 }  // namespace prefill
 
-template <WFmt FMT, typename OutT>
+template <WFmt FMT, typename OutT, int BT>
 __global__ void __launch_bounds__(prefill::kThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_ws,
                         const __grid_constant__ CUtensorMap tmap_a, const prefill::Params p) {
   using namespace prefill;
-  using SM = Smem<FMT>;
+  using SM = Smem<FMT, BT>;
+  using GE = Geo<BT>;
+  constexpr int kTiles = GE::kTiles, kItemRows = GE::kItemRows, kXPerUnit = GE::kXPerUnit;
+  constexpr int kXChunks = GE::kXChunks, kXChunkBytes = GE::kXChunkBytes, kXStages = SM::kXStages;
   constexpr int kWStage = SM::kWStage, kWStages = SM::kWStages, kWOff = SM::kWOff, kXOff = SM::kXOff;
   constexpr int kBarOff = SM::kBarOff, kMiscOff = SM::kMiscOff, kNumBars = SM::kNumBars;
   constexpr int bWFull = SM::bWFull, bWEmpty = SM::bWEmpty, bXFull = SM::bXFull, bXEmpty = SM::bXEmpty;
   constexpr int bSDone = SM::bSDone, bAccFull = SM::bAccFull, bAccEmpty = SM::bAccEmpty;
   constexpr int bFinal = SM::bFinal;
-  constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, kBatchTile);
+  constexpr uint32_t kIdesc = make_idesc_f16_f32(kTileRows, BT);
   constexpr bool kRows144 = aos_rows<FMT>();
   constexpr int kRowBytes = unit_row_bytes<FMT>();
-  constexpr int kAuxOff = kPairRows * kRowBytes;   // second plane of the stage's 256 rows
+  constexpr int kAuxOff = kItemRows * kRowBytes;   // second plane of the stage's rows
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_s = smem_u32(smem_raw);
@@ -158,16 +187,24 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   const long long T = (long long)items * S;
   const long long g0 = sk ? first_unit(T, bid, G) : 0;
   const int nunits = sk ? (int)(first_unit(T, bid + 1, G) - g0) : ((items - bid + G - 1) / G) * S;
-  // item and unit k of this CTA's u-th unit
+  // item and unit k of this CTA's u-th unit (T < 2^31: items x S units fit
+  // an int); the role loops step (it, k) with next_unit instead, a division
+  // per unit costing the MMA and producer warps hundreds of cycles each
   auto unit_at = [&](int u, int& it, int& k) {
     if (sk) {
-      const long long gu = g0 + u;
-      it = (int)(gu / S);
-      k = (int)(gu - (long long)it * S);
+      const int gu = (int)g0 + u;
+      it = gu / S;
+      k = gu - it * S;
     } else {
       const int j = u / S;
       k = u - j * S;
       it = bid + j * G;
+    }
+  };
+  auto next_unit = [&](int& it, int& k) {
+    if (++k == S) {
+      k = 0;
+      it += sk ? 1 : G;
     }
   };
   // pieces: the (partial) items of this CTA, in order
@@ -187,15 +224,13 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     return ok;
   };
   auto bar_count = [&](int b) -> uint32_t {
-    if (b >= bWEmpty && b < bWEmpty + kWStages) return 8;  // both tiles' dequant warps
+    if (b >= bWEmpty && b < bWEmpty + kWStages) return 8;  // every dequant warp
     if (b == bAccEmpty) return 4;                          // the epilogue warps
     return 1;                                              // TMA expect_tx arrivals, MMA commits
   };
 
-  // weight TMA of this CTA's unit u into stage u % kWStages
-  auto issue_w = [&](int u) {
-    int it, k;
-    unit_at(u, it, k);
+  // weight TMA of this CTA's unit u (item it, K unit k) into stage u % kWStages
+  auto issue_w = [&](int u, int it, int k) {
     const int pair = it / p.btiles;
     const int s = u % kWStages;
     const uint32_t dst = sbase + kWOff + s * kWStage;
@@ -206,24 +241,22 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         tma_load_2d(dst + wstage_bytes<FMT>(), &tmap_ws, k * kRowBytes, pair * kTileRows, BAR(bWFull + s),
                     kPolicyEvictLast);
       } else {
-        tma_load_2d(dst, &tmap_w, k * kRowBytes, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
-        if constexpr (FMT == WFmt::Q6K)  // the 256 rows' block scales d of unit k ([K/256][N] plane)
-          tma_load_2d(dst + kAuxOff, &tmap_ws, pair * kPairRows, k, BAR(bWFull + s), kPolicyEvictLast);
+        tma_load_2d(dst, &tmap_w, k * kRowBytes, pair * kItemRows, BAR(bWFull + s), kPolicyEvictLast);
+        if constexpr (FMT == WFmt::Q6K)  // the item rows' block scales d of unit k ([K/256][N] plane)
+          tma_load_2d(dst + kAuxOff, &tmap_ws, pair * kItemRows, k, BAR(bWFull + s), kPolicyEvictLast);
       }
     } else {
-      tma_load_2d(dst, &tmap_w, k * 128, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
-      tma_load_2d(dst + kAuxOff, &tmap_ws, k * 8, pair * kPairRows, BAR(bWFull + s), kPolicyEvictLast);
+      tma_load_2d(dst, &tmap_w, k * 128, pair * kItemRows, BAR(bWFull + s), kPolicyEvictLast);
+      tma_load_2d(dst + kAuxOff, &tmap_ws, k * 8, pair * kItemRows, BAR(bWFull + s), kPolicyEvictLast);
     }
   };
-  // activations of half unit v = 2u + h (chunks 2h, 2h+1 of unit u) into stage v % kXStages
-  auto issue_x = [&](int v) {
-    const int u = v >> 1, h = v & 1;
-    int it, k;
-    unit_at(u, it, k);
+  // activation piece v = kXPerUnit u + c (chunks c kXChunks .. of unit u: item
+  // it, K unit k) into stage v % kXStages
+  auto issue_x = [&](int v, int it, int k, int c) {
     const int bt = it % p.btiles;
     const int s = v % kXStages;
-    mbar_arrive_expect_tx(BAR(bXFull + s), kXStage);
-    tma_load_3d(sbase + kXOff + s * kXStage, &tmap_a, 0, bt * kBatchTile, k * kChunksPerUnit + 2 * h,
+    mbar_arrive_expect_tx(BAR(bXFull + s), kXStageBytes);
+    tma_load_3d(sbase + kXOff + s * kXStageBytes, &tmap_a, 0, bt * BT, k * kChunksPerUnit + c * kXChunks,
                 BAR(bXFull + s), kPolicyEvictLast);
   };
 
@@ -239,7 +272,11 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     for (int b = lane; b < kNumBars; b += 32) mbar_init(BAR(b), bar_count(b));
     fence_mbar_init();
     __syncwarp();
-    if (lane < w_early) issue_w(lane);
+    if (lane < w_early) {
+      int it, k;
+      unit_at(lane, it, k);
+      issue_w(lane, it, k);
+    }
     __syncwarp();
   } else if (warp == 1) {
     tmem_alloc(sbase + kMiscOff, prefill::kTmemCols);
@@ -254,12 +291,15 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
   if (warp == 0) {
     // ---------------- weight producer ----------------
     int issued = w_early;
+    int it, k;
+    unit_at(w_early, it, k);
     for (int u = w_early; u < nunits; ++u) {
       diag_unit = u;
       if (!warp_wait(BAR(bWEmpty + u % kWStages), ((u / kWStages) & 1) ^ 1)) break;
-      if (elect_one()) issue_w(u);
+      if (elect_one()) issue_w(u, it, k);
       __syncwarp();
       issued = u + 1;
+      next_unit(it, k);
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrWeightProducer);
     ok = true;
@@ -272,12 +312,18 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     // ---------------- activation producer ----------------
     pdl_wait_prerequisites();  // activations may be the previous kernel's output
     int issued = 0;
-    for (int v = 0; v < 2 * nunits; ++v) {
-      diag_unit = v >> 1;
+    int it, k, c = 0;
+    unit_at(0, it, k);
+    for (int v = 0; v < kXPerUnit * nunits; ++v) {
+      diag_unit = v / kXPerUnit;
       if (v >= kXStages && !warp_wait(BAR(bXEmpty + v % kXStages), ((v / kXStages) & 1) ^ 1)) break;
-      if (elect_one()) issue_x(v);
+      if (elect_one()) issue_x(v, it, k, c);
       __syncwarp();
       issued = v + 1;
+      if (++c == kXPerUnit) {
+        c = 0;
+        next_unit(it, k);
+      }
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrActProducer);
     ok = true;
@@ -290,37 +336,47 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     // ---------------- MMA issuer ----------------
     const uint64_t bdesc0 = make_sdesc_sw128(sbase + kXOff);
     int j = 0;   // piece
-    for (int u = 0; u < nunits; ++u) {
+    int it, k;
+    unit_at(0, it, k);
+    for (int u = 0; u < nunits; ++u, next_unit(it, k)) {
       diag_unit = u;
-      int it, k;
-      unit_at(u, it, k);
       const bool first = u == 0 || k == 0, last = u == nunits - 1 || k == S - 1;
       // the accumulators are free once the epilogue has read piece j - 1
       if (first && j >= 1) warp_wait(BAR(bAccEmpty), (uint32_t)((j - 1) & 1));
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
-        const int v = 2 * u + h;
-        warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1);
-        const uint64_t bx = bdesc0 + (uint64_t)(((v % kXStages) * kXStage) >> 4);
+        // the half's activation stages: pieces v0 .. v0 + 2 / kXChunks - 1; with
+        // one chunk a stage (BT = 256) the second is waited for only after the
+        // first chunk's MMAs are issued, and each stage is released right after
+        // its own MMAs
+        const int v0 = (2 * u + h) * (2 / kXChunks);
+        warp_wait(BAR(bXFull + v0 % kXStages), (v0 / kXStages) & 1);
 #pragma unroll 1
-        for (int t = 0; t < 2; ++t) {
-          const int sl = 2 * t + h;
-          named_bar_sync(prefill::kBarSlot0 + (uint32_t)sl, prefill::kSlotBarThreads);   // the tile's group published the half
+        for (int t = 0; t < kTiles; ++t) {
+          const int sl = BT == 128 ? 2 * t + h : 2 * (u & 1) + h;
+          named_bar_sync(prefill::kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // the slot's dequant warps published it
           tc_fence_after();
-          if (ok && elect_one()) {
-            const uint32_t d_acc = tmem + (uint32_t)(t * kAccCols);
-            const uint32_t a_t = tmem + (uint32_t)(kSlot0 + sl * kSlotCols);
+          const uint32_t d_acc = tmem + (uint32_t)(t * BT);
+          const uint32_t a_t = tmem + (uint32_t)(kSlot0 + sl * kSlotCols);
 #pragma unroll
-            for (int cl = 0; cl < 2; ++cl)
+          for (int cl = 0; cl < 2; ++cl) {
+            // chunk 2h + cl: stage of piece v0 + cl (one chunk a stage) or chunk cl of stage v0
+            const int v = kXChunks == 1 ? v0 + cl : v0;
+            if (kXChunks == 1 && cl == 1) warp_wait(BAR(bXFull + v % kXStages), (v / kXStages) & 1);
+            if (ok && elect_one()) {
+              const uint64_t bx =
+                  bdesc0 + (uint64_t)(((v % kXStages) * kXStageBytes + (kXChunks == 1 ? 0 : cl * kXChunkBytes)) >> 4);
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
-                mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks, bx + (uint64_t)(((cl * kXChunk) + 32 * ks) >> 4), kIdesc,
+                mma_f16_ts(d_acc, a_t + cl * 32 + 8 * ks, bx + (uint64_t)((32 * ks) >> 4), kIdesc,
                            (first && h == 0 && cl == 0 && ks == 0) ? 0u : 1u);
-            tc_commit(BAR(bSDone + sl));  // half slot free once these MMAs complete
+              if (kXChunks == 1) tc_commit(BAR(bXEmpty + v % kXStages));   // chunk stage free
+              if (cl == 1) tc_commit(BAR(bSDone + sl));   // half slot free once these MMAs complete
+            }
+            __syncwarp();
           }
-          __syncwarp();
         }
-        if (ok && elect_one()) tc_commit(BAR(bXEmpty + v % kXStages));  // activation stage free
+        if (kXChunks == 2 && ok && elect_one()) tc_commit(BAR(bXEmpty + v0 % kXStages));  // both tiles read the stage
         __syncwarp();
       }
       if (ok && elect_one() && last) tc_commit(BAR(bAccFull));  // piece's accumulators complete
@@ -330,12 +386,13 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     if (!ok && lane == 0) atomicOr(p.error, kErrMma);
     if (elect_one()) tc_commit(BAR(bFinal));
     __syncwarp();
-  } else if (warp >= 4 && warp < 12) {
-    // ---------------- dequant (tile t = group) ----------------
+  } else if (warp >= kDequantWarp0 && warp < kEpilogueWarp0) {
+    // ---------------- dequant (group g of every unit) ----------------
     const int q = warp & 3;
-    const int t = (warp - 4) >> 2;
+    const int g = (warp - kDequantWarp0) >> 2;
+    const int t = BT == 128 ? g : 0;
     const int r = q * 32 + lane;
-    const int row = t * kTileRows + r;       // row within the 256-row weight stage
+    const int row = t * kTileRows + r;       // row within the weight stage
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     for (int u = 0; u < nunits; ++u) {
       diag_unit = u;
@@ -343,10 +400,12 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
       warp_wait(BAR(bWFull + ws), (u / kWStages) & 1);
       const uint8_t* stage = smem + kWOff + ws * kWStage;
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int sl = 2 * t + h;
-        // half slot sl is free once the MMAs of the previous unit read it
-        if (u >= 1) warp_wait(BAR(bSDone + sl), (uint32_t)((u - 1) & 1));
+      for (int hh = 0; hh < kTiles; ++hh) {   // BT = 128: both halves of tile g; BT = 256: half g
+        const int h = BT == 128 ? hh : g;
+        const int sl = BT == 128 ? 2 * t + h : 2 * (u & 1) + h;
+        // half slot sl is free once the MMAs of its previous use read it
+        const int use = BT == 128 ? u : u >> 1;
+        if (use >= 1) warp_wait(BAR(bSDone + sl), (uint32_t)((use - 1) & 1));
         tc_fence_after();
         if (ok) {
           const uint32_t a_col = tmem + lane_off + (uint32_t)(kSlot0 + sl * kSlotCols);
@@ -358,13 +417,12 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         }
         tc_fence_before();
         __syncwarp();
-        named_bar_arrive(prefill::kBarSlot0 + (uint32_t)sl, prefill::kSlotBarThreads);   // always: the MMA warp syncs on every half
+        named_bar_arrive(prefill::kBarSlot0 + (uint32_t)sl, kSlotBarThreads);   // always: the MMA warp syncs on every half
       }
-      __syncwarp();
       if (lane == 0) mbar_arrive(BAR(bWEmpty + ws));
     }
     if (!ok && lane == 0) atomicOr(p.error, kErrDequant);
-  } else if (warp >= 12) {
+  } else if (warp >= kEpilogueWarp0) {
     // ---------------- epilogue ----------------
     const int q = warp & 3;
     const int r = q * 32 + lane;
@@ -380,26 +438,26 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
       const bool whole = !sk || ((long long)it * S >= g0 && (long long)(it + 1) * S <= g0 + nunits);
       float* part = whole ? nullptr : p.part + (size_t)(2 * bid + (j == 0 ? 0 : 1)) * kPartElems;
       // batch rows of the item that exist: only those are read from TMEM and written
-      const int mv = min(kBatchTile, p.M - bt * kBatchTile);
+      const int mv = min(BT, p.M - bt * BT);
       const bool have = warp_wait(BAR(bAccFull), (uint32_t)(j & 1));
       tc_fence_after();
       if (!waited_pdl) {
         pdl_wait_prerequisites();  // C may still be read by the previous kernel
         waited_pdl = true;
       }
-      if (p.swiglu) {
+      if (BT == 128 && p.swiglu) {
         // accumulator 0 holds the gate tile, 1 the up tile of the same rows
         const int n = pair * kTileRows + r;
 #pragma unroll 1
         for (int cb = 0; cb < mv; cb += 16) {
           uint32_t xg[16], xu[16];
           tmem_ld_x16(tmem + lane_off + (uint32_t)cb, xg);
-          tmem_ld_x16(tmem + lane_off + (uint32_t)(kAccCols + cb), xu);
+          tmem_ld_x16(tmem + lane_off + (uint32_t)(BT + cb), xu);
           tc_wait_ld();
           if (have && n < p.N) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const int b = bt * kBatchTile + cb + i;
+              const int b = bt * BT + cb + i;
               if (b < p.M)
                 C[(size_t)b * p.N + n] = to_out<OutT>(silu(__uint_as_float(xg[i])) * __uint_as_float(xu[i]));
             }
@@ -407,23 +465,23 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int t = 0; t < 2; ++t) {
-          const int n = pair * kPairRows + t * kTileRows + r;
+        for (int t = 0; t < kTiles; ++t) {
+          const int n = pair * kItemRows + t * kTileRows + r;
 #pragma unroll 1
           for (int cb = 0; cb < mv; cb += 32) {
             uint32_t x[32];
-            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb), x);
-            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * kAccCols + cb + 16), x + 16);
+            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * BT + cb), x);
+            tmem_ld_x16(tmem + lane_off + (uint32_t)(t * BT + cb + 16), x + 16);
             tc_wait_ld();
             if (have && part) {
-              // [batch row][weight row] of the pair, the item's existing batch rows
+              // [batch row][weight row] of the item, the item's existing batch rows
 #pragma unroll
               for (int i = 0; i < 32; ++i)
-                if (cb + i < mv) part[(cb + i) * kPairRows + t * kTileRows + r] = __uint_as_float(x[i]);
+                if (cb + i < mv) part[(cb + i) * kItemRows + t * kTileRows + r] = __uint_as_float(x[i]);
             } else if (have && n < p.N) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                const int b = bt * kBatchTile + cb + i;
+                const int b = bt * BT + cb + i;
                 if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(__uint_as_float(x[i]));
               }
             }
@@ -463,15 +521,19 @@ struct SplitItems {
 }  // namespace prefill
 
 // Stream-K fix-up: each split item is summed from its CTAs' partial tiles, in
-// CTA order, and written to C. Block (x, y): split item x, batch rows 4 y ..
-// 4 y + 3 of the item, 64 threads per row, each owning 4 consecutive weight
-// rows of the pair (one 16-byte load per partial tile). The loads of up to
-// eight partial tiles are issued together and added in CTA order.
-template <typename OutT>
+// CTA order, and written to C. Block (x, y): split item x, batch rows
+// kRowsPerBlock y .. of the item, item rows / 4 threads per batch row, each
+// owning 4 consecutive weight rows of the item (one 16-byte load per partial
+// tile). The loads of up to eight partial tiles are issued together and added
+// in CTA order.
+template <typename OutT, int BT>
 __global__ void __launch_bounds__(256) prefill_reduce_kernel(const float* __restrict__ part, OutT* __restrict__ c,
                                                            int M, int N, int btiles,
                                                            const __grid_constant__ prefill::SplitItems si) {
   using namespace prefill;
+  constexpr int kItemRows = Geo<BT>::kItemRows;
+  constexpr int kRowThreads = kItemRows / 4;
+  constexpr int kRowsPerBlock = 256 / kRowThreads;
   pdl_wait_prerequisites();   // the partial tiles are the previous kernel's output
   // the next kernel may start its set-up and weight loads; it reads C, and
   // writes partial tiles, only after its own wait for this grid to finish
@@ -479,10 +541,10 @@ __global__ void __launch_bounds__(256) prefill_reduce_kernel(const float* __rest
   const int4 e = si.e[blockIdx.x];
   const int it = e.x, c_lo = e.y, c_hi = e.z, slot_lo = e.w;
   const int pair = it / btiles, bt = it - (it / btiles) * btiles;
-  const int row = 4 * (int)blockIdx.y + ((int)threadIdx.x >> 6);          // batch row within the item
-  const int col = 4 * ((int)threadIdx.x & 63);                            // weight row within the pair
-  if (bt * kBatchTile + row >= M) return;
-  const size_t off = (size_t)row * kPairRows + col;
+  const int row = kRowsPerBlock * (int)blockIdx.y + (int)threadIdx.x / kRowThreads;   // batch row within the item
+  const int col = 4 * ((int)threadIdx.x % kRowThreads);                             // weight row within the item
+  if (bt * BT + row >= M) return;
+  const size_t off = (size_t)row * kItemRows + col;
   auto slot_ptr = [&](int cc) {
     const int slot = cc == c_lo ? slot_lo : 2 * cc;
     return reinterpret_cast<const float4*>(part + (size_t)slot * kPartElems + off);
@@ -502,8 +564,8 @@ __global__ void __launch_bounds__(256) prefill_reduce_kernel(const float* __rest
         acc.w += v[i].w;
       }
   }
-  const int b = bt * kBatchTile + row;
-  const int n = pair * kPairRows + col;
+  const int b = bt * BT + row;
+  const int n = pair * kItemRows + col;
   OutT* dst = c + (size_t)b * N + n;
   if (n < N) dst[0] = to_out<OutT>(acc.x);
   if (n + 1 < N) dst[1] = to_out<OutT>(acc.y);

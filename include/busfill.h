@@ -371,11 +371,17 @@ BUSFILL_API int busfill_version(void);
  *   BUSFILL_OPT_EXACT_KQUANT: accepted (0 or 1) and ignored: every K-quant
  *     GEMM builds the exact operand fp16_rn(fp32 w). Kept so that callers
  *     which set it keep working.
+ *   BUSFILL_OPT_PREFILL_BATCH_TILE: batch rows per work item of the prefill
+ *     kernel: 0 (default) chooses 256 (one 128-row weight tile, MMA N = 256)
+ *     for M >= 256 and 128 (two weight tiles) below; 128 or 256 forces it
+ *     (SwiGLU pairs always take 128). A tuning and test knob; results agree
+ *     within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
 #define BUSFILL_OPT_PREFILL_MIN_M 3
 #define BUSFILL_OPT_EXACT_KQUANT 4
+#define BUSFILL_OPT_PREFILL_BATCH_TILE 5
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,

@@ -4,7 +4,8 @@ Large batches (by default M > 64 for the plain GEMMs, whose prefill kernel
 spreads the work over all SMs stream-K style; M >= 128 with at least 64 work
 items of 256 weight rows x 128 batch rows where whole items are dealt out)
 run one pass over the weights for all rows; the decode kernel covers the rest. These tests force the prefill kernel
-(BUSFILL_OPT_PREFILL_MIN_M) onto small, ragged and multi-item shapes, and run
+(BUSFILL_OPT_PREFILL_MIN_M) onto small, ragged and multi-item shapes, with
+both work-item shapes (BUSFILL_OPT_PREFILL_BATCH_TILE 128 and 256), and run
 the BASELINE config-4 shapes at full size through the default dispatch,
 checked on sampled rows and columns against the oracle.
 Gates as in test_gpu_parity: max abs err <= 0.6 and rel-L2 <= 1e-3 against
@@ -38,13 +39,17 @@ def check(c_dev, a, w_ref, w_exact):
     assert rel_t <= TIGHT_REL_L2, rel_t
 
 
-@pytest.fixture
-def prefill_always():
+@pytest.fixture(params=[128, 256], ids=["bt128", "bt256"])
+def prefill_always(request):
+    """The prefill kernel for every M, with work items of 128 batch rows (two
+    weight tiles) or 256 (one weight tile, MMA N = 256)."""
     bf.set_prefill_min_m(1)
+    bf.set_prefill_batch_tile(request.param)
     try:
-        yield
+        yield request.param
     finally:
         bf.set_prefill_min_m(0)
+        bf.set_prefill_batch_tile(0)
 
 
 PREFILL_SHAPES = [
