@@ -170,6 +170,12 @@ def set_prefill_batch_tile(bt: int) -> None:
     _check(_lib().busfill_set_option(5, int(bt)), "busfill_set_option")
 
 
+def set_prefill_pair(mode: int) -> None:
+    """Prefill GEMMs on CTA pairs (256 x 256 items over a 2-CTA cluster):
+    0 = from M = 256 (default), 1 = always (not the SwiGLU pairs), 2 = never."""
+    _check(_lib().busfill_set_option(6, int(mode)), "busfill_set_option")
+
+
 # ---------------------------------------------------------------------------
 # torch-tensor wrappers
 # ---------------------------------------------------------------------------

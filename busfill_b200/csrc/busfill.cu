@@ -17,6 +17,7 @@
 #include "busfill.h"
 #include "decode_gemm.cuh"
 #include "prefill_gemm.cuh"
+#include "prefill_pair_gemm.cuh"
 #include "dequant.cuh"
 
 using namespace busfill;
@@ -68,8 +69,23 @@ int prefill_bt(int M, bool swiglu) {
   return M >= kWideMinM ? 256 : 128;
 }
 
+// CTA pairs (prefill_pair_gemm.cuh: items of 256 weight rows x 256 batch
+// rows on the two CTAs of a cluster, each loading half of the batch rows):
+// by default from kWideMinM rows; BUSFILL_OPT_PREFILL_PAIR 1 forces them for
+// every prefill GEMM but the SwiGLU pairs, 2 turns them off.
+std::atomic<int> g_prefill_pair{0};
+
+bool prefill_pairs(int M, bool swiglu) {
+  if (swiglu) return false;
+  const int mode = g_prefill_pair.load();
+  if (mode == 1) return true;
+  if (mode == 2) return false;
+  return M >= kWideMinM;
+}
+
 // work items of a prefill launch: weight-row groups x batch tiles
 long long prefill_items(int M, int N, bool swiglu) {
+  if (prefill_pairs(M, swiglu)) return (long long)((N + 255) / 256) * ((M + 255) / 256);
   const int bt = prefill_bt(M, swiglu);
   const int item_rows = swiglu ? kTileRows : bt == 128 ? 2 * kTileRows : kTileRows;  // SwiGLU: gate tile j + up tile j
   return (long long)((N + item_rows - 1) / item_rows) * ((M + bt - 1) / bt);
@@ -583,10 +599,113 @@ int run_prefill_bt(const DeviceInfo& di, int dev, const uint8_t* w, const uint16
   return BUSFILL_OK;
 }
 
+// CTA pairs this device runs at once for the pair kernel (one CTA per SM);
+// the launch never asks for more, so that no pair waits for a second wave
+template <WFmt FMT, typename OutT>
+int pair_capacity(int dev, int sm_count) {
+  static std::once_flag once[64];
+  static int cap[64];
+  std::call_once(once[dev & 63], [&] {
+    const void* kern = reinterpret_cast<const void*>(prefill_pair_kernel<FMT, OutT>);
+    int n = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             prefill_pair::Smem<FMT>::kAlloc) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * (sm_count / 2));
+      cfg.blockDim = dim3(prefill_pair::kThreads);
+      cfg.dynamicSmemBytes = prefill_pair::Smem<FMT>::kAlloc;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();
+    cap[dev & 63] = std::min(n, sm_count / 2);
+  });
+  return cap[dev & 63];
+}
+
+// The pair kernel: items of 256 weight rows x 256 batch rows, stream-K over
+// the pairs when `part` is given, else whole items round-robin.
+template <WFmt FMT, typename OutT>
+int run_prefill_pair(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
+                     int M, int N, int K, unsigned* error, cudaStream_t s, float* part) {
+  const int S = K / kUnitK;
+  CUtensorMap tw, tws, ta;
+  std::memset(&tws, 0, sizeof(tws));
+  if constexpr (aos_rows<FMT>()) {
+    constexpr int ub = unit_row_bytes<FMT>();
+    const uint64_t row = (uint64_t)S * ub;
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, row, (uint64_t)N, row, ub, kTileRows,
+                      CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    tws = tw;
+    if (FMT == WFmt::Q6K && !make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)N, (uint64_t)S,
+                                          (uint64_t)N * 2, kTileRows, 1, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+  } else {
+    if (!make_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, (uint64_t)K / 2, (uint64_t)N, (uint64_t)K / 2, 128,
+                      kTileRows, CU_TENSOR_MAP_SWIZZLE_128B))
+      return BUSFILL_ERR_CUDA;
+    if (!make_tmap_2d(&tws, CU_TENSOR_MAP_DATA_TYPE_UINT16, ws, (uint64_t)K / 32, (uint64_t)N, (uint64_t)K / 16, 8,
+                      kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+  }
+  if (!make_tmap_act3d(&ta, a, (uint64_t)M, (uint64_t)K, 128, 2)) return BUSFILL_ERR_CUDA;
+  const int cap = pair_capacity<FMT, OutT>(dev, di.sm_count);
+  if (cap < 1) return BUSFILL_ERR_LAUNCH;
+
+  prefill::Params p;
+  p.c = c;
+  p.error = error;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.pairs = (N + prefill_pair::kItemRows - 1) / prefill_pair::kItemRows;
+  p.btiles = (M + prefill_pair::kBatchTile - 1) / prefill_pair::kBatchTile;
+  p.units = S;
+  p.swiglu = 0;
+  p.part = part;
+  const long long items = (long long)p.pairs * p.btiles;
+  const long long units = items * S;
+  if (units > INT32_MAX) return BUSFILL_ERR_SHAPE;   // the kernel counts units in an int
+  const int pairs = part ? (int)std::min<long long>(std::min<long long>(units, cap), prefill::kMaxSplitItems + 1)
+                         : (int)std::min<long long>(items, cap);
+  const void* kern = reinterpret_cast<const void*>(prefill_pair_kernel<FMT, OutT>);
+  void* args[] = {&tw, &tws, &ta, &p};
+  if (launch(kern, dim3(2 * pairs), dim3(prefill_pair::kThreads), prefill_pair::Smem<FMT>::kAlloc, s, args,
+             g_use_pdl.load() != 0, 2) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_LAUNCH;
+  }
+  prefill::SplitItems si;
+  if (part) split_items(units, S, pairs, &si);
+  if (part && si.n > 0) {
+    // items split between pairs: their partial tiles summed in pair order
+    const float* cpart = part;
+    OutT* cc = reinterpret_cast<OutT*>(c);
+    int m = M, n = N, bts = p.btiles;
+    void* rargs[] = {&cpart, &cc, &m, &n, &bts, &si};
+    const int rows = std::min(M, prefill_pair::kBatchTile);
+    if (launch(reinterpret_cast<const void*>(prefill_pair_reduce_kernel<OutT>), dim3(si.n, (rows + 3) / 4),
+               dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
+      cudaGetLastError();
+      return BUSFILL_ERR_LAUNCH;
+    }
+  }
+  return BUSFILL_OK;
+}
+
 template <WFmt FMT, typename OutT>
 int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
                 int M, int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr,
                 float* part = nullptr) {
+  if (prefill_pairs(M, w_up != nullptr))
+    return run_prefill_pair<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, part);
   if (prefill_bt(M, w_up != nullptr) == 256)
     return run_prefill_bt<FMT, OutT, 256>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
   return run_prefill_bt<FMT, OutT, 128>(di, dev, w, ws, a, c, M, N, K, error, s, w_up, part);
@@ -798,7 +917,9 @@ int busfill_gemm_launches(int M, int N, int K, int sm_count) {
   // the stream-K prefill launch, and the fix-up launch if it splits an item
   const int S = K / kUnitK;
   const long long units = prefill_items(M, N, false) * S;
-  const int grid = (int)std::min<long long>(std::min<long long>(units, sm_count), prefill::kMaxSplitItems + 1);
+  // CTAs (or CTA pairs) that split the units: one per SM (pair of SMs)
+  const int ctas = prefill_pairs(M, false) ? sm_count / 2 : sm_count;
+  const int grid = (int)std::min<long long>(std::min<long long>(units, ctas), prefill::kMaxSplitItems + 1);
   prefill::SplitItems si;
   split_items(units, S, grid, &si);
   return si.n > 0 ? 2 : 1;
@@ -841,6 +962,11 @@ int busfill_set_option(int option, int value) {
   if (option == BUSFILL_OPT_PREFILL_BATCH_TILE) {
     if (value != 0 && value != 128 && value != 256) return BUSFILL_ERR_INVALID_ARG;
     g_prefill_bt.store(value);
+    return BUSFILL_OK;
+  }
+  if (option == BUSFILL_OPT_PREFILL_PAIR) {
+    if (value < 0 || value > 2) return BUSFILL_ERR_INVALID_ARG;
+    g_prefill_pair.store(value);
     return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;

@@ -162,6 +162,13 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// arrive on an mbarrier of another CTA of the cluster without release
+// semantics: for a signal whose payload was completed by a wait of its own
+// (tcgen05.wait::st before a TMEM operand is handed over). A release arrival
+// at cluster scope costs the arriving warp ~1000-1600 cycles on B200.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // wait that acquires at cluster scope (pairs with mbar_arrive_remote)
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
@@ -340,8 +347,54 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       : "memory");
 }
 
+// --- CTA pairs (cta_group::2): one MMA over both SMs of a 2-CTA cluster ---
+// TMEM allocation of the same columns in both CTAs: a collective of one warp
+// with the same warp index in each CTA of the pair, same destination offset.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D (+)= A * B^T over the pair, issued by the pair's rank-0 CTA: A [256 x 16]
+// from TMEM (rows 0-127 in rank 0's lanes, 128-255 in rank 1's), B [N x 16]
+// from shared memory at the same offset in both CTAs (rank 0 holds rows
+// 0..N/2-1, rank 1 the rest), D [256 x N] fp32 split like A.
+__device__ __forceinline__ void mma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the mbarrier at offset `bar` in each CTA of `cta_mask` once every
+// tcgen05 operation this thread issued has completed (pair MMAs).
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
+}
+// 3-D tensor copy into this CTA's shared memory whose completion is counted
+// on an mbarrier of either CTA of the pair (`bar_cluster`, a shared::cluster
+// address): both CTAs' halves of an operand complete on rank 0's barrier.
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* desc, int32_t x, int32_t y, int32_t z,
+                                                 uint32_t bar_cluster, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // Instruction descriptor for kind::f16: fp16 A/B, fp32 D, both K-major,
-// M = 128, N = n (multiple of 16, 16..256).
+// M = m (128; 256 for a CTA pair), N = n (multiple of 16, 16..256).
 __host__ __device__ constexpr uint32_t make_idesc_f16_f32(int m, int n) {
   return (1u << 4)                                 // D format: f32
          | (0u << 7) | (0u << 10)                  // A, B format: f16

@@ -376,12 +376,18 @@ BUSFILL_API int busfill_version(void);
  *     for M >= 256 and 128 (two weight tiles) below; 128 or 256 forces it
  *     (SwiGLU pairs always take 128). A tuning and test knob; results agree
  *     within the accuracy gate.
+ *   BUSFILL_OPT_PREFILL_PAIR: 0 (default) runs prefill GEMMs of M >= 256 on
+ *     CTA pairs (items of 256 weight rows x 256 batch rows, one MMA over the
+ *     two SMs of a 2-CTA cluster, each loading half of the batch rows); 1
+ *     runs every prefill GEMM but the SwiGLU pairs on CTA pairs; 2 never.
+ *     A tuning and test knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
 #define BUSFILL_OPT_PREFILL_MIN_M 3
 #define BUSFILL_OPT_EXACT_KQUANT 4
 #define BUSFILL_OPT_PREFILL_BATCH_TILE 5
+#define BUSFILL_OPT_PREFILL_PAIR 6
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,

@@ -422,6 +422,15 @@ def test_prefill_batch_tile_option_values():
     assert lib.busfill_set_option(5, 0) == 0
 
 
+def test_prefill_pair_option_values():
+    lib = bf.load_library()
+    for v in (0, 1, 2):
+        assert lib.busfill_set_option(6, v) == 0
+    for v in (-1, 3):
+        assert lib.busfill_set_option(6, v) == -1
+    assert lib.busfill_set_option(6, 0) == 0
+
+
 def test_kernel_choice_by_shape():
     """Default dispatch of the plain GEMMs: the stream-K prefill kernel for
     M > 64, and for M > 32 when N <= K and K >= 12288; the decode kernel

@@ -48,10 +48,12 @@ def canon(w16):
 
 def operand_via_onehot(gemm, n, k, prefill):
     """[n, k] fp16 operand: 32 one-hot activation rows per call; prefill: 0 =
-    the decode kernel, else the prefill kernel with that batch tile."""
+    the decode kernel, else the prefill kernel with that batch tile on one
+    CTA, or "pair": on CTA pairs."""
     out = np.empty((n, k), dtype=np.float16)
     bf.set_prefill_min_m(1 if prefill else 10 ** 6)
-    bf.set_prefill_batch_tile(prefill or 0)
+    bf.set_prefill_pair(1 if prefill == "pair" else 2)
+    bf.set_prefill_batch_tile(prefill if prefill in (128, 256) else 0)
     try:
         for g in range(0, k, 32):
             m = min(32, k - g)
@@ -63,6 +65,7 @@ def operand_via_onehot(gemm, n, k, prefill):
     finally:
         bf.set_prefill_min_m(0)
         bf.set_prefill_batch_tile(0)
+        bf.set_prefill_pair(0)
     return out
 
 
@@ -71,7 +74,7 @@ def assert_bits_equal(got, want):
     assert not diff.any(), f"{int(diff.sum())} of {diff.size} operand values differ from the oracle"
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 def test_q4_0_operand_is_reference_dequant(prefill):
     wq, ws = orc.gen_q4_0(N, K, seed=31)
     got = operand_via_onehot(lambda a: bf.gemm_q4_0(cu(wq), cu(ws), a), N, K, prefill)
@@ -100,7 +103,7 @@ def gather_one_rank(blocks, n, k):
     return gemm
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 @pytest.mark.parametrize("entry", ["gemm", "noalloc", "gather"])
 def test_q4k_operand_is_the_oracle(prefill, entry):
     if entry == "gather" and prefill:
@@ -129,7 +132,7 @@ def constant_q4k(n, k, value_q=8, sc=8):
     return orc.make_q4k_blocks(d16, dmin16, scs, ms, q)
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 def test_swiglu_up_operand_is_the_oracle(prefill):
     """Gate weights all 64.0: silu(64) is 64 exactly in fp32 (exp(-64) is
     below half an ulp of 1), so with one-hot rows h = fp16(64 * W_up'[n, k])
@@ -162,14 +165,14 @@ def test_swiglu_gate_operand_through_silu():
                   np.spacing(np.abs(want)).astype(np.float64) + 1e-12)
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 def test_q5k_operand_is_the_oracle(prefill):
     blocks = orc.gen_q5k(N, K, seed=33)
     got = operand_via_onehot(lambda a: bf.gemm_q5k(cu(blocks), a), N, K, prefill)
     assert_bits_equal(got, orc.dequant_q5k(blocks, K))
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 def test_q6k_operand_is_the_oracle(prefill):
     blocks = orc.gen_q6k(N, K, seed=34)
     body, dplane = bf.repack_q6k(cu(blocks), K)
@@ -177,7 +180,7 @@ def test_q6k_operand_is_the_oracle(prefill):
     assert_bits_equal(got, orc.dequant_q6k(blocks, K))
 
 
-@pytest.mark.parametrize("prefill", [0, 128, 256], ids=["decode", "prefill128", "prefill256"])
+@pytest.mark.parametrize("prefill", [0, 128, 256, "pair"], ids=["decode", "prefill128", "prefill256", "pair"])
 @pytest.mark.parametrize("name", ["q4k_gguf.npz", "q5k_gguf.npz", "q6k_gguf.npz"])
 def test_operand_on_golden_blocks(golden_dir, name, prefill):
     """Every byte random (all 6-bit scale / min patterns, fp16 exponents over

@@ -5,7 +5,8 @@ spreads the work over all SMs stream-K style; M >= 128 with at least 64 work
 items of 256 weight rows x 128 batch rows where whole items are dealt out)
 run one pass over the weights for all rows; the decode kernel covers the rest. These tests force the prefill kernel
 (BUSFILL_OPT_PREFILL_MIN_M) onto small, ragged and multi-item shapes, with
-both work-item shapes (BUSFILL_OPT_PREFILL_BATCH_TILE 128 and 256), and run
+every work-item shape (BUSFILL_OPT_PREFILL_BATCH_TILE 128 and 256 on one
+CTA, BUSFILL_OPT_PREFILL_PAIR on CTA pairs), and run
 the BASELINE config-4 shapes at full size through the default dispatch,
 checked on sampled rows and columns against the oracle.
 Gates as in test_gpu_parity: max abs err <= 0.6 and rel-L2 <= 1e-3 against
@@ -39,17 +40,23 @@ def check(c_dev, a, w_ref, w_exact):
     assert rel_t <= TIGHT_REL_L2, rel_t
 
 
-@pytest.fixture(params=[128, 256], ids=["bt128", "bt256"])
+@pytest.fixture(params=[128, 256, "pair"], ids=["bt128", "bt256", "pair"])
 def prefill_always(request):
-    """The prefill kernel for every M, with work items of 128 batch rows (two
-    weight tiles) or 256 (one weight tile, MMA N = 256)."""
+    """The prefill kernel for every M: one CTA per work item of 128 batch rows
+    (two weight tiles) or 256 (one weight tile, MMA N = 256), or CTA pairs
+    (256 x 256 items, one cta_group::2 MMA over two SMs)."""
     bf.set_prefill_min_m(1)
-    bf.set_prefill_batch_tile(request.param)
+    if request.param == "pair":
+        bf.set_prefill_pair(1)
+    else:
+        bf.set_prefill_pair(2)
+        bf.set_prefill_batch_tile(request.param)
     try:
         yield request.param
     finally:
         bf.set_prefill_min_m(0)
         bf.set_prefill_batch_tile(0)
+        bf.set_prefill_pair(0)
 
 
 PREFILL_SHAPES = [

@@ -69,11 +69,15 @@ def test_gemm_q5k_decode(m, n, k):
     check(c, a, orc.dequant_q5k_f32(blocks, k))
 
 
-@pytest.mark.parametrize("bt", [128, 256])
+@pytest.mark.parametrize("bt", [128, 256, "pair"])
 @pytest.mark.parametrize("m,n,k", [(128, 512, 512), (300, 640, 2048), (64, 256, 1024)])
 def test_gemm_q5k_prefill(m, n, k, bt):
     bf.set_prefill_min_m(1)
-    bf.set_prefill_batch_tile(bt)
+    if bt == "pair":
+        bf.set_prefill_pair(1)
+    else:
+        bf.set_prefill_pair(2)
+        bf.set_prefill_batch_tile(bt)
     try:
         blocks = orc.gen_q5k(n, k, seed=m + 2 * n + k)
         a = orc.gen_activations(m, k, seed=m + k)
@@ -82,6 +86,7 @@ def test_gemm_q5k_prefill(m, n, k, bt):
     finally:
         bf.set_prefill_min_m(0)
         bf.set_prefill_batch_tile(0)
+        bf.set_prefill_pair(0)
     check(c, a, orc.dequant_q5k_f32(blocks, k))
 
 
