@@ -428,6 +428,8 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
     const int r = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     OutT* C = reinterpret_cast<OutT*>(p.c);
+    // fp16 C with rows of a multiple of 8 values on a 16-byte boundary: vector stores
+    const bool vec16 = sizeof(OutT) == 2 && (p.N & 7) == 0 && (reinterpret_cast<uintptr_t>(p.c) & 15) == 0;
     bool waited_pdl = false;
     for (int j = 0; j < npieces; ++j) {
       diag_unit = j;
@@ -478,6 +480,26 @@ __global__ void __launch_bounds__(prefill::kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i)
                 if (cb + i < mv) part[(cb + i) * kItemRows + t * kTileRows + r] = __uint_as_float(x[i]);
+            } else if (have && vec16) {
+              // lane j of each group of 8 then holds batch row 8b + j of the
+              // group's 8 consecutive weight rows: one 16-byte store per block
+              // (2-byte stores strided by N made the drain of an item ~2.4x
+              // longer, and the next item's MMAs wait for it)
+              float* v = reinterpret_cast<float*>(x);
+              transpose_8x8_blocks<32>(v, lane);
+              const int n0 = n - (lane & 7);
+#pragma unroll
+              for (int b = 0; b < 4; ++b) {
+                const int row = bt * BT + cb + 8 * b + (lane & 7);
+                if (row < p.M && n0 < p.N) {   // N % 8 == 0: the group's 8 rows are all in range
+                  uint4 w;
+                  w.x = h2_as_u32(__floats2half2_rn(v[8 * b], v[8 * b + 1]));
+                  w.y = h2_as_u32(__floats2half2_rn(v[8 * b + 2], v[8 * b + 3]));
+                  w.z = h2_as_u32(__floats2half2_rn(v[8 * b + 4], v[8 * b + 5]));
+                  w.w = h2_as_u32(__floats2half2_rn(v[8 * b + 6], v[8 * b + 7]));
+                  *reinterpret_cast<uint4*>(C + (size_t)row * p.N + n0) = w;
+                }
+              }
             } else if (have && n < p.N) {
 #pragma unroll
               for (int i = 0; i < 32; ++i) {

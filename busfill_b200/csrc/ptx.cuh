@@ -312,6 +312,33 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* desc, int3
       : "memory");
 }
 
+// Transposes, in each group of 8 lanes, the 8x8 blocks of the NB values the
+// lanes hold: before, lane j of a group holds batch rows 0..NB-1 of weight
+// row n0 + j; after, acc[8b + i] of lane j holds batch row 8b + j of weight
+// row n0 + i. Three butterfly stages (lane distance 4, 2, 1); in each, the
+// lanes of a pair swap the halves the other needs. All 32 lanes take part.
+template <int NB>
+__device__ __forceinline__ void transpose_8x8_blocks(float* acc, int lane) {
+  const int j = lane & 7;
+#pragma unroll
+  for (int b = 0; b < NB / 8; ++b) {
+    float* v = acc + 8 * b;
+#pragma unroll
+    for (int m = 4; m >= 1; m >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (i & m) continue;
+        const bool hi = (j & m) != 0;
+        const float y = __shfl_xor_sync(0xffffffffu, hi ? v[i] : v[i | m], m);
+        if (hi)
+          v[i] = y;
+        else
+          v[i | m] = y;
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------------------
 // tcgen05
 // ----------------------------------------------------------------------------

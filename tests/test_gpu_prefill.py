@@ -61,6 +61,7 @@ def prefill_always(request):
 
 PREFILL_SHAPES = [
     (128, 512, 512), (130, 384, 768), (256, 1280, 1024), (300, 640, 2048), (257, 200, 256), (512, 2304, 1536),
+    (260, 100, 512),   # N % 8 != 0: the epilogue's scalar stores
 ]
 
 
