@@ -571,6 +571,7 @@ int run_prefill_bt(const DeviceInfo& di, int dev, const uint8_t* w, const uint16
   const long long units = items * S;
   if (units > INT32_MAX) return BUSFILL_ERR_SHAPE;   // the kernel counts units in an int
   p.part = swiglu ? nullptr : part;
+  p.gate_mul = 0;
   const int grid = p.part ? (int)std::min<long long>(std::min<long long>(units, di.sm_count), prefill::kMaxSplitItems + 1)
                            : (int)std::min<long long>(items, di.sm_count);
   void* args[] = {&tw, &tws, &ta, &p};
@@ -630,10 +631,12 @@ int pair_capacity(int dev, int sm_count) {
 }
 
 // The pair kernel: items of 256 weight rows x 256 batch rows, stream-K over
-// the pairs when `part` is given, else whole items round-robin.
+// the pairs when `part` is given, else whole items round-robin. gate_mul: C
+// holds the up projection and receives silu(A W^T) * C (the SwiGLU pair's
+// second pass).
 template <WFmt FMT, typename OutT>
 int run_prefill_pair(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c,
-                     int M, int N, int K, unsigned* error, cudaStream_t s, float* part) {
+                     int M, int N, int K, unsigned* error, cudaStream_t s, float* part, int gate_mul = 0) {
   const int S = K / kUnitK;
   CUtensorMap tw, tws, ta;
   std::memset(&tws, 0, sizeof(tws));
@@ -670,6 +673,7 @@ int run_prefill_pair(const DeviceInfo& di, int dev, const uint8_t* w, const uint
   p.units = S;
   p.swiglu = 0;
   p.part = part;
+  p.gate_mul = gate_mul;
   const long long items = (long long)p.pairs * p.btiles;
   const long long units = items * S;
   if (units > INT32_MAX) return BUSFILL_ERR_SHAPE;   // the kernel counts units in an int
@@ -688,8 +692,8 @@ int run_prefill_pair(const DeviceInfo& di, int dev, const uint8_t* w, const uint
     // items split between pairs: their partial tiles summed in pair order
     const float* cpart = part;
     OutT* cc = reinterpret_cast<OutT*>(c);
-    int m = M, n = N, bts = p.btiles;
-    void* rargs[] = {&cpart, &cc, &m, &n, &bts, &si};
+    int m = M, n = N, bts = p.btiles, gm = gate_mul;
+    void* rargs[] = {&cpart, &cc, &m, &n, &bts, &gm, &si};
     const int rows = std::min(M, prefill_pair::kBatchTile);
     if (launch(reinterpret_cast<const void*>(prefill_pair_reduce_kernel<OutT>), dim3(si.n, (rows + 3) / 4),
                dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
@@ -715,6 +719,18 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
 template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
              int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr, bool may_alloc = true) {
+  // SwiGLU pairs of many rows: two CTA-pair GEMMs, the up projection into C,
+  // then the gate with an epilogue that writes silu(gate) * C (the up values
+  // rounded to fp16 once); one fused launch takes whole 128-row items and
+  // cannot use CTA pairs (the gate and up accumulators of a row would sit in
+  // different CTAs)
+  if (w_up && g_prefill_pair.load() != 2 && (g_prefill_pair.load() == 1 || M >= kWideMinM) &&
+      use_prefill(M, N, K, true, false)) {
+    float* part = may_alloc ? prefill_workspace(dev, s, di.sm_count) : nullptr;
+    const int st = run_prefill_pair<FMT, OutT>(di, dev, w_up, ws, a, c, M, N, K, error, s, part, 0);
+    if (st != BUSFILL_OK) return st;
+    return run_prefill_pair<FMT, OutT>(di, dev, w, ws, a, c, M, N, K, error, s, part, 1);
+  }
   // the stream-K workspace is only looked up (and made) for GEMMs that may use it
   const bool want_sk = may_alloc && !w_up && (g_prefill_min_m.load() > 0 || M > 32);
   float* part = want_sk ? prefill_workspace(dev, s, di.sm_count) : nullptr;

@@ -141,6 +141,7 @@ struct Params {
   int units;          // S = K / 256
   int swiglu;         // 1: C = silu(A Wg^T) * (A Wu^T); tmap_w gate, tmap_ws up (128-row boxes)
   float* part;        // stream-K partial tiles [2 G][BT batch rows][item rows], or nullptr
+  int gate_mul;       // CTA-pair kernel: 1 = C holds the up projection (fp16); write silu(A W^T) * C
 };
 
 // Stream-K range of CTA c of g over t units: [first_unit(c), first_unit(c + 1)).

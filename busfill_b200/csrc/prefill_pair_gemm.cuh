@@ -370,11 +370,22 @@ __global__ void __launch_bounds__(prefill_pair::kThreads, 1)
         waited_pdl = true;
       }
       const int n = grp * kItemRows + rank * kTileRows + r;
+      const int n0 = n - (lane & 7);   // the lane group's first weight row
 #pragma unroll 1
       for (int cb = 0; cb < mv; cb += 32) {
         uint32_t x[32];
         tmem_ld_x16(tmem + lane_off + (uint32_t)cb, x);
         tmem_ld_x16(tmem + lane_off + (uint32_t)(cb + 16), x + 16);
+        // SwiGLU second pass: the up values this lane will combine after the
+        // transpose, loaded before the TMEM wait so their latency overlaps it
+        uint4 up[4];
+        if (p.gate_mul && have && !part && vec16) {
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const int row = bt * kBatchTile + cb + 8 * b + (lane & 7);
+            if (row < p.M && n0 < p.N) up[b] = *reinterpret_cast<const uint4*>(C + (size_t)row * p.N + n0);
+          }
+        }
         tc_wait_ld();
         if (have && part) {
           // [batch row][this CTA's 128 weight rows], the item's existing batch rows
@@ -389,24 +400,37 @@ __global__ void __launch_bounds__(prefill_pair::kThreads, 1)
           // wait for it)
           float* v = reinterpret_cast<float*>(x);
           transpose_8x8_blocks<32>(v, lane);
-          const int n0 = n - (lane & 7);
 #pragma unroll
           for (int b = 0; b < 4; ++b) {
             const int row = bt * kBatchTile + cb + 8 * b + (lane & 7);
             if (row < p.M && n0 < p.N) {   // N % 8 == 0: the group's 8 rows are all in range
+              uint4* dst = reinterpret_cast<uint4*>(C + (size_t)row * p.N + n0);
+              if (p.gate_mul) {   // SwiGLU second pass: C holds the up projection
+                const __half2* uh = reinterpret_cast<const __half2*>(&up[b]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 uf = __half22float2(uh[e]);
+                  v[8 * b + 2 * e] = silu(v[8 * b + 2 * e]) * uf.x;
+                  v[8 * b + 2 * e + 1] = silu(v[8 * b + 2 * e + 1]) * uf.y;
+                }
+              }
               uint4 w;
               w.x = h2_as_u32(__floats2half2_rn(v[8 * b], v[8 * b + 1]));
               w.y = h2_as_u32(__floats2half2_rn(v[8 * b + 2], v[8 * b + 3]));
               w.z = h2_as_u32(__floats2half2_rn(v[8 * b + 4], v[8 * b + 5]));
               w.w = h2_as_u32(__floats2half2_rn(v[8 * b + 6], v[8 * b + 7]));
-              *reinterpret_cast<uint4*>(C + (size_t)row * p.N + n0) = w;
+              *dst = w;
             }
           }
         } else if (have && n < p.N) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             const int b = bt * kBatchTile + cb + i;
-            if (b < p.M) C[(size_t)b * p.N + n] = to_out<OutT>(__uint_as_float(x[i]));
+            if (b < p.M) {
+              OutT* dst = C + (size_t)b * p.N + n;
+              const float g = __uint_as_float(x[i]);
+              *dst = to_out<OutT>(p.gate_mul ? silu(g) * out_to_f32(*dst) : g);
+            }
           }
         }
       }
@@ -447,6 +471,7 @@ __global__ void __launch_bounds__(prefill_pair::kThreads, 1)
 template <typename OutT>
 __global__ void __launch_bounds__(256) prefill_pair_reduce_kernel(const float* __restrict__ part,
                                                                 OutT* __restrict__ c, int M, int N, int btiles,
+                                                                int gate_mul,
                                                                 const __grid_constant__ prefill::SplitItems si) {
   using namespace prefill_pair;
   pdl_wait_prerequisites();   // the partial tiles are the previous kernel's output
@@ -481,6 +506,12 @@ __global__ void __launch_bounds__(256) prefill_pair_reduce_kernel(const float* _
   const int b = bt * kBatchTile + row;
   const int n = grp * kItemRows + col;
   OutT* dst = c + (size_t)b * N + n;
+  if (gate_mul) {   // SwiGLU second pass: C holds the up projection
+    acc.x = n < N ? silu(acc.x) * out_to_f32(dst[0]) : 0.f;
+    acc.y = n + 1 < N ? silu(acc.y) * out_to_f32(dst[1]) : 0.f;
+    acc.z = n + 2 < N ? silu(acc.z) * out_to_f32(dst[2]) : 0.f;
+    acc.w = n + 3 < N ? silu(acc.w) * out_to_f32(dst[3]) : 0.f;
+  }
   if (n < N) dst[0] = to_out<OutT>(acc.x);
   if (n + 1 < N) dst[1] = to_out<OutT>(acc.y);
   if (n + 2 < N) dst[2] = to_out<OutT>(acc.z);

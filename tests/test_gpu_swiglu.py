@@ -1,5 +1,7 @@
 """GPU parity of the fused SwiGLU pair busfill_gemm_q4k_swiglu, through the C ABI:
-h = silu(A deq(Wg)^T) * (A deq(Wu)^T), fp32 products, one fp16 rounding.
+h = silu(A deq(Wg)^T) * (A deq(Wu)^T), fp32 products, one fp16 rounding (two
+on the CTA-pair path of M >= 256, where the up projection is rounded to fp16
+before the product).
 
 Checked against the oracle's float64 SwiGLU on the fp32-dequantized weights:
 rel-L2 <= 1e-3 and max abs err <= 2e-3 of the largest |h| (the kernel's fp16
@@ -55,13 +57,19 @@ def test_swiglu_decode_forced_ksplit(csize):
         bf.set_ksplit(0)
 
 
-@pytest.mark.parametrize("m,n,k", [(64, 512, 1024), (300, 640, 2048), (129, 200, 512)])
-def test_swiglu_prefill_forced(m, n, k):
+@pytest.mark.parametrize("pair", [0, 1, 2], ids=["auto", "pairs", "fused"])
+@pytest.mark.parametrize("m,n,k", [(64, 512, 1024), (300, 640, 2048), (129, 200, 512), (520, 1000, 1536)])
+def test_swiglu_prefill_forced(m, n, k, pair):
+    """The prefill kernels: one fused launch of whole (gate, up) tile pairs,
+    or (BUSFILL_OPT_PREFILL_PAIR, by default from M = 256) two CTA-pair GEMMs,
+    the up projection into h and then the gate with h = silu(gate) * h."""
     bf.set_prefill_min_m(1)
+    bf.set_prefill_pair(pair)
     try:
         run_and_check(m, n, k, seed=m * 3 + k)
     finally:
         bf.set_prefill_min_m(0)
+        bf.set_prefill_pair(0)
 
 
 def test_swiglu_config3_shape():
