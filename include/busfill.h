@@ -75,9 +75,13 @@ BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint1
  * with both products accumulated in fp32 and h rounded once to fp16.
  * w_gate and w_up are llama.cpp block_q4_K rows [N, K/256 x 144 B] (the
  * ffn_gate and ffn_up tensors), a [M, K] fp16, h [M, N] fp16. Requires
- * K % 256 == 0; all pointers 16-byte aligned. The gate and up tiles of the
- * same 128 rows are computed by the same CTAs, so neither product goes to
- * memory. No reference counterpart: the epilogue BASELINE config 3's layer
+ * K % 256 == 0; all pointers 16-byte aligned. Below M = 256 the gate and up
+ * tiles of the same 128 rows are computed by the same CTAs, so neither
+ * product goes to memory. From M = 256 (BUSFILL_OPT_PREFILL_PAIR) the pair
+ * runs as two CTA-pair GEMMs: the up projection into h (fp16), then the gate
+ * with h = fp16(silu(gate) * h), so the up product is rounded to fp16 before
+ * the multiplication (within the same accuracy gate; twice as fast as the
+ * fused launch there). No reference counterpart: the epilogue BASELINE config 3's layer
  * set puts after the up projection (kernels/q4k_batched.py:7-8 names the
  * Q4_K GEMM it belongs to). */
 BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const uint16_t* a, uint16_t* h,
@@ -378,8 +382,9 @@ BUSFILL_API int busfill_version(void);
  *     within the accuracy gate.
  *   BUSFILL_OPT_PREFILL_PAIR: 0 (default) runs prefill GEMMs of M >= 256 on
  *     CTA pairs (items of 256 weight rows x 256 batch rows, one MMA over the
- *     two SMs of a 2-CTA cluster, each loading half of the batch rows); 1
- *     runs every prefill GEMM but the SwiGLU pairs on CTA pairs; 2 never.
+ *     two SMs of a 2-CTA cluster, each loading half of the batch rows), and
+ *     SwiGLU pairs of M >= 256 as two such GEMMs; 1 does so for every prefill
+ *     GEMM and SwiGLU pair; 2 never.
  *     A tuning and test knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
