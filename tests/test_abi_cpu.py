@@ -594,4 +594,8 @@ def test_gemm_launch_count_by_shape():
     # 40 items x 20 units = 800 units over 40 CTAs: every range boundary on an item edge
     assert bf.gemm_launches(256, 5120, 5120, 40) == 1
     assert bf.gemm_launches(256, 5120, 5120, 100) == 2
+    # CTA pairs: 136 items of 256 x 256 on 68 of the 74 pairs, whole items, no fix-up
+    assert bf.gemm_launches(512, 17408, 5120, 148) == 1
+    # 40 items of 68 units on 74 pairs: stream-K, split items summed by the fix-up
+    assert bf.gemm_launches(512, 5120, 17408, 148) == 2
     assert bf.load_library().busfill_gemm_launches(8, 5120, 300, 148) == -2
