@@ -759,17 +759,22 @@ def cublas_comparator(torch, bf, dev, l2, weights, a, args):
 
 
 def e2e(torch, bf, dev, weights, a, args, steps):
-    """The same metric through the public API with HOST buffers. Each call
-    copies its activations from pinned host memory, runs the C-ABI GEMM and
-    reads its output back to pinned host memory; every call has its own host
-    and device buffers, as independent requests do. Two measurements:
+    """The same metric through the public API with HOST buffers: every step
+    copies its calls' activations from pinned host memory, runs the C-ABI
+    GEMMs and reads their outputs back to pinned host memory; every call has
+    its own host and device buffers. Three measurements:
 
     * value: the calls of a step (one per weight copy) captured once as a
-      CUDA graph with the copies on their own streams, so that call i+1's
-      input copy and call i-1's output copy overlap call i's GEMM (the way a
-      serving loop drives the library); the graph is replayed `steps` times,
-      replays one after another, CUDA events around them.
-    * eager_serial: the same calls issued one by one from Python on a single
+      CUDA graph, their transfers grouped `group` calls at a time (one
+      host-to-device copy of the group's activations, one device-to-host
+      copy of its outputs, on their own streams) so that group g+1's input
+      copy and group g-1's output copy overlap group g's GEMMs, as a serving
+      loop batches its transfers: a 327 KB copy each way per call is bound
+      by PCIe at ~16 us a call on B200 boxes (both directions at once),
+      more than the GEMM; the graph is replayed `steps` times, CUDA events
+      around the replays.
+    * per_call_copies: the same with one copy each way per call.
+    * eager_serial: the calls issued one by one from Python on a single
       stream (copy, GEMM, copy), host overheads included.
     """
     m, k = a.shape
@@ -794,22 +799,40 @@ def e2e(torch, bf, dev, weights, a, args, steps):
             gemm(i, w, s_cmp)
             h_c[i].copy_(d_c[i], non_blocking=True)
 
-    def pipelined_step():
+    def transfer_groups(group):
+        """Calls per transfer: `group` at a time, ramping up from and down to
+        one call at the step's ends, where a copy has no GEMM to hide behind."""
+        if group == 1:
+            return [1] * R
+        ramp = [1, group - 1]
+        sizes = ramp[:]
+        left = R - 2 * sum(ramp)
+        while left > 0:
+            sizes.append(min(group, left))
+            left -= sizes[-1]
+        sizes += ramp[::-1]
+        assert sum(sizes) == R
+        return sizes
+
+    def pipelined_step(group):
         fork = torch.cuda.Event()
         fork.record(s_cmp)
         s_in.wait_event(fork)
         s_out.wait_event(fork)
-        for i, w in enumerate(weights):
+        g1 = 0
+        for size in transfer_groups(group):
+            g0, g1 = g1, g1 + size
             e_in, e_cmp = torch.cuda.Event(), torch.cuda.Event()
             with torch.cuda.stream(s_in):
-                d_a[i].copy_(h_a[i], non_blocking=True)
+                d_a[g0:g1].copy_(h_a[g0:g1], non_blocking=True)
                 e_in.record(s_in)
             s_cmp.wait_event(e_in)
-            gemm(i, w, s_cmp)
+            for i in range(g0, g1):
+                gemm(i, weights[i], s_cmp)
             e_cmp.record(s_cmp)
             s_out.wait_event(e_cmp)
             with torch.cuda.stream(s_out):
-                h_c[i].copy_(d_c[i], non_blocking=True)
+                h_c[g0:g1].copy_(d_c[g0:g1], non_blocking=True)
         join_in, join_out = torch.cuda.Event(), torch.cuda.Event()
         join_in.record(s_in)
         join_out.record(s_out)
@@ -827,30 +850,43 @@ def e2e(torch, bf, dev, weights, a, args, steps):
         return e0.elapsed_time(e1)
 
     # warm-up, eager (also makes the library's per-stream words before capture)
+    group = 4 if R >= 12 else 1
     with torch.cuda.stream(s_cmp):
         for _ in range(2):
             serial_step()
-            pipelined_step()
+            pipelined_step(group)
+            pipelined_step(1)
     torch.cuda.synchronize(dev)
     ms_serial = timed(serial_step)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s_cmp):
-        pipelined_step()
-    with torch.cuda.stream(s_cmp):
-        g.replay()
-    torch.cuda.synchronize(dev)
-    ms = timed(g.replay)
-    assert bf.stream_status(s_cmp) == 0
-    # every call's output reached the host
-    want = d_c[R - 1].cpu()
-    assert torch.equal(h_c[R - 1], want) and torch.equal(h_c[0], d_c[0].cpu())
-    del g
+
+    def graph_ms(grp):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s_cmp):
+            pipelined_step(grp)
+        with torch.cuda.stream(s_cmp):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        h_c.zero_()
+        t = timed(g.replay)
+        assert bf.stream_status(s_cmp) == 0
+        # every call's output reached the host
+        assert torch.equal(h_c[R - 1], d_c[R - 1].cpu()) and torch.equal(h_c[0], d_c[0].cpu())
+        del g
+        return t
+
+    ms = graph_ms(group)
+    ms_1 = graph_ms(1)
     calls = steps * R
     return {"value": round(m * calls / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": R * m * k * 2, "d2h_bytes_per_step": R * m * n * 2,
             "us_per_call": round(ms * 1e3 / calls, 3), "steps": steps, "calls_per_step": R,
-            "path": "pinned host A -> cudaMemcpyAsync (stream 2) -> busfill_gemm_* (C ABI via ctypes, stream 1) -> "
-                    "cudaMemcpyAsync (stream 3) -> pinned host C; one step's calls captured as a CUDA graph",
+            "calls_per_transfer": transfer_groups(group),
+            "path": "pinned host A -> cudaMemcpyAsync of a group of calls' activations (stream 2) -> busfill_gemm_* "
+                    "(C ABI via ctypes, stream 1) -> cudaMemcpyAsync of their outputs (stream 3) -> pinned host C; "
+                    "one step's calls captured as a CUDA graph",
+            "per_call_copies": {"value": round(m * calls / (ms_1 / 1e3), 1), "unit": "tokens/s",
+                                "us_per_call": round(ms_1 * 1e3 / calls, 3),
+                                "path": "the same with one copy each way per call"},
             "eager_serial": {"value": round(m * calls / (ms_serial / 1e3), 1), "unit": "tokens/s",
                              "us_per_call": round(ms_serial * 1e3 / calls, 3),
                              "path": "the same calls from Python, one stream, no graph"}}
