@@ -71,8 +71,12 @@ int prefill_bt(int M, bool swiglu) {
 
 // CTA pairs (prefill_pair_gemm.cuh: items of 256 weight rows x 256 batch
 // rows on the two CTAs of a cluster, each loading half of the batch rows):
-// by default from kWideMinM rows; BUSFILL_OPT_PREFILL_PAIR 1 forces them for
-// every prefill GEMM but the SwiGLU pairs, 2 turns them off.
+// by default from kPairMinM rows (measured on B200, us one CTA / pairs:
+// M = 128, N = 17408, K = 5120 37.7 / 42.3; M = 160 56.7 / 43.6; M = 224
+// 58.9 / 46.5; N = 5120, K = 17408, M = 192 51.8 / 40.1);
+// BUSFILL_OPT_PREFILL_PAIR 1 forces them for every prefill GEMM but the
+// SwiGLU pairs, 2 turns them off.
+constexpr int kPairMinM = 129;
 std::atomic<int> g_prefill_pair{0};
 
 bool prefill_pairs(int M, bool swiglu) {
@@ -80,7 +84,7 @@ bool prefill_pairs(int M, bool swiglu) {
   const int mode = g_prefill_pair.load();
   if (mode == 1) return true;
   if (mode == 2) return false;
-  return M >= kWideMinM;
+  return M >= kPairMinM;
 }
 
 // work items of a prefill launch: weight-row groups x batch tiles

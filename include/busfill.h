@@ -380,7 +380,7 @@ BUSFILL_API int busfill_version(void);
  *     for M >= 256 and 128 (two weight tiles) below; 128 or 256 forces it
  *     (SwiGLU pairs always take 128). A tuning and test knob; results agree
  *     within the accuracy gate.
- *   BUSFILL_OPT_PREFILL_PAIR: 0 (default) runs prefill GEMMs of M >= 256 on
+ *   BUSFILL_OPT_PREFILL_PAIR: 0 (default) runs prefill GEMMs of M > 128 on
  *     CTA pairs (items of 256 weight rows x 256 batch rows, one MMA over the
  *     two SMs of a 2-CTA cluster, each loading half of the batch rows), and
  *     SwiGLU pairs of M >= 256 as two such GEMMs; 1 does so for every prefill
