@@ -99,6 +99,11 @@ bool use_prefill(int M, int N, int K, bool swiglu = false, bool stream_k = false
   const int forced = g_prefill_min_m.load();
   if (forced > 0) return M >= forced;
   if (stream_k && !swiglu) return M > kStreamKMinM || (M > 32 && N <= K && K >= kPrefillMinK);
+  // SwiGLU pairs: the decode kernel takes them 32 rows a launch; one fused
+  // prefill launch of whole items is faster from M = 33 (N = 17408, K = 5120,
+  // M = 64: 70 us as two decode launches; M = 96: 104 us as three; one
+  // prefill launch, 54 us at M = 128)
+  if (swiglu) return M > 32 && prefill_items(M, N, swiglu) >= kPrefillMinItems;
   return M >= 128 && prefill_items(M, N, swiglu) >= kPrefillMinItems;
 }
 
@@ -738,12 +743,13 @@ int run_prefill(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t*
 template <WFmt FMT, typename OutT>
 int run_gemm(const DeviceInfo& di, int dev, const uint8_t* w, const uint16_t* ws, const uint16_t* a, void* c, int M,
              int N, int K, unsigned* error, cudaStream_t s, const uint8_t* w_up = nullptr, bool may_alloc = true) {
-  // SwiGLU pairs of many rows: two CTA-pair GEMMs, the up projection into C,
-  // then the gate with an epilogue that writes silu(gate) * C (the up values
-  // rounded to fp16 once); one fused launch takes whole 128-row items and
-  // cannot use CTA pairs (the gate and up accumulators of a row would sit in
-  // different CTAs)
-  if (w_up && g_prefill_pair.load() != 2 && (g_prefill_pair.load() == 1 || M >= kWideMinM) &&
+  // SwiGLU pairs of more than 128 rows: two CTA-pair GEMMs, the up
+  // projection into C, then the gate with an epilogue that writes silu(gate)
+  // * C (the up values rounded to fp16 once); one fused launch takes whole
+  // 128-row items and cannot use CTA pairs (the gate and up accumulators of a
+  // row would sit in different CTAs). N = 17408, K = 5120, us fused / two
+  // passes: M = 128 53.9 / 83.8; 160 99.7 / 85.2; 224 101.8 / 94.7.
+  if (w_up && g_prefill_pair.load() != 2 && (g_prefill_pair.load() == 1 || M >= kPairMinM) &&
       use_prefill(M, N, K, true, false)) {
     float* part = may_alloc ? prefill_workspace(dev, s, di.sm_count) : nullptr;
     const int st = run_prefill_pair<FMT, OutT>(di, dev, w_up, ws, a, c, M, N, K, error, s, part, 0);

@@ -75,9 +75,9 @@ BUSFILL_API int busfill_gemm_q4k(const uint8_t* blocks, const uint16_t* a, uint1
  * with both products accumulated in fp32 and h rounded once to fp16.
  * w_gate and w_up are llama.cpp block_q4_K rows [N, K/256 x 144 B] (the
  * ffn_gate and ffn_up tensors), a [M, K] fp16, h [M, N] fp16. Requires
- * K % 256 == 0; all pointers 16-byte aligned. Below M = 256 the gate and up
+ * K % 256 == 0; all pointers 16-byte aligned. Up to M = 128 the gate and up
  * tiles of the same 128 rows are computed by the same CTAs, so neither
- * product goes to memory. From M = 256 (BUSFILL_OPT_PREFILL_PAIR) the pair
+ * product goes to memory. Above M = 128 (BUSFILL_OPT_PREFILL_PAIR) the pair
  * runs as two CTA-pair GEMMs: the up projection into h (fp16), then the gate
  * with h = fp16(silu(gate) * h), so the up product is rounded to fp16 before
  * the multiplication (within the same accuracy gate; twice as fast as the
@@ -383,7 +383,7 @@ BUSFILL_API int busfill_version(void);
  *   BUSFILL_OPT_PREFILL_PAIR: 0 (default) runs prefill GEMMs of M > 128 on
  *     CTA pairs (items of 256 weight rows x 256 batch rows, one MMA over the
  *     two SMs of a 2-CTA cluster, each loading half of the batch rows), and
- *     SwiGLU pairs of M >= 256 as two such GEMMs; 1 does so for every prefill
+ *     SwiGLU pairs of M > 128 as two such GEMMs; 1 does so for every prefill
  *     GEMM and SwiGLU pair; 2 never.
  *     A tuning and test knob; results agree within the accuracy gate.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */

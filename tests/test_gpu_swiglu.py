@@ -72,6 +72,13 @@ def test_swiglu_prefill_forced(m, n, k, pair):
         bf.set_prefill_pair(0)
 
 
+@pytest.mark.parametrize("m", [48, 100, 200])
+def test_swiglu_default_dispatch_mid_batch(m):
+    """Default dispatch between the decode launches (M <= 32), one fused
+    prefill launch (32 < M <= 128) and two CTA-pair GEMMs (M > 128)."""
+    run_and_check(m, 8192, 512, seed=m + 11)
+
+
 def test_swiglu_config3_shape():
     """The 27B layer set's gate/up pair (N = 17408, K = 5120) at M = 32."""
     run_and_check(32, 17408, 5120, seed=7)
