@@ -719,7 +719,7 @@ int run_prefill_pair(const DeviceInfo& di, int dev, const uint8_t* w, const uint
     int m = M, n = N, bts = p.btiles, gm = gate_mul;
     void* rargs[] = {&cpart, &cc, &m, &n, &bts, &gm, &si};
     const int rows = std::min(M, prefill_pair::kBatchTile);
-    if (launch(reinterpret_cast<const void*>(prefill_pair_reduce_kernel<OutT>), dim3(si.n, (rows + 3) / 4),
+    if (launch(reinterpret_cast<const void*>(prefill_pair_reduce_kernel<OutT>), dim3(si.n, (rows + 15) / 16),
                dim3(256), 0, s, rargs, g_use_pdl.load() != 0) != cudaSuccess) {
       cudaGetLastError();
       return BUSFILL_ERR_LAUNCH;

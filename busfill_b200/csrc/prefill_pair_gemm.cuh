@@ -466,8 +466,9 @@ __global__ void __launch_bounds__(prefill_pair::kThreads, 1)
 // to 256 batch rows) is summed from the partial tiles of its pairs, in pair
 // order, and written to C. A pair's partial of an item is two tiles, one per
 // CTA (its 128 weight rows); CTA 2 c + r of pair c holds slots 2 (2 c + r)
-// (first item) and + 1 (last item). Block (x, y): split item x, batch rows 4 y
-// .. 4 y + 3, 64 threads per batch row, each owning 4 consecutive weight rows.
+// (first item) and + 1 (last item). Block (x, y): split item x, batch rows
+// 16 y .. 16 y + 15; thread t owns 4 consecutive weight rows (4 (t % 64) ..)
+// of batch rows 16 y + 4 (t / 64) .. + 3.
 template <typename OutT>
 __global__ void __launch_bounds__(256) prefill_pair_reduce_kernel(const float* __restrict__ part,
                                                                 OutT* __restrict__ c, int M, int N, int btiles,
@@ -479,43 +480,59 @@ __global__ void __launch_bounds__(256) prefill_pair_reduce_kernel(const float* _
   const int4 e = si.e[blockIdx.x];
   const int it = e.x, c_lo = e.y, c_hi = e.z, slot_lo = e.w;   // pair indices; slot of c_lo's piece (2 c_lo + which)
   const int grp = it / btiles, bt = it - (it / btiles) * btiles;
-  const int row = 4 * (int)blockIdx.y + ((int)threadIdx.x >> 6);   // batch row within the item
-  const int col = 4 * ((int)threadIdx.x & 63);                     // weight row within the item
-  if (bt * kBatchTile + row >= M) return;
-  const int half = col >> 7;                                       // the CTA of the pair holding it
-  const size_t off = (size_t)row * kTileRows + (col & 127);
-  auto slot_ptr = [&](int cc) {
+  // 4 batch rows per thread: their loads (two pieces at a time) are in
+  // flight together, 8 per thread instead of 2 (at M = 512, N = 5120, K =
+  // 17408 the fix-up of 40 split items took ~13 us under ncu with one row)
+  constexpr int kRowsPerThread = 4;
+  const int row0 = 16 * (int)blockIdx.y + kRowsPerThread * ((int)threadIdx.x >> 6);   // batch rows within the item
+  const int col = 4 * ((int)threadIdx.x & 63);                                          // weight row within the item
+  const int half = col >> 7;                                                           // the CTA of the pair holding it
+  const int b0 = bt * kBatchTile + row0;
+  if (b0 >= M) return;
+  const int nrows = min(kRowsPerThread, M - b0);
+  auto slot_ptr = [&](int cc, int rr) {
     const int slot = cc == c_lo ? 2 * (2 * c_lo + half) + (slot_lo & 1) : 2 * (2 * cc + half);
-    return reinterpret_cast<const float4*>(part + (size_t)slot * prefill::kPartElems + off);
+    return reinterpret_cast<const float4*>(part + (size_t)slot * prefill::kPartElems +
+                                           (size_t)(row0 + rr) * kTileRows + (col & 127));
   };
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int c0 = c_lo; c0 <= c_hi; c0 += 8) {
-    float4 v[8];
+  float4 acc[kRowsPerThread];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (c0 + i <= c_hi) v[i] = *slot_ptr(c0 + i);
+  for (int rr = 0; rr < kRowsPerThread; ++rr) acc[rr] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c0 = c_lo; c0 <= c_hi; c0 += 2) {   // pieces in pair order, two at a time
+    float4 v[kRowsPerThread][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (c0 + i <= c_hi) {
-        acc.x += v[i].x;
-        acc.y += v[i].y;
-        acc.z += v[i].z;
-        acc.w += v[i].w;
-      }
+    for (int rr = 0; rr < kRowsPerThread; ++rr)
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (rr < nrows && c0 + i <= c_hi) v[rr][i] = *slot_ptr(c0 + i, rr);
+#pragma unroll
+    for (int rr = 0; rr < kRowsPerThread; ++rr)
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+        if (rr < nrows && c0 + i <= c_hi) {
+          acc[rr].x += v[rr][i].x;
+          acc[rr].y += v[rr][i].y;
+          acc[rr].z += v[rr][i].z;
+          acc[rr].w += v[rr][i].w;
+        }
   }
-  const int b = bt * kBatchTile + row;
   const int n = grp * kItemRows + col;
-  OutT* dst = c + (size_t)b * N + n;
-  if (gate_mul) {   // SwiGLU second pass: C holds the up projection
-    acc.x = n < N ? silu(acc.x) * out_to_f32(dst[0]) : 0.f;
-    acc.y = n + 1 < N ? silu(acc.y) * out_to_f32(dst[1]) : 0.f;
-    acc.z = n + 2 < N ? silu(acc.z) * out_to_f32(dst[2]) : 0.f;
-    acc.w = n + 3 < N ? silu(acc.w) * out_to_f32(dst[3]) : 0.f;
+#pragma unroll
+  for (int rr = 0; rr < kRowsPerThread; ++rr) {
+    if (rr >= nrows) break;
+    float4 a = acc[rr];
+    OutT* dst = c + (size_t)(b0 + rr) * N + n;
+    if (gate_mul) {   // SwiGLU second pass: C holds the up projection
+      a.x = n < N ? silu(a.x) * out_to_f32(dst[0]) : 0.f;
+      a.y = n + 1 < N ? silu(a.y) * out_to_f32(dst[1]) : 0.f;
+      a.z = n + 2 < N ? silu(a.z) * out_to_f32(dst[2]) : 0.f;
+      a.w = n + 3 < N ? silu(a.w) * out_to_f32(dst[3]) : 0.f;
+    }
+    if (n < N) dst[0] = to_out<OutT>(a.x);
+    if (n + 1 < N) dst[1] = to_out<OutT>(a.y);
+    if (n + 2 < N) dst[2] = to_out<OutT>(a.z);
+    if (n + 3 < N) dst[3] = to_out<OutT>(a.w);
   }
-  if (n < N) dst[0] = to_out<OutT>(acc.x);
-  if (n + 1 < N) dst[1] = to_out<OutT>(acc.y);
-  if (n + 2 < N) dst[2] = to_out<OutT>(acc.z);
-  if (n + 3 < N) dst[3] = to_out<OutT>(acc.w);
 }
 
 }  // namespace busfill
