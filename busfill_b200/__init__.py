@@ -19,7 +19,7 @@ import re
 
 __all__ = [
     "BusfillError", "load_library", "library_path", "header_functions",
-    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q4k_noalloc", "gemm_q5k", "gemm_q6k", "repack_q6k",
+    "gemm_q4_0", "gemm_q4k", "gemm_q4_0_ggml", "gemm_q4k_swiglu", "gemm_q4k_sweep", "SweepOp", "gemm_q4k_noalloc", "gemm_q5k", "gemm_q6k", "repack_q6k",
     "busfill_q4", "repack_q4k_planar", "gemm_q4k_planar", "Tensor", "tensor_desc", "mul_mat", "dequant_q4_0", "dequant_q4_0_ggml", "dequant_q4k", "dequant_q5k", "dequant_q6k",
     "stream_status", "stream_status_bits", "noalloc_status", "internal_allocations", "set_pdl", "set_ksplit", "set_prefill_min_m", "set_exact_kquant", "uses_prefill", "gemm_launches", "probe_umma", "version",
 ]
@@ -63,6 +63,7 @@ _SIGS = {
     "busfill_gemm_q4k": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4_0_ggml": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_gemm_q4k_swiglu": [_P, _P, _P, _P, _I, _I, _I, _P],
+    "busfill_gemm_q4k_sweep": [_P, _I, _I, _P],
     "busfill_gemm_q5k": [_P, _P, _P, _I, _I, _I, _P],
     "busfill_dequant_q5k": [_P, _P, _I, _I, _P],
     "busfill_gemm_q6k": [_P, _P, _P, _P, _I, _I, _I, _P],
@@ -273,6 +274,46 @@ def gemm_q4k_swiglu(w_gate, w_up, a, out=None, stream=None):
     _check(_lib().busfill_gemm_q4k_swiglu(_ptr(w_gate), _ptr(w_up), _ptr(a), _ptr(out), m, n, k, _stream(stream)),
            "busfill_gemm_q4k_swiglu")
     return out
+
+
+class SweepOp(ctypes.Structure):
+    """busfill_sweep_op: one GEMM of a layer sweep."""
+    _fields_ = [("w", _P), ("w_up", _P), ("a", _P), ("c", _P), ("N", _I), ("K", _I), ("dep", _I)]
+
+
+SWEEP_MAX_OPS = 4
+
+
+def gemm_q4k_sweep(ops, stream=None):
+    """Run up to SWEEP_MAX_OPS Q4_K GEMMs of one batch size M <= 32 as one
+    launch (busfill_gemm_q4k_sweep). `ops` is a list of dicts with keys ``w``
+    (block_q4_K rows [N, K/256*144]), ``a`` (fp16 [M, K]), ``out`` (fp16
+    [M, N]) and optionally ``w_up`` (SwiGLU pair: out = silu(a w^T) * (a
+    w_up^T)) and ``dep`` (index of the earlier op whose output ``a`` is).
+    Returns the outputs."""
+    torch = _torch()
+    if not 1 <= len(ops) <= SWEEP_MAX_OPS:
+        raise ValueError(f"1..{SWEEP_MAX_OPS} ops, got {len(ops)}")
+    arr = (SweepOp * len(ops))()
+    m = None
+    for i, op in enumerate(ops):
+        w, a, out, w_up = op["w"], op["a"], op["out"], op.get("w_up")
+        _need(w, torch.uint8, "w"); _need(a, torch.float16, "a"); _need(out, torch.float16, "out")
+        mi, k = a.shape
+        n = w.shape[0]
+        if m is None:
+            m = mi
+        if mi != m or k % 256 or w.shape[1] != k // 256 * 144 or tuple(out.shape) != (m, n):
+            raise ValueError(f"op {i}: shape mismatch: w {tuple(w.shape)}, a {tuple(a.shape)}, out {tuple(out.shape)}")
+        if w_up is not None:
+            _need(w_up, torch.uint8, "w_up")
+            if tuple(w_up.shape) != tuple(w.shape):
+                raise ValueError(f"op {i}: w_up {tuple(w_up.shape)} != w {tuple(w.shape)}")
+        arr[i].w, arr[i].a, arr[i].c = w.data_ptr(), a.data_ptr(), out.data_ptr()
+        arr[i].w_up = w_up.data_ptr() if w_up is not None else None
+        arr[i].N, arr[i].K, arr[i].dep = n, k, int(op.get("dep", -1))
+    _check(_lib().busfill_gemm_q4k_sweep(arr, len(ops), m, _stream(stream)), "busfill_gemm_q4k_sweep")
+    return [op["out"] for op in ops]
 
 
 def gemm_q4k_noalloc(blocks, a, out, stream=None):

@@ -18,6 +18,7 @@
 #include "decode_gemm.cuh"
 #include "prefill_gemm.cuh"
 #include "prefill_pair_gemm.cuh"
+#include "sweep_gemm.cuh"
 #include "dequant.cuh"
 
 using namespace busfill;
@@ -244,6 +245,33 @@ float* prefill_workspace(int dev, cudaStream_t s, int sm_count) {
       w = nullptr;
     } else {
       ++g_internal_allocs;
+    }
+  }
+  return w;
+}
+
+// The layer-sweep kernel's workspace, one per (device, stream): its counter
+// words (zeroed here; the kernel leaves them zero) and the partial tiles of
+// up to sm_count CTAs per op. Never made while the stream is capturing.
+std::map<std::pair<int, cudaStream_t>, unsigned*> g_sweep;
+
+unsigned* sweep_workspace(int dev, cudaStream_t s, int sm_count) {
+  // caller holds g_mu
+  unsigned*& w = g_sweep[{dev, s}];
+  if (!w) {
+    if (capturing(s)) return nullptr;
+    const size_t bytes = (size_t)sweep::kFlagWords * 4 + (size_t)sweep::kMaxOps * sm_count * sweep::kSlotsPerCta *
+                                                               kTileRows * sweep::kMaxNB * sizeof(float);
+    if (cudaMalloc(&w, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      w = nullptr;
+      return nullptr;
+    }
+    ++g_internal_allocs;
+    if (cudaMemsetAsync(w, 0, (size_t)sweep::kFlagWords * 4, s) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w);
+      w = nullptr;
     }
   }
   return w;
@@ -932,6 +960,87 @@ int repack_q4k_planar_impl(const uint8_t* qs, const uint16_t* d, const uint16_t*
   return cudaGetLastError() == cudaSuccess ? BUSFILL_OK : BUSFILL_ERR_LAUNCH;
 }
 
+// ---------------------------------------------------------------------------
+// layer sweep: several small-batch Q4_K GEMMs in one launch
+// ---------------------------------------------------------------------------
+template <int NB>
+int launch_sweep(int dev, const sweep::Params& p, cudaStream_t s) {
+  const void* kern = reinterpret_cast<const void*>(sweep::sweep_gemm_kernel<NB>);
+  constexpr int smem = sweep::Smem<NB>::kAlloc;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return BUSFILL_ERR_LAUNCH;
+  void* args[] = {const_cast<sweep::Params*>(&p)};
+  if (launch(kern, dim3((unsigned)p.G), dim3(kThreads), smem, s, args, g_use_pdl.load() != 0) != cudaSuccess) {
+    cudaGetLastError();
+    return BUSFILL_ERR_LAUNCH;
+  }
+  return BUSFILL_OK;
+}
+
+int gemm_sweep_impl(const busfill_sweep_op* ops, int nops, int M, cudaStream_t s) {
+  if (!ops) return BUSFILL_ERR_INVALID_ARG;
+  if (nops < 1 || nops > sweep::kMaxOps || M < 1 || M > sweep::kMaxNB) return BUSFILL_ERR_SHAPE;
+  for (int o = 0; o < nops; ++o) {
+    const busfill_sweep_op& op = ops[o];
+    if (!op.w || !op.a || !op.c || op.dep < -1 || op.dep >= o) return BUSFILL_ERR_INVALID_ARG;
+    if (op.N < 1 || op.N > sweep::kMaxTiles * kTileRows || op.K < kUnitK || op.K % kUnitK != 0 ||
+        op.K > (1 << 20))
+      return BUSFILL_ERR_SHAPE;
+    if (!aligned16(op.w) || !aligned16(op.a) || (op.w_up && !aligned16(op.w_up))) return BUSFILL_ERR_ALIGNMENT;
+  }
+  DeviceInfo di;
+  int dev = 0;
+  int st = current_device(&di, &dev);
+  if (st != BUSFILL_OK) return st;
+  unsigned* err = nullptr;
+  unsigned* ws = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    st = get_error_words(dev, s, &err);
+    if (st != BUSFILL_OK) return st;
+    ws = sweep_workspace(dev, s, di.sm_count);
+  }
+  if (!ws) return BUSFILL_ERR_ALLOC;
+  const int nb = M <= 16 ? 16 : 32;
+  sweep::Params p;
+  std::memset(&p, 0, sizeof(p));
+  unsigned max_units = 0;
+  for (int o = 0; o < nops; ++o) {
+    const busfill_sweep_op& op = ops[o];
+    const int S = op.K / kUnitK;
+    const uint64_t row = (uint64_t)S * kQ4KBlockBytes;
+    if (!make_tmap_2d(&p.tw[o], CU_TENSOR_MAP_DATA_TYPE_UINT8, op.w, row, (uint64_t)op.N, row, kQ4KBlockBytes,
+                      kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    p.twu[o] = p.tw[o];
+    if (op.w_up && !make_tmap_2d(&p.twu[o], CU_TENSOR_MAP_DATA_TYPE_UINT8, op.w_up, row, (uint64_t)op.N, row,
+                                 kQ4KBlockBytes, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return BUSFILL_ERR_CUDA;
+    if (!make_tmap_act3d(&p.ta[o], op.a, (uint64_t)M, (uint64_t)op.K, (uint32_t)nb, kChunksPerUnit))
+      return BUSFILL_ERR_CUDA;
+    sweep::Op& d = p.op[o];
+    d.c = op.c;
+    d.N = op.N;
+    d.tiles = (op.N + kTileRows - 1) / kTileRows;
+    d.S = S;
+    d.planes = op.w_up ? 2 : 1;
+    d.dep = op.dep;
+    d.units = (unsigned)d.tiles * (unsigned)d.planes * (unsigned)S;
+    max_units = std::max(max_units, d.units);
+  }
+  p.nops = nops;
+  p.M = M;
+  p.G = (int)std::min<unsigned>((unsigned)di.sm_count, max_units);
+  p.flags = ws;
+  p.part = reinterpret_cast<float*>(ws + sweep::kFlagWords);
+  p.error = err;
+  return nb == 16 ? launch_sweep<16>(dev, p, s) : launch_sweep<32>(dev, p, s);
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1028,6 +1137,10 @@ int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_up, const ui
                             int K, void* stream) {
   return gemm_impl<WFmt::Q4K, __half>(w_gate, nullptr, a, h, M, N, K, reinterpret_cast<cudaStream_t>(stream), w_up,
                                       true);
+}
+
+int busfill_gemm_q4k_sweep(const busfill_sweep_op* ops, int nops, int M, void* stream) {
+  return gemm_sweep_impl(ops, nops, M, reinterpret_cast<cudaStream_t>(stream));
 }
 
 int busfill_gemm_q5k(const uint8_t* blocks, const uint16_t* a, uint16_t* c, int M, int N, int K, void* stream) {
@@ -1332,8 +1445,12 @@ int busfill_stream_status_ex(void* stream, unsigned* bits) {
     g_last_detail = err2[1];
   }
   if (err == 0) return BUSFILL_OK;
-  // a kernel gave up part way: clear the words for the next call
+  // a kernel gave up part way: clear the words for the next call, and the
+  // layer-sweep counters (a CTA that gave up may have left some raised)
   if (cudaMemset(it->second, 0, kErrorWordsBytes) != cudaSuccess) return BUSFILL_ERR_CUDA;
+  auto sw = g_sweep.find({dev, s});
+  if (sw != g_sweep.end() && sw->second && cudaMemset(sw->second, 0, (size_t)sweep::kFlagWords * 4) != cudaSuccess)
+    return BUSFILL_ERR_CUDA;
   return BUSFILL_ERR_DEVICE_TIMEOUT;
 }
 

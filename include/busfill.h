@@ -88,6 +88,36 @@ BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_
                                         int M, int N, int K, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Layer sweep: up to BUSFILL_SWEEP_MAX_OPS small-batch Q4_K GEMMs in one launch
+ *
+ * Runs a list of GEMMs ("ops") that share the batch M (1..32) as one kernel
+ * launch, e.g. a decoder layer's O, QKV, gate/up (SwiGLU) and down
+ * projections. Op o computes c[M, N] = a[M, K] deq(w)[N, K]^T, or with w_up
+ * the SwiGLU pair c = silu(a deq(w)^T) * (a deq(w_up)^T), from block_q4_K
+ * rows as busfill_gemm_q4k takes them, with the same numerics. Every op's
+ * units are split evenly over all SMs; a CTA moves on to the next op's weights
+ * as soon as it has done its share of one, and an op with dep = j >= 0 reads
+ * its activations only once op j's whole output is stored (j < o: its `a` is
+ * op j's `c`, or computed from it). Ops with dep = -1 must not read an
+ * earlier op's output in this call. Outputs must not overlap inputs.
+ * The first call on a stream allocates its workspace (~40 MB: counters and
+ * partial tiles; fails with BUSFILL_ERR_ALLOC inside a graph capture); calls
+ * on one stream share it in stream order. Failures are read with
+ * busfill_stream_status. No reference counterpart: the reference launches
+ * one GEMM per kernel (kernels/busfill_v1a.cu:151-154); this is the layer
+ * set of its decode benchmark as one launch. */
+#define BUSFILL_SWEEP_MAX_OPS 4
+typedef struct busfill_sweep_op {
+  const uint8_t* w;      /* block_q4_K rows [N][K/256 * 144] (the gate with w_up) */
+  const uint8_t* w_up;   /* SwiGLU: the up projection's rows, same shape; else NULL */
+  const uint16_t* a;     /* activations [M][K] fp16 */
+  uint16_t* c;           /* output [M][N] fp16 */
+  int N, K;
+  int dep;               /* index of the earlier op whose output `a` is, or -1 */
+} busfill_sweep_op;
+BUSFILL_API int busfill_gemm_q4k_sweep(const busfill_sweep_op* ops, int nops, int M, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Column-split GEMMs with the all-gather fused into the epilogue
  *
  * Over a group of `npeers` GPUs (one process each, same node), rank r holds

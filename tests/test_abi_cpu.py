@@ -599,3 +599,101 @@ def test_gemm_launch_count_by_shape():
     # 40 items of 68 units on 74 pairs: stream-K, split items summed by the fix-up
     assert bf.gemm_launches(512, 5120, 17408, 148) == 2
     assert bf.load_library().busfill_gemm_launches(8, 5120, 300, 148) == -2
+
+
+# ---------------------------------------------------------------------------
+# layer sweep (busfill_gemm_q4k_sweep)
+# ---------------------------------------------------------------------------
+def _sweep_ops(specs):
+    arr = (bf.SweepOp * max(1, len(specs)))()
+    buf = ctypes.create_string_buffer(64)
+    base = (ctypes.addressof(buf) + 15) // 16 * 16
+    for i, (n, k, dep, up) in enumerate(specs):
+        arr[i].w, arr[i].a, arr[i].c = base, base, base
+        arr[i].w_up = base if up else None
+        arr[i].N, arr[i].K, arr[i].dep = n, k, dep
+    return arr, buf
+
+
+def test_sweep_checks_before_any_device_work():
+    lib = bf.load_library()
+    ops, keep = _sweep_ops([(256, 512, -1, False), (512, 256, 0, True)])
+    assert lib.busfill_gemm_q4k_sweep(None, 1, 8, None) == -1
+    assert lib.busfill_gemm_q4k_sweep(ops, 0, 8, None) == -2          # no ops
+    assert lib.busfill_gemm_q4k_sweep(ops, 5, 8, None) == -2          # more than BUSFILL_SWEEP_MAX_OPS
+    assert lib.busfill_gemm_q4k_sweep(ops, 2, 0, None) == -2          # M < 1
+    assert lib.busfill_gemm_q4k_sweep(ops, 2, 33, None) == -2         # M > 32
+    bad, keep2 = _sweep_ops([(256, 512, 0, False)])                   # depends on itself
+    assert lib.busfill_gemm_q4k_sweep(bad, 1, 8, None) == -1
+    bad, keep3 = _sweep_ops([(256, 512, -1, False), (256, 512, 1, False)])   # on a later op
+    assert lib.busfill_gemm_q4k_sweep(bad, 2, 8, None) == -1
+    bad, keep4 = _sweep_ops([(256, 500, -1, False)])                  # K % 256
+    assert lib.busfill_gemm_q4k_sweep(bad, 1, 8, None) == -2
+    bad, keep5 = _sweep_ops([(1024 * 128 + 1, 256, -1, False)])      # N beyond 1024 tiles
+    assert lib.busfill_gemm_q4k_sweep(bad, 1, 8, None) == -2
+    bad, keep6 = _sweep_ops([(256, 512, -1, False)])
+    bad[0].a = bad[0].a + 2                                           # activations not 16-byte aligned
+    assert lib.busfill_gemm_q4k_sweep(bad, 1, 8, None) == -3
+
+
+def _sweep_schedule(ops, g):
+    """The sweep kernel's split restated (sweep_gemm.cuh: range_begin, owner,
+    slot_of): per op, CTA b takes units [U b / G, U (b + 1) / G); returns per
+    op the units covered, the partial slots written and the tiles stored."""
+    def rb(u, b):
+        return u * b // g
+
+    def owner(u_tot, u):
+        return ((u + 1) * g - 1) // u_tot
+
+    res = []
+    for tiles, s, planes in ops:
+        u_tot, q = tiles * s * planes, s * planes
+        covered, slots, arrivals, stored = {}, {}, {}, []
+        for b in range(g):
+            rs, re = rb(u_tot, b), rb(u_tot, b + 1)
+            u = rs
+            while u < re:
+                tile, w = divmod(u, q)
+                pl, sb = divmod(w, s)
+                ln = min(s - sb, re - u)
+                for j in range(ln):
+                    assert (tile, pl, sb + j) not in covered
+                    covered[(tile, pl, sb + j)] = b
+                whole = rs <= tile * q and (tile + 1) * q <= re
+                if whole:
+                    if pl == planes - 1:
+                        stored.append(tile)
+                else:
+                    k = (0 if rs // q == tile else 2) + pl
+                    assert (b, k) not in slots
+                    slots[(b, k)] = (tile, pl)
+                    if u + ln == min((tile + 1) * q, re):
+                        arrivals.setdefault(tile, []).append(b)
+                u += ln
+        for tile, bs in arrivals.items():
+            c_lo, c_hi = owner(u_tot, tile * q), owner(u_tot, tile * q + q - 1)
+            assert bs == [c for c in range(c_lo, c_hi + 1) if rb(u_tot, c) < rb(u_tot, c + 1)]
+            stored.append(tile)
+            for pl in range(planes):
+                lo, hi = tile * q + pl * s, tile * q + (pl + 1) * s
+                n = 0
+                for c in range(c_lo, c_hi + 1):
+                    a0, a1 = rb(u_tot, c), rb(u_tot, c + 1)
+                    if max(a0, lo) < min(a1, hi):
+                        assert slots[(c, (0 if a0 // q == tile else 2) + pl)] == (tile, pl)
+                        n += min(a1, hi) - max(a0, lo)
+                assert n == s
+        res.append((len(covered) == u_tot, sorted(stored) == list(range(tiles))))
+    return res
+
+
+@pytest.mark.parametrize("g", [1, 2, 7, 64, 148])
+def test_sweep_schedule_covers_every_unit_and_stores_every_tile_once(g):
+    # BASELINE config 3's layer (O, QKV, gate/up pair, down) and small ops
+    # with fewer units than CTAs
+    layer = [(40, 32, 1), (80, 20, 1), (136, 20, 2), (40, 68, 1)]
+    small = [(1, 1, 1), (3, 2, 2), (16, 4, 1), (5, 3, 2)]
+    for ops in (layer, small):
+        gg = min(g, max(t * s * p for t, s, p in ops))
+        assert all(a and b for a, b in _sweep_schedule(ops, gg))
