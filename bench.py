@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-extras", action="store_true", help="skip sweep / cuBLAS / e2e / CPU / layer-set legs")
     ap.add_argument("--layers", type=int, default=64, help="layers in the BASELINE config-3 layer-set sweep")
+    ap.add_argument("--layerset-only", action="store_true",
+                    help="after the headline, run the layer-set leg alone (profiling the layer-sweep kernel)")
     return ap.parse_args()
 
 
@@ -462,7 +464,7 @@ def run_busfill(args):
 
     if not args.no_extras:
         out["layerset"] = layerset(torch, bf, tp, dev, world, rank, args, hbm_peak)
-    if world == 1 and not args.no_extras:
+    if world == 1 and not args.no_extras and not args.layerset_only:
         out["isolated_no_pdl"] = isolated_no_pdl(bf, capture, time_graph, min(steps, 50), R, M)
         out["sweep"] = sweep(torch, bf, dev, l2, hbm_peak, args)
         out["cublas_fp16"] = cublas_comparator(torch, bf, dev, l2, weights, a, args)
@@ -662,6 +664,45 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     del g
+    fused = None
+    if world == 1:
+        # the same layers as one busfill_gemm_q4k_sweep launch each (ops in
+        # the order O, QKV, gate/up after O, down after gate/up; the down
+        # outputs alternate between two buffers so no op writes what another
+        # op of its launch reads)
+        downs = [full["down"], torch.empty_like(full["down"])]
+
+        def sweep_fused():
+            h = x
+            for li, lw in enumerate(layers):
+                dn = downs[li & 1]
+                bf.gemm_q4k_sweep([{"w": lw["o"], "a": attn, "out": full["o"]},
+                                   {"w": lw["qkv"], "a": h, "out": full["qkv"]},
+                                   {"w": lw["gate"], "w_up": lw["up"], "a": full["o"], "out": full["gate"], "dep": 0},
+                                   {"w": lw["down"], "a": full["gate"], "out": dn, "dep": 2}], stream=st)
+                h = dn
+
+        with torch.cuda.stream(st):
+            sweep_fused()
+            st.synchronize()
+            assert bf.stream_status(st) == 0
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2, stream=st):
+                sweep_fused()
+            g2.replay()
+            st.synchronize()
+            e0.record(st)
+            for _ in range(sweeps):
+                g2.replay()
+            e1.record(st)
+        e1.synchronize()
+        assert bf.stream_status(st) == 0
+        ms2 = e0.elapsed_time(e1) / sweeps
+        del g2
+        fused = {"ms_per_sweep": round(ms2, 4), "us_per_layer": round(ms2 * 1e3 / L, 2),
+                 "tokens_per_s": round(m / (ms2 * 1e-3), 1),
+                 "hbm_frac_per_gpu": round(local_bytes / (ms2 * 1e-3) / 1e9 / hbm_peak, 4),
+                 "kernels": "busfill_gemm_q4k_sweep x1 per layer (4 ops, stream-K over all SMs)"}
     del layers
     if space is not None:
         torch.cuda.synchronize(dev)
@@ -674,7 +715,8 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
             "hbm_frac_per_gpu": round(local_bytes / (ms * 1e-3) / 1e9 / hbm_peak, 4),
             "n_gpus": world, "parallelism": (f"tp{world} column split, all-gather fused into every GEMM's epilogue "
                                              f"(NVLink peer stores + flags)") if world > 1 else "single GPU", "kernels": "busfill_gemm_q4k x3 + busfill_gemm_q4k_swiglu per layer",
-            "timing": f"CUDA graph of one {L}-layer sweep, {sweeps} replays, CUDA events, max over ranks"}
+            "timing": f"CUDA graph of one {L}-layer sweep, {sweeps} replays, CUDA events, max over ranks",
+            **({"layer_sweep_kernel": fused} if fused else {})}
 
 
 def config4(torch, bf, dev, args, hbm_peak, tc_peak, peak_src):

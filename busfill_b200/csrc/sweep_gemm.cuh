@@ -28,8 +28,8 @@
 // No CTA waits for another inside an op; counters are zero between launches.
 //
 // Per CTA and unit the pipeline is the decode kernel's (weight TMA ring ->
-// dequant warps -> TMEM operand slots -> swap-AB tcgen05.mma into a
-// double-buffered TMEM accumulator -> epilogue), see decode_gemm.cuh: the same
+// dequant warps -> TMEM operand slots -> swap-AB tcgen05.mma into one of
+// three TMEM accumulators -> epilogue), see decode_gemm.cuh: the same
 // warp roles, barriers and numerics, with the unit list spanning all ops.
 //
 // Every wait is bounded (kWaitTimeoutNs); a CTA that gives up records an error
@@ -48,6 +48,11 @@ constexpr int kMaxOps = 4;
 constexpr int kMaxTiles = 1024;    // tiles per op: N <= 131072
 constexpr int kSlotsPerCta = 4;    // partial tiles per CTA and op: {first, last tile} x {plane 0, 1}
 constexpr int kMaxNB = 32;
+// TMEM accumulators: three segment buffers, so that the MMAs can run two
+// segments ahead of the epilogue (whose split-tile hand-offs take microseconds
+// of global-memory round trips), then the SwiGLU gate tile; the operand slots
+// start at column 128
+constexpr int kAccBufs = 3;
 // counter words ahead of the partial slots in a workspace: per op and tile
 // the contributions, then per op the tiles stored, then the CTAs finished
 constexpr int kCntWords = kMaxOps * kMaxTiles;
@@ -105,8 +110,8 @@ struct Smem {
   static constexpr int bReady = bWEmpty + kWStages;   // 4 dequant warps + the activation producer (+ TMA bytes)
   static constexpr int bUDone = bReady + kSlots;      // unit's MMAs complete: operand slot free
   static constexpr int bAccFull = bUDone + kSlots;    // segment accumulator b complete
-  static constexpr int bAccEmpty = bAccFull + 2;      // segment accumulator b read by the epilogue
-  static constexpr int bXFree = bAccEmpty + 2;        // activation stage free
+  static constexpr int bAccEmpty = bAccFull + kAccBufs;   // segment accumulator b read by the epilogue
+  static constexpr int bXFree = bAccEmpty + kAccBufs;     // activation stage free
   static constexpr int bFinal = bXFree + kXStages;
   static constexpr int kNumBars = bFinal + 1;
   static constexpr int kMiscOff = kBarOff + kNumBars * 8;
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
   auto bar_count = [&](int bb) -> uint32_t {
     if (bb >= L::bWEmpty && bb < L::bWEmpty + kWStages) return 4;
     if (bb >= L::bReady && bb < L::bReady + kSlots) return 5;
-    if (bb >= L::bAccEmpty && bb < L::bAccEmpty + 2) return 4;
+    if (bb >= L::bAccEmpty && bb < L::bAccEmpty + kAccBufs) return 4;
     return 1;
   };
   // weight TMA for unit i (cursor c) into ring stage i % kWStages; one thread
@@ -334,18 +339,18 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
     const uint64_t bdesc0 = make_sdesc_sw128(sbase + L::kXOff);
     Cursor c;
     seek_op(p, b, c, 0);
-    int s = 0, seg = 0;
-    uint32_t ph = 0;
+    int s = 0, seg = 0, abuf = 0;
+    uint32_t ph = 0, aph = 0;   // aph: parity of this use of accumulator abuf (seg / kAccBufs)
     bool pre = false;
     for (int i = 0; i < nunits; ++i) {
       diag_unit = i;
-      const int buf = seg & 1;
       const bool first = c.first, last = seg_last(p, c);
-      if (first && seg >= 2 && !warp_wait(BAR(L::bAccEmpty + buf), ((seg >> 1) & 1) ^ 1)) break;
+      // accumulator abuf is free once the epilogue has read segment seg - kAccBufs
+      if (first && seg >= kAccBufs && !warp_wait(BAR(L::bAccEmpty + abuf), aph ^ 1u)) break;
       if (!pre && !warp_wait(BAR(L::bReady + s), ph)) break;
       tc_fence_after();
       if (elect_one()) {
-        const uint32_t d_acc = tmem + TM::kAcc + (uint32_t)(buf * NB);
+        const uint32_t d_acc = tmem + (uint32_t)(abuf * NB);
         const uint32_t a_t = tmem + TM::kA + (uint32_t)(s * 128);
         const uint64_t bd = bdesc0 + (uint64_t)(((i % L::kXStages) * L::kXSlotBytes) >> 4);
 #pragma unroll
@@ -356,14 +361,20 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
                        (first && cc == 0 && t == 0) ? 0u : 1u);
         tc_commit(BAR(L::bUDone + s));
         tc_commit(BAR(L::bXFree + i % L::kXStages));
-        if (last) tc_commit(BAR(L::bAccFull + buf));
+        if (last) tc_commit(BAR(L::bAccFull + abuf));
       }
       __syncwarp();
       if (++s == kSlots) {
         s = 0;
         ph ^= 1u;
       }
-      if (last) ++seg;
+      if (last) {
+        ++seg;
+        if (++abuf == kAccBufs) {
+          abuf = 0;
+          aph ^= 1u;
+        }
+      }
       step(p, b, c);
       pre = (i + 1 < nunits) && __all_sync(0xffffffffu, mbar_test_wait(BAR(L::bReady + s), ph));
     }
@@ -404,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
     // SwiGLU: the finished gate tile waits for its up tile in TMEM columns
     // [2 NB, 3 NB) (free: the accumulators take [0, 2 NB), the operand slots
     // start at 128), not in registers
-    const uint32_t gate_t = tmem + lane_off + (uint32_t)(2 * NB);
-    static_assert(3 * NB <= DecodeTmem<NB>::kA, "gate columns");
+    const uint32_t gate_t = tmem + lane_off + (uint32_t)(kAccBufs * NB);
+    static_assert((kAccBufs + 1) * NB <= DecodeTmem<NB>::kA, "accumulator and gate columns");
     auto save_gate = [&]() {
 #pragma unroll
       for (int h = 0; h < NB; h += 16) tmem_st_x16(gate_t + (uint32_t)h, reinterpret_cast<const uint32_t*>(acc + h));
@@ -454,7 +465,8 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
     pdl_wait_prerequisites();   // partial slots, counters and C may still be in use by the previous kernel
     Cursor c;
     seek_op(p, b, c, 0);
-    int seg = 0;
+    int seg = 0, abuf = 0;
+    uint32_t aph = 0;
     unsigned stored = 0;   // tiles of the current op this CTA stored
     while (c.op < p.nops) {
       const Op& op = p.op[c.op];
@@ -465,13 +477,12 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
       const bool tile_end = c.u + len == min(t_hi, c.end);
       const bool op_end = c.u + len == c.end;
       diag_unit = seg;
-      const int buf = seg & 1;
-      if (warp_wait(BAR(L::bAccFull + buf), (uint32_t)((seg >> 1) & 1))) {
+      if (warp_wait(BAR(L::bAccFull + abuf), aph)) {
         tc_fence_after();
 #pragma unroll
         for (int h = 0; h < NB; h += 16) {
           uint32_t x[16];
-          tmem_ld_x16(tmem + lane_off + TM::kAcc + (uint32_t)(buf * NB + h), x);
+          tmem_ld_x16(tmem + lane_off + (uint32_t)(abuf * NB + h), x);
           tc_wait_ld();
 #pragma unroll
           for (int t = 0; t < 16; ++t) acc[h + t] = __uint_as_float(x[t]);
@@ -482,7 +493,11 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + buf));
+      if (lane == 0) mbar_arrive(BAR(L::bAccEmpty + abuf));
+      if (++abuf == kAccBufs) {
+        abuf = 0;
+        aph ^= 1u;
+      }
 
       if (whole) {
         if (P == 2 && c.plane == 0) {
