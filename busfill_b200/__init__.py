@@ -171,6 +171,11 @@ def set_prefill_batch_tile(bt: int) -> None:
     _check(_lib().busfill_set_option(5, int(bt)), "busfill_set_option")
 
 
+def set_sweep_ctas(n: int) -> None:
+    """BUSFILL_OPT_SWEEP_CTAS: CTAs of a layer-sweep launch (0 = one per SM)."""
+    _check(_lib().busfill_set_option(7, n), "busfill_set_option")
+
+
 def set_prefill_pair(mode: int) -> None:
     """Prefill GEMMs on CTA pairs (256 x 256 items over a 2-CTA cluster):
     0 = from M = 256 (default), 1 = always (not the SwiGLU pairs), 2 = never."""

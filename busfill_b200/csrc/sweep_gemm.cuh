@@ -69,6 +69,7 @@ struct Op {
   int planes;       // 1, or 2 for a SwiGLU pair (tw = gate, twu = up)
   int dep;          // index of an earlier op whose output this op's activations are, or -1
   unsigned units;   // T * planes * S
+  int ctas;         // CTAs 0 .. ctas-1 share the op (<= G; the others have no units of it)
 };
 
 struct Params {
@@ -91,6 +92,10 @@ __host__ __device__ __forceinline__ unsigned range_begin(unsigned U, int b, int 
 // the CTA whose range holds unit u: the largest b with range_begin(U, b, G) <= u
 __host__ __device__ __forceinline__ int owner(unsigned U, unsigned u, int G) {
   return (int)((((unsigned long long)u + 1ull) * (unsigned)G - 1ull) / U);
+}
+// first unit of CTA b's range when CTAs [0, Go) share the op (b >= Go: none)
+__host__ __device__ __forceinline__ unsigned op_begin(unsigned U, int b, int Go) {
+  return b >= Go ? U : range_begin(U, b, Go);
 }
 // partial slot of a CTA whose range starts at unit rs, for tile `tile` and plane pl
 __host__ __device__ __forceinline__ int slot_of(unsigned rs, unsigned Q, int tile, int pl) {
@@ -130,6 +135,7 @@ struct Cursor {
   unsigned rs;       // start of this CTA's range in the op
   int S, P;          // the op's units per plane and planes
   unsigned U;        // the op's units
+  int Go;            // CTAs sharing the op (Op::ctas)
   int tile, plane, sb;
   bool first;        // first unit of a segment (a run of one plane of one tile)
 };
@@ -137,12 +143,14 @@ struct Cursor {
 __device__ __forceinline__ void seek_op(const Params& p, int b, Cursor& c, int o) {
   for (; o < p.nops; ++o) {
     const unsigned U = p.op[o].units;
-    const unsigned u0 = range_begin(U, b, p.G), u1 = range_begin(U, b + 1, p.G);
+    const int Go = p.op[o].ctas;
+    const unsigned u0 = op_begin(U, b, Go), u1 = op_begin(U, b + 1, Go);
     if (u0 < u1) {
       const unsigned S = (unsigned)p.op[o].S, Q = S * (unsigned)p.op[o].planes;
       c.S = (int)S;
       c.P = p.op[o].planes;
       c.U = U;
+      c.Go = Go;
       c.op = o;
       c.u = u0;
       c.rs = u0;
@@ -216,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
   const int G = p.G;
   int nunits = 0;
   for (int o = 0; o < p.nops; ++o)
-    nunits += (int)(range_begin(p.op[o].units, b + 1, G) - range_begin(p.op[o].units, b, G));
+    nunits += (int)(op_begin(p.op[o].units, b + 1, p.op[o].ctas) - op_begin(p.op[o].units, b, p.op[o].ctas));
 
   bool ok = true;
   int diag_unit = -1;
@@ -521,16 +529,17 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
           // ~4 us per tile on B200 while the TMA streams ran); the leader's
           // acquire half makes the other contributors' partials visible to
           // the loads below, which the second barrier orders after it.
-          const int c_lo = owner(U, t_lo, G), c_hi = owner(U, t_hi - 1, G);
+          const int Go = c.Go;
+          const int c_lo = owner(U, t_lo, Go), c_hi = owner(U, t_hi - 1, Go);
           named_bar_sync(2, kEpilogueThreads);
           if (leader) {
             // contributors: the CTAs in [c_lo, c_hi] with units in this op
             // (all of them unless the op has fewer units than CTAs)
             unsigned n = (unsigned)(c_hi - c_lo + 1);
-            if (U < (unsigned)G) {
+            if (U < (unsigned)Go) {
               n = 0;
               for (int cc = c_lo; cc <= c_hi; ++cc)
-                n += range_begin(U, cc, G) < range_begin(U, cc + 1, G) ? 1u : 0u;
+                n += range_begin(U, cc, Go) < range_begin(U, cc + 1, Go) ? 1u : 0u;
             }
             unsigned* cnt = p.flags + c.op * kMaxTiles + c.tile;
             misc[1] = (atom_add_acq_rel_gpu(cnt, 1u) == n - 1u) ? 1u : 0u;
@@ -542,10 +551,10 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
 #pragma unroll
               for (int t = 0; t < NB; ++t) acc[t] = 0.f;
               const unsigned p_lo = t_lo + pl * S, p_hi = p_lo + S;
-              unsigned a1 = range_begin(U, c_lo, G);
+              unsigned a1 = range_begin(U, c_lo, Go);
               for (int cc = c_lo; cc <= c_hi; ++cc) {
                 const unsigned a0 = a1;
-                a1 = range_begin(U, cc + 1, G);
+                a1 = range_begin(U, cc + 1, Go);
                 if (max(a0, p_lo) >= min(a1, p_hi)) continue;   // no units of this plane
                 const float4* src = reinterpret_cast<const float4*>(
                     p.part + ((size_t)(c.op * G + cc) * kSlotsPerCta + slot_of(a0, Q, c.tile, (int)pl)) * kSlotFloats);

@@ -416,6 +416,10 @@ BUSFILL_API int busfill_version(void);
  *     SwiGLU pairs of M > 128 as two such GEMMs; 1 does so for every prefill
  *     GEMM and SwiGLU pair; 2 never.
  *     A tuning and test knob; results agree within the accuracy gate.
+ *   BUSFILL_OPT_SWEEP_CTAS: CTAs of a busfill_gemm_q4k_sweep launch; 0
+ *     (default) one per SM. A tuning and test knob; results agree within the
+ *     accuracy gate (the split of split tiles, so the fp32 summation order,
+ *     follows the CTA count).
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
@@ -423,6 +427,7 @@ BUSFILL_API int busfill_version(void);
 #define BUSFILL_OPT_EXACT_KQUANT 4
 #define BUSFILL_OPT_PREFILL_BATCH_TILE 5
 #define BUSFILL_OPT_PREFILL_PAIR 6
+#define BUSFILL_OPT_SWEEP_CTAS 7
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,

@@ -431,6 +431,15 @@ def test_prefill_pair_option_values():
     assert lib.busfill_set_option(6, 0) == 0
 
 
+def test_sweep_ctas_option_values():
+    lib = bf.load_library()
+    for v in (0, 1, 120, 148, 4096):
+        assert lib.busfill_set_option(7, v) == 0
+    assert lib.busfill_set_option(7, -1) == -1
+    assert lib.busfill_set_option(7, 4097) == -1
+    assert lib.busfill_set_option(7, 0) == 0
+
+
 def test_kernel_choice_by_shape():
     """Default dispatch of the plain GEMMs: the stream-K prefill kernel for
     M > 64, and for M > 32 when N <= K and K >= 12288; the decode kernel

@@ -208,3 +208,33 @@ def test_sweep_full_size_layer():
     assert bf.stream_status() == 0
     for name, got, ref in (("o", o, ref_o), ("qkv", qkv, ref_qkv), ("h", h, ref_h), ("down", dn, ref_d)):
         check_rel(host(got), host(ref), name, rel_gate=2e-3, abs_frac=4e-3)
+
+
+def test_sweep_whole_tile_ops():
+    """Ops whose tile count nearly fills the grid take whole tiles per CTA (no
+    split tiles): 140 tiles, 280 tiles (two per CTA) and a SwiGLU pair of 148
+    tiles on a 148-SM B200, next to a split op."""
+    m = 8
+    specs = [(140 * 128, 512, False), (280 * 128, 256, False), (148 * 128, 256, True), (1280, 1024, False)]
+    ops, ref = [], []
+    for i, (n, k, sw) in enumerate(specs):
+        wq = orc.gen_q4k(n, k, seed=40 + i)
+        a = (orc.gen_activations(m, k, seed=50 + i).astype(np.float32) / 64).astype(np.float16)
+        out = torch.empty((m, n), dtype=torch.float16, device=DEV)
+        op = {"w": cu(wq), "a": cu(a), "out": out}
+        if sw:
+            wu = orc.gen_q4k(n, k, seed=60 + i)
+            op["w_up"] = cu(wu)
+            ref.append(("swiglu", orc.swiglu_ref(a, orc.dequant_q4k_f32(wq, k), orc.dequant_q4k_f32(wu, k))))
+        else:
+            ref.append(("gemm", orc.gemm_ref(a, orc.dequant_q4k_f32(wq, k))))
+        ops.append(op)
+    bf.gemm_q4k_sweep(ops)
+    assert bf.stream_status() == 0
+    for op, (kind, want) in zip(ops, ref):
+        got = host(op["out"]).astype(np.float32)
+        if kind == "swiglu":
+            check_rel(got, want, "swiglu")
+        else:
+            max_abs, rel, finite = orc.gemm_errors(got, want)
+            assert finite and max_abs <= 0.6 and rel <= 1e-3, (max_abs, rel)
