@@ -666,21 +666,41 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
     del g
     fused = None
     if world == 1:
-        # the same layers as one busfill_gemm_q4k_sweep launch each (ops in
-        # the order O, QKV, gate/up after O, down after gate/up; the down
-        # outputs alternate between two buffers so no op writes what another
-        # op of its launch reads)
-        downs = [full["down"], torch.empty_like(full["down"])]
+        # the same layers through busfill_gemm_q4k_sweep, two layers (eight
+        # ops) per launch, ordered so that no op directly follows the op whose
+        # output it reads: O1, O2, QKV1, gate/up1 (after O1), gate/up2 (after
+        # O2), down1, down2, QKV2 (after down1); an odd last layer runs alone
+        # (O, QKV, gate/up, down). Outputs never overlap an input of their own
+        # launch: the second layer's down output alternates between two
+        # buffers from launch to launch.
+        o2 = [full["o"], torch.empty_like(full["o"])]
+        gu = [full["gate"], torch.empty_like(full["gate"])]
+        q2 = [full["qkv"], torch.empty_like(full["qkv"])]
+        d1 = torch.empty_like(full["down"])
+        dl = [full["down"], torch.empty_like(full["down"])]
 
         def sweep_fused():
             h = x
-            for li, lw in enumerate(layers):
-                dn = downs[li & 1]
-                bf.gemm_q4k_sweep([{"w": lw["o"], "a": attn, "out": full["o"]},
-                                   {"w": lw["qkv"], "a": h, "out": full["qkv"]},
-                                   {"w": lw["gate"], "w_up": lw["up"], "a": full["o"], "out": full["gate"], "dep": 0},
-                                   {"w": lw["down"], "a": full["gate"], "out": dn, "dep": 2}], stream=st)
+            for j in range(0, L - 1, 2):
+                la, lb = layers[j], layers[j + 1]
+                dn = dl[(j // 2) & 1]
+                bf.gemm_q4k_sweep([{"w": la["o"], "a": attn, "out": o2[0]},
+                                   {"w": lb["o"], "a": attn, "out": o2[1]},
+                                   {"w": la["qkv"], "a": h, "out": q2[0]},
+                                   {"w": la["gate"], "w_up": la["up"], "a": o2[0], "out": gu[0], "dep": 0},
+                                   {"w": lb["gate"], "w_up": lb["up"], "a": o2[1], "out": gu[1], "dep": 1},
+                                   {"w": la["down"], "a": gu[0], "out": d1, "dep": 3},
+                                   {"w": lb["down"], "a": gu[1], "out": dn, "dep": 4},
+                                   {"w": lb["qkv"], "a": d1, "out": q2[1], "dep": 5}], stream=st)
                 h = dn
+            if L % 2:
+                lw = layers[L - 1]
+                dn = dl[((L - 1) // 2) & 1]
+                bf.gemm_q4k_sweep([{"w": lw["o"], "a": attn, "out": o2[0]},
+                                   {"w": lw["qkv"], "a": h, "out": q2[0]},
+                                   {"w": lw["gate"], "w_up": lw["up"], "a": o2[0], "out": gu[0], "dep": 0},
+                                   {"w": lw["down"], "a": gu[0], "out": d1, "dep": 2}],
+                                  stream=st)
 
         with torch.cuda.stream(st):
             sweep_fused()
@@ -702,7 +722,7 @@ def layerset(torch, bf, tp, dev, world, rank, args, hbm_peak, m=32, sweeps=10):
         fused = {"ms_per_sweep": round(ms2, 4), "us_per_layer": round(ms2 * 1e3 / L, 2),
                  "tokens_per_s": round(m / (ms2 * 1e-3), 1),
                  "hbm_frac_per_gpu": round(local_bytes / (ms2 * 1e-3) / 1e9 / hbm_peak, 4),
-                 "kernels": "busfill_gemm_q4k_sweep x1 per layer (4 ops, stream-K over all SMs)"}
+                 "kernels": "busfill_gemm_q4k_sweep x1 per two layers (8 ops, stream-K over all SMs)"}
     del layers
     if space is not None:
         torch.cuda.synchronize(dev)

@@ -286,7 +286,7 @@ class SweepOp(ctypes.Structure):
     _fields_ = [("w", _P), ("w_up", _P), ("a", _P), ("c", _P), ("N", _I), ("K", _I), ("dep", _I)]
 
 
-SWEEP_MAX_OPS = 4
+SWEEP_MAX_OPS = 8
 
 
 def gemm_q4k_sweep(ops, stream=None):

@@ -44,7 +44,7 @@
 namespace busfill {
 namespace sweep {
 
-constexpr int kMaxOps = 4;
+constexpr int kMaxOps = 8;   // two decoder layers
 constexpr int kMaxTiles = 1024;    // tiles per op: N <= 131072
 constexpr int kSlotsPerCta = 4;    // partial tiles per CTA and op: {first, last tile} x {plane 0, 1}
 constexpr int kMaxNB = 32;
@@ -58,7 +58,7 @@ constexpr int kAccBufs = 3;
 constexpr int kCntWords = kMaxOps * kMaxTiles;
 constexpr int kDoneOff = kCntWords;
 constexpr int kFinOff = kDoneOff + kMaxOps;
-constexpr int kFlagWords = 8192;   // 32 KB, keeps the partial slots 256-byte aligned
+constexpr int kFlagWords = 16384;   // 64 KB, keeps the partial slots 256-byte aligned
 static_assert(kFinOff < kFlagWords, "flag region");
 
 struct Op {

@@ -100,13 +100,18 @@ BUSFILL_API int busfill_gemm_q4k_swiglu(const uint8_t* w_gate, const uint8_t* w_
  * its activations only once op j's whole output is stored (j < o: its `a` is
  * op j's `c`, or computed from it). Ops with dep = -1 must not read an
  * earlier op's output in this call. Outputs must not overlap inputs.
- * The first call on a stream allocates its workspace (~40 MB: counters and
+ * Order matters for speed, not for results: an op that directly follows
+ * the op it reads waits for that op's last tile; with an independent op in
+ * between, the wait is hidden. Two decoder layers per call (eight ops) in
+ * the order O1, O2, QKV1, gate/up1 (dep 0), gate/up2 (dep 1), down1 (dep 3),
+ * down2 (dep 4), QKV2 (dep 5) hide every wait.
+ * The first call on a stream allocates its workspace (~80 MB: counters and
  * partial tiles; fails with BUSFILL_ERR_ALLOC inside a graph capture); calls
  * on one stream share it in stream order. Failures are read with
  * busfill_stream_status. No reference counterpart: the reference launches
  * one GEMM per kernel (kernels/busfill_v1a.cu:151-154); this is the layer
  * set of its decode benchmark as one launch. */
-#define BUSFILL_SWEEP_MAX_OPS 4
+#define BUSFILL_SWEEP_MAX_OPS 8
 typedef struct busfill_sweep_op {
   const uint8_t* w;      /* block_q4_K rows [N][K/256 * 144] (the gate with w_up) */
   const uint8_t* w_up;   /* SwiGLU: the up projection's rows, same shape; else NULL */

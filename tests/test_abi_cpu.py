@@ -629,7 +629,7 @@ def test_sweep_checks_before_any_device_work():
     ops, keep = _sweep_ops([(256, 512, -1, False), (512, 256, 0, True)])
     assert lib.busfill_gemm_q4k_sweep(None, 1, 8, None) == -1
     assert lib.busfill_gemm_q4k_sweep(ops, 0, 8, None) == -2          # no ops
-    assert lib.busfill_gemm_q4k_sweep(ops, 5, 8, None) == -2          # more than BUSFILL_SWEEP_MAX_OPS
+    assert lib.busfill_gemm_q4k_sweep(ops, 9, 8, None) == -2          # more than BUSFILL_SWEEP_MAX_OPS
     assert lib.busfill_gemm_q4k_sweep(ops, 2, 0, None) == -2          # M < 1
     assert lib.busfill_gemm_q4k_sweep(ops, 2, 33, None) == -2         # M > 32
     bad, keep2 = _sweep_ops([(256, 512, 0, False)])                   # depends on itself

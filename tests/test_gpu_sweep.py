@@ -238,3 +238,18 @@ def test_sweep_whole_tile_ops():
         else:
             max_abs, rel, finite = orc.gemm_errors(got, want)
             assert finite and max_abs <= 0.6 and rel <= 1e-3, (max_abs, rel)
+
+
+def test_sweep_two_layers_eight_ops():
+    """Two layers in one launch (BUSFILL_SWEEP_MAX_OPS = 8), interleaved so
+    that no op directly follows the op it reads: O1, O2, QKV1, gate/up1 (after
+    O1), gate/up2 (after O2), down1, down2, QKV2."""
+    w1, d1, attn1, x1, out1, ops1 = layer(16, seed=71)
+    w2, d2, attn2, x2, out2, ops2 = layer(16, seed=72)
+    o1, o2, q1, g1, g2, dn1, dn2, q2 = ops1[0], ops2[0], ops1[1], dict(ops1[2]), dict(ops2[2]), dict(ops1[3]), \
+        dict(ops2[3]), ops2[1]
+    g1["dep"], g2["dep"], dn1["dep"], dn2["dep"] = 0, 1, 3, 4
+    bf.gemm_q4k_sweep([o1, o2, q1, g1, g2, dn1, dn2, q2])
+    assert bf.stream_status() == 0
+    check_layer(w1, attn1, x1, out1)
+    check_layer(w2, attn2, x2, out2)
