@@ -80,6 +80,7 @@ int prefill_bt(int M, bool swiglu) {
 constexpr int kPairMinM = 129;
 std::atomic<int> g_prefill_pair{0};
 std::atomic<int> g_sweep_ctas{0};   // BUSFILL_OPT_SWEEP_CTAS: 0 = one CTA per SM
+std::atomic<int> g_sweep_unmet{0};  // BUSFILL_OPT_SWEEP_UNMET_DEP (failure-detection tests)
 
 bool prefill_pairs(int M, bool swiglu) {
   if (swiglu) return false;
@@ -1052,6 +1053,7 @@ int gemm_sweep_impl(const busfill_sweep_op* ops, int nops, int M, cudaStream_t s
     d.ctas = (d.tiles % k == 0 && whole <= p.G && whole * 8 >= p.G * 7) ? whole : p.G;
   }
   p.flags = ws;
+  p.dep_extra = g_sweep_unmet.load() ? 1u : 0u;
   p.part = reinterpret_cast<float*>(ws + sweep::kFlagWords);
   p.error = err;
   return nb == 16 ? launch_sweep<16>(dev, p, s) : launch_sweep<32>(dev, p, s);
@@ -1140,6 +1142,11 @@ int busfill_set_option(int option, int value) {
   if (option == BUSFILL_OPT_SWEEP_CTAS) {
     if (value < 0 || value > 4096) return BUSFILL_ERR_INVALID_ARG;
     g_sweep_ctas.store(value);
+    return BUSFILL_OK;
+  }
+  if (option == BUSFILL_OPT_SWEEP_UNMET_DEP) {
+    if (value < 0 || value > 1) return BUSFILL_ERR_INVALID_ARG;
+    g_sweep_unmet.store(value);
     return BUSFILL_OK;
   }
   return BUSFILL_ERR_INVALID_ARG;

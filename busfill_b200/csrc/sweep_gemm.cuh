@@ -81,6 +81,7 @@ struct Params {
   int M;
   int G;                      // CTAs in the grid
   unsigned* flags;            // kFlagWords counter words (zero between launches)
+  unsigned dep_extra;         // 0; failure-detection tests: 1 makes every dependency wait run out
   float* part;                // [nops][G][kSlotsPerCta][128 * NB] fp32 partial tiles
   unsigned* error;            // device error word (+1: first failure record)
 };
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) sweep_gemm_kernel(const __grid_co
           // every tile of op d stored (by whichever CTA finished it)
           bool got = true;
           if (lane == 0) {
-            got = wait_count_gpu(p.flags + kDoneOff + d, (unsigned)p.op[d].tiles);
+            got = wait_count_gpu(p.flags + kDoneOff + d, (unsigned)p.op[d].tiles + p.dep_extra);
             fence_proxy_async_global();
           }
           if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {

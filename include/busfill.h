@@ -425,6 +425,12 @@ BUSFILL_API int busfill_version(void);
  *     (default) one per SM. A tuning and test knob; results agree within the
  *     accuracy gate (the split of split tiles, so the fp32 summation order,
  *     follows the CTA count).
+ *   BUSFILL_OPT_SWEEP_UNMET_DEP: 0 (default); 1 makes every dependent op of a
+ *     busfill_gemm_q4k_sweep wait for one tile more than its input op
+ *     stores, so that its bounded wait (1 s) runs out: the call's output is
+ *     invalid and busfill_stream_status reports BUSFILL_ERR_DEVICE_TIMEOUT
+ *     (and clears the stream's words and counters). For failure-detection
+ *     tests only.
  * Returns BUSFILL_ERR_INVALID_ARG for an unknown option or value. */
 #define BUSFILL_OPT_PDL 1
 #define BUSFILL_OPT_KSPLIT 2
@@ -433,6 +439,7 @@ BUSFILL_API int busfill_version(void);
 #define BUSFILL_OPT_PREFILL_BATCH_TILE 5
 #define BUSFILL_OPT_PREFILL_PAIR 6
 #define BUSFILL_OPT_SWEEP_CTAS 7
+#define BUSFILL_OPT_SWEEP_UNMET_DEP 8
 BUSFILL_API int busfill_set_option(int option, int value);
 
 /* Which kernel a plain GEMM (busfill_gemm_q4_0 / _q4k / ...) of M batch rows,

@@ -431,6 +431,14 @@ def test_prefill_pair_option_values():
     assert lib.busfill_set_option(6, 0) == 0
 
 
+def test_sweep_unmet_dep_option_values():
+    lib = bf.load_library()
+    for v in (0, 1, 0):
+        assert lib.busfill_set_option(8, v) == 0
+    for v in (-1, 2):
+        assert lib.busfill_set_option(8, v) == -1
+
+
 def test_sweep_ctas_option_values():
     lib = bf.load_library()
     for v in (0, 1, 120, 148, 4096):

@@ -56,3 +56,43 @@ def test_wait_that_runs_out_reports_timeout_and_context_survives():
     max_abs, rel, finite = orc.gemm_errors(c.float().cpu().numpy(),
                                            orc.gemm_ref(a_np, orc.dequant_q4k_f32(orc.gen_q4k(n, k, seed=5), k)))
     assert finite and max_abs <= orc.GATE_MAX_ABS and rel <= orc.GATE_REL_L2
+
+
+def test_sweep_dependency_wait_that_runs_out_reports_timeout_and_next_sweep_is_right():
+    """The layer sweep's dependency wait (an op reading an earlier op's output
+    waits for that op's stored-tile count): with BUSFILL_OPT_SWEEP_UNMET_DEP
+    the dependent op waits for one tile more than exists, its activation
+    producer gives up after the 1 s bound, and busfill_stream_status reports
+    the timeout and clears the stream's error words and sweep counters; the
+    next sweep on the same stream (counters back at zero) is right."""
+    m = 8
+    w0_np, w1_np = orc.gen_q4k(512, 512, seed=81), orc.gen_q4k(256, 512, seed=82)
+    a_np = (orc.gen_activations(m, 512, seed=83).astype(np.float32) / 64).astype(np.float16)
+    w0, w1, a = (torch.from_numpy(x).to(DEV) for x in (w0_np, w1_np, a_np))
+    h = torch.empty((m, 512), dtype=torch.float16, device=DEV)
+    y = torch.empty((m, 256), dtype=torch.float16, device=DEV)
+    ops = [{"w": w0, "a": a, "out": h}, {"w": w1, "a": h, "out": y, "dep": 0}]
+    lib = bf.load_library()
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        bf.gemm_q4k_sweep(ops, stream=st)                    # makes the stream's workspace
+        assert bf.stream_status(st) == 0
+        assert lib.busfill_set_option(8, 1) == 0
+        try:
+            bf.gemm_q4k_sweep(ops, stream=st)                # the launch itself is fine
+            status, bits = bf.stream_status_bits(st)
+        finally:
+            assert lib.busfill_set_option(8, 0) == 0
+        assert status == TIMEOUT, status
+        assert bits & ACT_PRODUCER_BIT, bits
+        h.zero_()
+        y.zero_()
+        bf.gemm_q4k_sweep(ops, stream=st)
+        assert bf.stream_status(st) == 0
+    h_np = h.cpu().numpy()
+    max_abs, rel, finite = orc.gemm_errors(h_np.astype(np.float32), orc.gemm_ref(a_np, orc.dequant_q4k_f32(w0_np, 512)))
+    assert finite and max_abs <= orc.GATE_MAX_ABS and rel <= orc.GATE_REL_L2
+    want = orc.gemm_ref(h_np, orc.dequant_q4k_f32(w1_np, 512))
+    got = y.float().cpu().numpy()
+    assert np.all(np.isfinite(got))
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) <= 1e-3
