@@ -1,5 +1,6 @@
-// One launch for a list of small-batch Q4_K GEMMs (a decoder layer's
-// projections: O, QKV, gate/up SwiGLU pair, down), M <= 32, on sm_100a.
+// One launch for a list of up to eight small-batch Q4_K GEMMs (one or two
+// decoder layers' projections: O, QKV, gate/up SwiGLU pair, down), M <= 32,
+// on sm_100a.
 //
 // Why: a decode-sized GEMM (M <= 32) is too short to amortise a launch. Each
 // launch of the one-GEMM decode kernel (decode_gemm.cuh) pays a fixed ~7 us on
@@ -18,8 +19,11 @@
 // U = T P S units are cut into G contiguous ranges, CTA b taking units
 // [U b / G, U (b + 1) / G). Every CTA thus takes an equal share of every op,
 // so all CTAs reach an op's end together and a dependent op waits little.
-// A tile that lies inside one CTA's range is finished by that CTA (C stored,
-// SwiGLU combined in registers). A tile split between CTAs: each contributor
+// An op whose tiles nearly fill the grid takes whole tiles on fewer CTAs
+// instead (Op::ctas, chosen by the host), so that none of its tiles is split.
+// A tile that lies inside one CTA's range is finished by that CTA (C stored;
+// a SwiGLU pair's gate tile waits in TMEM for its up tile). A tile split
+// between CTAs: each contributor
 // stores its fp32 sums of the tile's planes into its own partial slots, makes
 // them visible and adds 1 to the tile's counter; the contributor that brings
 // the counter to the number of contributors (the last to arrive) adds all
